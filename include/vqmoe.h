@@ -1,0 +1,198 @@
+/*
+ * vqmoe.h -- C ABI of the B200 VQ-MoE expert layer (libvqmoe.so).
+ *
+ * Drop-in for the expert path of Knurlogic's Qwen3.5-MoE sparse block with
+ * VQ-quantised experts. Every entry point takes plain device pointers,
+ * sizes and a cudaStream_t (passed as void*), allocates no device memory
+ * (callers pass a workspace sized by the *_workspace_size queries), never
+ * throws, and returns a vqmoe_status. Every call only enqueues work on
+ * `stream` (no host synchronisation).
+ *
+ * Reference interfaces each entry point replaces (paths inside the
+ * Knurlogic project):
+ *   vqmoe_sparse_moe_block  SparseMoeBlock.__call__
+ *       src/knurlogic/engine/families/qwen/architecture/qwen3_5.py:170-192
+ *   vqmoe_switch_glu        SwitchGLU.__call__
+ *       .../glm5_next/_mlx_vlm/models/switch_layers.py:172-193
+ *   vqmoe_switch_linear     VQSwitchLinear.__call__ (artifact model.py; the
+ *       contract is engine/families/deepseek/heads/deepseek_v4.py:77-130)
+ *       and SwitchLinear.__call__ (switch_layers.py:116-125) for bf16 experts
+ *   vqmoe_router            the router lines qwen3_5.py:174-179 (+ the
+ *       shared_expert_gate Linear of qwen3_5.py:186)
+ *   vqmoe_dequant           the VQ runtime's dense fp16 expert decode
+ *       (src/knurlogic/tuning/measured.py:21-33, VQ_DECODE_CHUNK)
+ *   vqmoe_prepare_codes     loading VQSwitchLinear.codes (deepseek_v4.py:
+ *       111-130 layout) into the device layout the kernels read
+ *
+ * Numerics (matching the reference's rounding order, qwen3_5.py:35-40,
+ * 108-112, 170-192): bf16 matmul outputs; fp32 softmax / top-k /
+ * renormalisation with weights rounded to bf16; silu / sigmoid in fp32
+ * rounded once; the top-k sum in fp32 rounded once. VQ weights dequantise
+ * to W = fp16(f32(codebook[code][j]) * f32(vq_scale)) and the VQ matmul
+ * takes the bf16 activations as fp16 (saturated at +-65504).
+ */
+#ifndef VQMOE_H_
+#define VQMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VQMOE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define VQMOE_API __attribute__((visibility("default")))
+#else
+#define VQMOE_API
+#endif
+
+typedef enum {
+    VQMOE_OK = 0,
+    VQMOE_BAD_SHAPE = 1,         /* a size is out of range or does not divide */
+    VQMOE_BAD_FORMAT = 2,        /* unknown weight format / unsupported dim, K */
+    VQMOE_BAD_POINTER = 3,       /* null or misaligned pointer */
+    VQMOE_WORKSPACE_TOO_SMALL = 4,
+    VQMOE_BAD_CODE = 5,          /* a VQ code >= codebook size */
+    VQMOE_LAUNCH_FAILED = 6,     /* a CUDA launch or call returned an error */
+    VQMOE_TIMEOUT = 7,           /* reserved: a bounded device wait ran out */
+    VQMOE_NOT_SUPPORTED = 8
+} vqmoe_status;
+
+/* Weight formats of one switch (expert) linear. */
+enum {
+    VQMOE_FMT_DENSE_BF16 = 0,    /* weight [E, OUT, IN] bf16 (SwitchLinear) */
+    VQMOE_FMT_VQ_U8 = 1          /* codes [E, OUT, IN/dim] uint8, device layout
+                                    (vqmoe_prepare_codes); codebook [K, dim]
+                                    fp16; scales [E, OUT, IN/group] fp16 */
+};
+
+/* One switch linear: y[r] = x[r] @ W[expert(r)]^T, W [E, OUT, IN].
+ * Mirrors VQSwitchLinear(codes, codebook, vq_scales, group_size=,
+ * pack_bits=0) (deepseek_v4.py:126-130). Supported VQ: dim 4, K <= 256,
+ * group_size 64, IN % 64 == 0, OUT % 16 == 0. Dense: IN % 16 == 0,
+ * OUT % 16 == 0. Pointers 16-byte aligned. */
+typedef struct {
+    int32_t format;
+    int32_t num_experts;
+    int32_t out_features;
+    int32_t in_features;
+    const void *weight;          /* DENSE_BF16 */
+    const void *codes;           /* VQ_U8 (device layout) */
+    const void *codebook;        /* VQ_U8 */
+    const void *scales;          /* VQ_U8 */
+    int32_t codebook_size;       /* K */
+    int32_t dim;                 /* code vector length */
+    int32_t group_size;          /* inputs per vq_scales entry */
+    int32_t reserved;
+} vqmoe_linear;
+
+/* One Qwen3.5-MoE sparse block (qwen3_5.py:170-192). The shared expert is
+ * optional (shared_inter == 0 disables it and its gate). */
+typedef struct {
+    int32_t hidden;              /* H */
+    int32_t num_experts;         /* E (<= 512) */
+    int32_t top_k;               /* k (<= 32, <= E) */
+    int32_t shared_inter;        /* I_s, 0 = no shared expert */
+    const void *router_w;        /* mlp.gate.weight [E, H] bf16 */
+    vqmoe_linear gate;           /* mlp.switch_mlp.gate_proj [E, I, H] */
+    vqmoe_linear up;             /* mlp.switch_mlp.up_proj   [E, I, H] */
+    vqmoe_linear down;           /* mlp.switch_mlp.down_proj [E, H, I] */
+    const void *shared_gate_w;   /* mlp.shared_expert.gate_proj [I_s, H] bf16 */
+    const void *shared_up_w;     /* mlp.shared_expert.up_proj   [I_s, H] bf16 */
+    const void *shared_down_w;   /* mlp.shared_expert.down_proj [H, I_s] bf16 */
+    const void *shared_expert_gate_w; /* mlp.shared_expert_gate [1, H] bf16 */
+} vqmoe_block;
+
+/* Output dtype of vqmoe_sparse_moe_block. F32 holds the bf16 block output
+ * widened to float32: the tensor split sums rank partials in float32
+ * (src/knurlogic/engine/split/tensor.py:159-187). */
+enum { VQMOE_OUT_BF16 = 0, VQMOE_OUT_F32 = 1 };
+
+/* Workspace bytes for vqmoe_sparse_moe_block / vqmoe_switch_glu /
+ * vqmoe_router at T tokens. */
+VQMOE_API size_t vqmoe_block_workspace_size(const vqmoe_block *blk, int32_t tokens);
+VQMOE_API size_t vqmoe_switch_glu_workspace_size(int32_t tokens, int32_t top_k,
+                                       int32_t inter);
+VQMOE_API size_t vqmoe_router_workspace_size(int32_t tokens, int32_t num_experts);
+
+/* SparseMoeBlock.__call__: out[T, H] = routed combine + gated shared expert.
+ * x [T, H] bf16; out bf16 or f32 (out_dtype). */
+VQMOE_API vqmoe_status vqmoe_sparse_moe_block(const vqmoe_block *blk, const void *x,
+                                    int32_t tokens, void *out,
+                                    int32_t out_dtype, void *workspace,
+                                    size_t workspace_bytes, void *stream);
+
+/* vqmoe_sparse_moe_block that also records six caller-created CUDA events
+ * (cudaEvent_t, passed as void*) on `stream`: before the router, then after
+ * the router, the routed gate/up + SwiGLU, the routed down, the shared
+ * expert, and the combine. For profiling; tokens <= 2048. */
+VQMOE_API vqmoe_status vqmoe_sparse_moe_block_timed(
+    const vqmoe_block *blk, const void *x, int32_t tokens, void *out,
+    int32_t out_dtype, void *workspace, size_t workspace_bytes, void *stream,
+    void *const *events, int32_t n_events);
+
+/* SwitchGLU.__call__: y[T, k, H] bf16 = down(bf16(silu(gate(x))) * up(x))
+ * for each (token, slot) of indices [T, k] int32. */
+VQMOE_API vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate,
+                              const vqmoe_linear *up,
+                              const vqmoe_linear *down, const void *x,
+                              const int32_t *indices, int32_t tokens,
+                              int32_t top_k, void *y, void *workspace,
+                              size_t workspace_bytes, void *stream);
+
+/* VQSwitchLinear.__call__ / SwitchLinear.__call__: y[T, k, OUT] bf16 with
+ * y[t, s] = x_row @ W[indices[t, s]]^T. x_per_pair = 0: x is [T, IN] (one
+ * row per token, shared by its k slots); 1: x is [T*k, IN] (one row per
+ * (token, slot), e.g. the down projection's input). */
+VQMOE_API vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x,
+                                 int32_t x_per_pair, const int32_t *indices,
+                                 int32_t tokens, int32_t top_k, void *y,
+                                 void *stream);
+
+/* Router: inds [T, k] int32 (descending logit, ties to the lower expert),
+ * scores [T, k] float32 holding bf16 values, and, when shared_expert_gate_w
+ * is not NULL, sgate [T] float32 = bf16(sigmoid(bf16(x @ w_sg^T))). */
+VQMOE_API vqmoe_status vqmoe_router(const void *x, const void *router_w,
+                          const void *shared_expert_gate_w, int32_t tokens,
+                          int32_t hidden, int32_t num_experts, int32_t top_k,
+                          int32_t *inds, float *scores, float *sgate,
+                          void *workspace, size_t workspace_bytes,
+                          void *stream);
+
+/* Dense fp16 weights of experts [first, first + count): out [count, OUT, IN]
+ * fp16, W = fp16(codebook[code][j] * scale). */
+VQMOE_API vqmoe_status vqmoe_dequant(const vqmoe_linear *w, int32_t first,
+                           int32_t count, void *out, void *stream);
+
+/* Permute reference-layout uint8 codes [rows, codes_per_row] (rows = E*OUT)
+ * into the device layout the VQ kernels read. src and dst are distinct
+ * device buffers. */
+VQMOE_API vqmoe_status vqmoe_prepare_codes(const uint8_t *src, uint8_t *dst,
+                                 int64_t rows, int32_t codes_per_row,
+                                 void *stream);
+
+/* *bad_count (device uint32, zeroed by the caller) += the number of codes
+ * >= codebook_size among codes[0, count). A loader calls it once; the
+ * kernels trust the codes. */
+VQMOE_API vqmoe_status vqmoe_count_bad_codes(const uint8_t *codes, int64_t count,
+                                   int32_t codebook_size, uint32_t *bad_count,
+                                   void *stream);
+
+/* Inverse of vqmoe_prepare_codes (device layout -> reference layout). */
+VQMOE_API vqmoe_status vqmoe_unprepare_codes(const uint8_t *src, uint8_t *dst,
+                                   int64_t rows, int32_t codes_per_row,
+                                   void *stream);
+
+/* Message of the last non-OK status returned on this host thread. */
+VQMOE_API const char *vqmoe_last_error(void);
+
+VQMOE_API int32_t vqmoe_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VQMOE_H_ */

@@ -1,0 +1,12 @@
+"""knurlogic_b200: the VQ-quantised MoE expert layer of Knurlogic, on B200.
+
+Drop-in modules with the reference's interface (`VQSwitchLinear`,
+`SwitchLinear`, `SwitchGLU`, `SparseMoeBlock`) over libvqmoe.so, hand-written
+sm_100a CUDA behind a C ABI (include/vqmoe.h). Tensor parallelism follows
+the reference's split rules (`tensor_split`).
+"""
+from .switch_layers import SwitchGLU, SwitchLinear, VQSwitchLinear  # noqa: F401
+from .moe import CapturedBlock, SharedExpert, SparseMoeBlock  # noqa: F401
+
+__all__ = ["SwitchGLU", "SwitchLinear", "VQSwitchLinear", "SharedExpert", "CapturedBlock",
+           "SparseMoeBlock"]

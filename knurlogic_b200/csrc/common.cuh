@@ -1,0 +1,147 @@
+// Shared device helpers of libvqmoe: exact rounding, packed loads, the
+// mma.sync wrappers the decode kernels use, and host-side error plumbing.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/vqmoe.h"
+
+namespace vqmoe {
+
+// ------------------------------------------------------------- rounding
+
+// float -> bf16 bits, round to nearest even (NaN kept quiet).
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+__device__ __forceinline__ float bf16_to_f32(uint32_t b) {
+    return __uint_as_float(b << 16);
+}
+
+__device__ __forceinline__ float bf16r(float f) {
+    return bf16_to_f32(f32_to_bf16(f));
+}
+
+// double -> bf16 bits in one rounding (nearest even on the float64
+// significand, no float32 step). Values below float32's normal range take
+// the float32 route (bf16 rounds at a coarser position there).
+__device__ __forceinline__ uint16_t f64_to_bf16(double d) {
+    double a = fabs(d);
+    if (!(a >= 1.1754943508222875e-38) || !(a <= 3.3895313892515355e38))
+        return f32_to_bf16((float)d);
+    unsigned long long u = (unsigned long long)__double_as_longlong(d);
+    const unsigned long long mask = (1ull << 45) - 1ull;
+    unsigned long long low = u & mask;
+    unsigned long long odd = (u >> 45) & 1ull;
+    unsigned long long r = u & ~mask;
+    if (low > (1ull << 44) || (low == (1ull << 44) && odd)) r += (1ull << 45);
+    return f32_to_bf16((float)__longlong_as_double((long long)r));
+}
+
+// bf16 value -> fp16 bits for the VQ matmul: saturate to +-65504, then
+// round to nearest even (exact for |v| in [2^-14, 65504]).
+__device__ __forceinline__ uint16_t bf16_to_f16_sat(uint32_t b) {
+    float v = bf16_to_f32(b);
+    v = fminf(fmaxf(v, -65504.0f), 65504.0f);
+    return __half_as_ushort(__float2half_rn(v));
+}
+
+__device__ __forceinline__ float silu_f32(float g) {
+    return g / (1.0f + expf(-g));
+}
+
+__device__ __forceinline__ float sigmoid_f32(float g) {
+    return 1.0f / (1.0f + expf(-g));
+}
+
+// -------------------------------------------------------------- loads
+
+__device__ __forceinline__ uint4 ldg_stream_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t ldg_stream_u32(const void *p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];\n"
+                 : "=r"(r)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint2 ldg_nc_v2(const void *p) {
+    uint2 r;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n"
+                 : "=r"(r.x), "=r"(r.y)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint16_t ldg_nc_u16(const void *p) {
+    uint16_t r;
+    asm volatile("ld.global.nc.u16 %0, [%1];\n" : "=h"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint2 lds_v2(uint32_t saddr) {
+    uint2 r;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n"
+                 : "=r"(r.x), "=r"(r.y)
+                 : "r"(saddr));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// half2 multiply (IEEE, round to nearest even per lane)
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// ---------------------------------------------------------------- mma
+
+// D += A(16x16, row) * B(16x8, col); fp32 accumulate.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
+                                        uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0,
+                                         uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------ host side
+
+vqmoe_status set_error(vqmoe_status s, const char *fmt, ...);
+vqmoe_status check_launch(const char *what);
+int sm_count();
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline bool aligned16(const void *p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+}  // namespace vqmoe

@@ -1,0 +1,279 @@
+"""Switch (expert) linears and SwitchGLU over libvqmoe, with the reference's
+module interface.
+
+Reference interfaces mirrored here:
+* `VQSwitchLinear(codes, codebook, vq_scales, *, group_size, pack_bits,
+  in_features=None)` -- the VQ runtime's module, as Knurlogic builds and
+  calls it (`src/knurlogic/engine/families/deepseek/heads/deepseek_v4.py:
+  77-130`; attributes read by `engine/split/viability.py:37-40` and
+  `engine/split/tensor.py:258-267`), called `mod(x, indices,
+  sorted_indices=...)` (`switch_layers.py:71-86`).
+* `SwitchLinear(weight)` -- mlx-lm's bf16 expert linear
+  (`glm5_next/_mlx_vlm/models/switch_layers.py:89-125`).
+* `SwitchGLU(gate_proj, up_proj, down_proj)` -- `switch_layers.py:151-193`.
+
+Every call runs on the CUDA path; there is no CPU implementation.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+from torch import nn
+
+from . import _lib
+
+
+def _stream(t: torch.Tensor):
+    return c_stream(t.device)
+
+
+def c_stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "knurlogic_b200 runs on CUDA tensors only (there is no CPU "
+                f"path); got a tensor on {t.device}")
+
+
+def _contig(t: torch.Tensor) -> torch.Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+class _SwitchBase(nn.Module):
+    """What both switch linears share: the call convention."""
+
+    num_experts: int
+    output_dims: int
+    input_dims: int
+
+    def descriptor(self) -> _lib.Linear:           # pragma: no cover
+        raise NotImplementedError
+
+    def _x_dtype(self):
+        return torch.bfloat16
+
+    def forward(self, x: torch.Tensor, indices: torch.Tensor,
+                sorted_indices: bool = False) -> torch.Tensor:
+        """y[..., k, 1, OUT] = x @ W[indices]^T.
+
+        x is `[..., 1, 1, IN]` (one row per token, SwitchGLU's
+        `expand_dims(x, (-2, -3))`), `[..., k, 1, IN]` (one row per
+        (token, slot)), or, with indices `[N]`, `[N, 1, IN]` (the sorted
+        form `_gather_sort` makes). `sorted_indices` is accepted for the
+        reference's signature; the kernel groups pairs by expert itself."""
+        require_cuda(x, indices)
+        if x.dtype != torch.bfloat16:
+            raise TypeError(f"x must be bfloat16, got {x.dtype}")
+        if x.shape[-1] != self.input_dims:
+            raise ValueError(f"x has {x.shape[-1]} features, the module "
+                             f"{self.input_dims}")
+        # gather_mm's rule: x's batch shape x.shape[:-2] broadcasts against
+        # the indices' shape; one output row per index
+        if x.dim() < 2 or x.shape[-2] != 1:
+            raise ValueError(f"x must be [..., 1, IN], got {tuple(x.shape)}")
+        xb, ib = tuple(x.shape[:-2]), tuple(indices.shape)
+        try:
+            B = tuple(torch.broadcast_shapes(xb, ib))
+        except RuntimeError:
+            raise ValueError(f"x {tuple(x.shape)} does not broadcast with "
+                             f"indices {ib}") from None
+        if B != ib:
+            raise ValueError(f"indices {ib} must cover x's batch {xb}")
+        P = int(np.prod(B)) if B else 1
+        k = B[-1] if B else 1
+        if len(xb) == len(B) and xb[:-1] == B[:-1] and xb[-1] == 1 and k > 1:
+            per_pair, tokens = 0, P // k          # one x row per token
+        else:
+            if xb != B:
+                x = x.expand(*B, 1, self.input_dims)
+            per_pair, tokens, k = 1, P, 1         # one x row per index
+        xi = _contig(x.reshape(-1, self.input_dims))
+        ii = _contig(indices.reshape(-1).to(torch.int32))
+        y = torch.empty((P, self.output_dims), dtype=torch.bfloat16, device=x.device)
+        d = self.descriptor()
+        _lib.call("vqmoe_switch_linear", ctypes_ref(d), xi.data_ptr(),
+                  per_pair, ii.data_ptr(), tokens, k, y.data_ptr(), _stream(x))
+        return y.reshape(*B, 1, self.output_dims)
+
+
+def ctypes_ref(s):
+    import ctypes
+    return ctypes.byref(s)
+
+
+class SwitchLinear(_SwitchBase):
+    """bf16 experts: weight [E, OUT, IN] (`switch_layers.py:89-125`)."""
+
+    def __init__(self, weight: torch.Tensor):
+        super().__init__()
+        if weight.dim() != 3:
+            raise ValueError(f"weight must be [E, OUT, IN], got {tuple(weight.shape)}")
+        self.weight = nn.Parameter(weight.to(torch.bfloat16).contiguous(),
+                                   requires_grad=False)
+
+    @property
+    def num_experts(self):
+        return self.weight.shape[0]
+
+    @property
+    def output_dims(self):
+        return self.weight.shape[1]
+
+    @property
+    def input_dims(self):
+        return self.weight.shape[2]
+
+    def descriptor(self) -> _lib.Linear:
+        w = self.weight
+        require_cuda(w)
+        return _lib.Linear(format=_lib.FMT_DENSE_BF16, num_experts=w.shape[0],
+                           out_features=w.shape[1], in_features=w.shape[2],
+                           weight=w.data_ptr())
+
+
+class VQSwitchLinear(_SwitchBase):
+    """VQ experts: codes [E, OUT, IN/dim] uint8 (one code per entry),
+    codebook [K, dim] fp16 (shared by all experts, never split), vq_scales
+    [E, OUT, IN/group] fp16.
+
+    Weight of expert e, row o, input i (the dequantisation this build
+    defines; the reference runtime is absent):
+        W = fp16(codebook[codes[e, o, i // dim], i % dim] * vq_scales[e, o, i // group])
+    and the activations enter the matmul as fp16.
+
+    `codes` stays in the reference layout; the kernels read a permuted copy
+    (`vqmoe_prepare_codes`) made on the module's device at first use.
+    Packed codes (`pack_bits` > 0, uint32 words of ceil(log2 K)-bit fields)
+    are rejected: their bit order is not pinned by the reference."""
+
+    def __init__(self, codes: torch.Tensor, codebook: torch.Tensor,
+                 vq_scales: torch.Tensor, *, group_size: int, pack_bits: int = 0,
+                 in_features: int | None = None):
+        super().__init__()
+        if codes.dim() != 3 or vq_scales.dim() != 3 or codebook.dim() != 2:
+            raise ValueError("VQ needs codes [E, OUT, W], codebook [K, dim] and "
+                             "vq_scales [E, OUT, IN/group]")
+        E, OUT, W = (int(n) for n in codes.shape)
+        K, dim = (int(n) for n in codebook.shape)
+        if pack_bits:
+            raise NotImplementedError(
+                f"packed {pack_bits}-bit VQ codes are not supported (the field "
+                "order inside a uint32 word is not pinned); pass one code per "
+                "entry (pack_bits=0)")
+        IN = W * dim
+        if in_features is not None and int(in_features) != IN:
+            raise ValueError(f"codes rows are {W} wide; in={in_features} at dim "
+                             f"{dim} needs {int(in_features) // dim} codes")
+        ngrp = int(vq_scales.shape[-1])
+        if tuple(vq_scales.shape[:2]) != (E, OUT):
+            raise ValueError(f"vq_scales {tuple(vq_scales.shape)}: shape mismatch "
+                             f"with codes {tuple(codes.shape)}")
+        if ngrp <= 0 or IN % ngrp or IN // ngrp != int(group_size):
+            raise ValueError(f"in={IN} does not divide into {ngrp} scale groups "
+                             f"of {group_size}")
+        if codes.dtype != torch.uint8 or K > 256:
+            raise ValueError(f"codes must be uint8 with K <= 256 (got {codes.dtype}, K={K})")
+        self.group_size = int(group_size)
+        self.pack_bits = 0
+        self._k_expect = K
+        self.register_buffer("codes", codes.contiguous(), persistent=True)
+        self.register_buffer("codebook", codebook.to(torch.float16).contiguous())
+        self.register_buffer("vq_scales", vq_scales.to(torch.float16).contiguous())
+        self._dev = None          # (device, data_ptr, prepared codes)
+
+    @property
+    def num_experts(self):
+        return self.codes.shape[0]
+
+    @property
+    def output_dims(self):
+        return self.codes.shape[1]
+
+    @property
+    def input_dims(self):
+        return self.codes.shape[2] * self.codebook.shape[1]
+
+    def prepared_codes(self) -> torch.Tensor:
+        """The device-layout copy of `codes` (made once per device)."""
+        c = self.codes
+        require_cuda(c)
+        key = (c.device, c.data_ptr(), c._version)
+        if self._dev is None or self._dev[0] != key:
+            E, OUT, W = c.shape
+            K = int(self.codebook.shape[0])
+            if self.codebook.shape[1] != 4:
+                raise NotImplementedError(
+                    f"VQ dim {self.codebook.shape[1]} is not supported (dim 4)")
+            bad = torch.zeros(1, dtype=torch.int32, device=c.device)
+            _lib.call("vqmoe_count_bad_codes", c.data_ptr(), c.numel(), K,
+                      bad.data_ptr(), _stream(c))
+            n_bad = int(bad.item())
+            if n_bad:
+                raise ValueError(f"{n_bad} VQ codes are >= the codebook size {K}")
+            out = torch.empty_like(c)
+            _lib.call("vqmoe_prepare_codes", c.data_ptr(), out.data_ptr(),
+                      E * OUT, W, _stream(c))
+            self._dev = (key, out)
+        return self._dev[1]
+
+    def descriptor(self) -> _lib.Linear:
+        pc = self.prepared_codes()
+        require_cuda(self.codebook, self.vq_scales)
+        return _lib.Linear(format=_lib.FMT_VQ_U8, num_experts=self.num_experts,
+                           out_features=self.output_dims,
+                           in_features=self.input_dims, codes=pc.data_ptr(),
+                           codebook=self.codebook.data_ptr(),
+                           scales=self.vq_scales.data_ptr(),
+                           codebook_size=int(self.codebook.shape[0]),
+                           dim=int(self.codebook.shape[1]),
+                           group_size=self.group_size)
+
+    def dequantize(self, first: int = 0, count: int | None = None) -> torch.Tensor:
+        """Dense fp16 weights of experts [first, first + count) -- what the
+        VQ runtime's prefill path decodes experts to (`tuning/measured.py:
+        21-33`)."""
+        count = self.num_experts - first if count is None else count
+        out = torch.empty((count, self.output_dims, self.input_dims),
+                          dtype=torch.float16, device=self.codes.device)
+        d = self.descriptor()
+        _lib.call("vqmoe_dequant", ctypes_ref(d), first, count, out.data_ptr(),
+                  _stream(out))
+        return out
+
+
+class SwitchGLU(nn.Module):
+    """`SwitchGLU` (`switch_layers.py:151-193`) with the Qwen3.5 activation
+    (`_SwiGLU`, `qwen3_5.py:108-112`): y = down(bf16(silu(gate(x))) * up(x))
+    per (token, slot). One fused gate/up launch and one down launch."""
+
+    def __init__(self, gate_proj: _SwitchBase, up_proj: _SwitchBase,
+                 down_proj: _SwitchBase):
+        super().__init__()
+        self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
+
+    def forward(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        require_cuda(x, indices)
+        if x.dtype != torch.bfloat16:
+            raise TypeError(f"x must be bfloat16, got {x.dtype}")
+        H = self.gate_proj.input_dims
+        k = indices.shape[-1]
+        lead = indices.shape[:-1]
+        xi = _contig(x.reshape(-1, H))
+        T = xi.shape[0]
+        ii = _contig(indices.reshape(T, k).to(torch.int32))
+        y = torch.empty((T, k, self.down_proj.output_dims), dtype=torch.bfloat16,
+                        device=x.device)
+        I = self.gate_proj.output_dims
+        ws_bytes = _lib.lib().vqmoe_switch_glu_workspace_size(min(T, 2048), k, I)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+        g, u, d = (m.descriptor() for m in (self.gate_proj, self.up_proj, self.down_proj))
+        _lib.call("vqmoe_switch_glu", ctypes_ref(g), ctypes_ref(u), ctypes_ref(d),
+                  xi.data_ptr(), ii.data_ptr(), T, k, y.data_ptr(), ws.data_ptr(),
+                  ws_bytes, _stream(x))
+        return y.reshape(*lead, k, -1)
