@@ -273,9 +273,10 @@ def run_ours(args, world, rank, local):
     if stage:
         gu_bytes = stage["gateup_bytes"]
         achieved = gu_bytes / (stage["gateup_ms"] / 1e3) / 1e9
-        traffic = traffic_from_profiles("expert_kernel<1,1>", workload)
-        roof = {"bound": "hbm", "kernel": "expert_kernel<VQ, gate/up + SwiGLU>",
+        traffic = traffic_from_profiles("expert_units_kernel<true,true>", workload)
+        roof = {"bound": "hbm", "kernel": "fused VQ gate/up + SwiGLU (+ shared expert gate/up)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "kernel_name": "expert_units_kernel<true, true>",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": int(gu_bytes),
                 "traffic": traffic,
@@ -300,7 +301,7 @@ def run_ours(args, world, rank, local):
         "stages_ms": stage and {k: round(v, 5) for k, v in stage.items() if k.endswith("_ms")},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": 7 * args.steps if cfg.shared_inter else 5 * args.steps,
+        "gpu_launches": 6 * args.steps,
         "clocks": clocks.record(),
     }
     return line
@@ -335,6 +336,8 @@ def stage_profile(blocks, x, cfg, dev, args, world):
                   out.data_ptr(), odt, wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream,
                   arr, 6)
     torch.cuda.synchronize(dev)
+    # events: start | router+route | gate/up stage (routed + shared units) |
+    # down stage (routed + shared) | (same) | combine
     names = ["router_ms", "gateup_ms", "down_ms", "shared_ms", "combine_ms"]
     acc = {k: 0.0 for k in names}
     lay = 0.0
@@ -345,14 +348,17 @@ def stage_profile(blocks, x, cfg, dev, args, world):
     m = len(evs[min(10, n - 1):])
     st = {k: v / m for k, v in acc.items()}
     st["layer_ms"] = lay / m
-    # distinct experts touched (the routing is the same for every copy's
-    # router? no: each copy has its own router -- take copy 0's)
-    ws0 = wss[0]
+    # distinct experts touched: copy 0's routing (every copy has its own
+    # router, all drawn from the same distribution)
     inds = routed_experts(blocks[0], x, dev)
     D = len(set(inds))
     H, I, k = cfg.hidden, cfg.inter // world, cfg.top_k
+    Is = cfg.shared_inter // world
     per = 2 * (I * H // cfg.dim + 2 * I * H // cfg.group)
-    st["gateup_bytes"] = D * per + 2 * cfg.codebook_size * cfg.dim * 2 + T * H * 2 + T * k * I * 2
+    # gate/up launch: routed codes + scales, the two codebooks, the shared
+    # expert's gate/up weights, x (bf16 + its fp16 copy), act out
+    st["gateup_bytes"] = (D * per + 2 * cfg.codebook_size * cfg.dim * 2 + 2 * Is * H * 2
+                          + 2 * T * H * 2 + T * k * I * 2 + T * Is * 2)
     c2 = synth.MoEConfig("x", cfg.experts, cfg.top_k, H, I, cfg.shared_inter // world, T)
     st["layer_bytes"] = synth.algorithmic_bytes(c2, D)
     return st, D

@@ -21,8 +21,9 @@
  *       shared_expert_gate Linear of qwen3_5.py:186)
  *   vqmoe_dequant           the VQ runtime's dense fp16 expert decode
  *       (src/knurlogic/tuning/measured.py:21-33, VQ_DECODE_CHUNK)
- *   vqmoe_prepare_codes     loading VQSwitchLinear.codes (deepseek_v4.py:
- *       111-130 layout) into the device layout the kernels read
+ *   vqmoe_prepare_vq        loading VQSwitchLinear.codes / .vq_scales
+ *       (deepseek_v4.py:111-130 layout) into the device layout the kernels
+ *       read
  *
  * Numerics (matching the reference's rounding order, qwen3_5.py:35-40,
  * 108-112, 170-192): bf16 matmul outputs; fp32 softmax / top-k /
@@ -64,9 +65,9 @@ typedef enum {
 /* Weight formats of one switch (expert) linear. */
 enum {
     VQMOE_FMT_DENSE_BF16 = 0,    /* weight [E, OUT, IN] bf16 (SwitchLinear) */
-    VQMOE_FMT_VQ_U8 = 1          /* codes [E, OUT, IN/dim] uint8, device layout
-                                    (vqmoe_prepare_codes); codebook [K, dim]
-                                    fp16; scales [E, OUT, IN/group] fp16 */
+    VQMOE_FMT_VQ_U8 = 1          /* codes and scales in the device layout
+                                    (vqmoe_prepare_vq); codebook [K, dim] fp16
+                                    (the reference's, shared by all experts) */
 };
 
 /* One switch linear: y[r] = x[r] @ W[expert(r)]^T, W [E, OUT, IN].
@@ -112,10 +113,15 @@ typedef struct {
 enum { VQMOE_OUT_BF16 = 0, VQMOE_OUT_F32 = 1 };
 
 /* Workspace bytes for vqmoe_sparse_moe_block / vqmoe_switch_glu /
- * vqmoe_router at T tokens. */
+ * vqmoe_switch_linear / vqmoe_router at T tokens (host-only queries). */
 VQMOE_API size_t vqmoe_block_workspace_size(const vqmoe_block *blk, int32_t tokens);
-VQMOE_API size_t vqmoe_switch_glu_workspace_size(int32_t tokens, int32_t top_k,
-                                       int32_t inter);
+VQMOE_API size_t vqmoe_switch_glu_workspace_size(const vqmoe_linear *gate,
+                                                 const vqmoe_linear *down,
+                                                 int32_t tokens, int32_t top_k);
+VQMOE_API size_t vqmoe_switch_linear_workspace_size(const vqmoe_linear *w,
+                                                    int32_t tokens,
+                                                    int32_t top_k,
+                                                    int32_t x_per_pair);
 VQMOE_API size_t vqmoe_router_workspace_size(int32_t tokens, int32_t num_experts);
 
 /* SparseMoeBlock.__call__: out[T, H] = routed combine + gated shared expert.
@@ -150,6 +156,7 @@ VQMOE_API vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate,
 VQMOE_API vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x,
                                  int32_t x_per_pair, const int32_t *indices,
                                  int32_t tokens, int32_t top_k, void *y,
+                                 void *workspace, size_t workspace_bytes,
                                  void *stream);
 
 /* Router: inds [T, k] int32 (descending logit, ties to the lower expert),
@@ -165,26 +172,45 @@ VQMOE_API vqmoe_status vqmoe_router(const void *x, const void *router_w,
 /* Dense fp16 weights of experts [first, first + count): out [count, OUT, IN]
  * fp16, W = fp16(codebook[code][j] * scale). */
 VQMOE_API vqmoe_status vqmoe_dequant(const vqmoe_linear *w, int32_t first,
-                           int32_t count, void *out, void *stream);
+                                     int32_t count, void *out, void *stream);
 
-/* Permute reference-layout uint8 codes [rows, codes_per_row] (rows = E*OUT)
- * into the device layout the VQ kernels read. src and dst are distinct
- * device buffers. */
-VQMOE_API vqmoe_status vqmoe_prepare_codes(const uint8_t *src, uint8_t *dst,
-                                 int64_t rows, int32_t codes_per_row,
-                                 void *stream);
+/* Device layout of one VQ switch linear (what vqmoe_linear.codes / .scales
+ * point to): bytes of its codes and of its scales. Rows are padded to a
+ * multiple of 32 and inputs to a multiple of 256, then cut into tiles of
+ * 32 rows x 256 inputs ordered for the kernels' loads (padded weights are
+ * exactly zero). */
+VQMOE_API vqmoe_status vqmoe_vq_layout_bytes(int32_t num_experts,
+                                             int32_t out_features,
+                                             int32_t in_features,
+                                             int64_t *code_bytes,
+                                             int64_t *scale_bytes);
+
+/* Reference-layout codes [E, OUT, IN/4] uint8 and vq_scales [E, OUT, IN/64]
+ * fp16 (device buffers) -> the device layout, into caller buffers sized by
+ * vqmoe_vq_layout_bytes. Requires IN % 64 == 0 and OUT % 16 == 0. */
+VQMOE_API vqmoe_status vqmoe_prepare_vq(const uint8_t *codes,
+                                        const void *scales,
+                                        int32_t num_experts,
+                                        int32_t out_features,
+                                        int32_t in_features,
+                                        uint8_t *codes_dev, void *scales_dev,
+                                        void *stream);
+
+/* Device-layout codes -> reference-layout codes [E, OUT, IN/4]. */
+VQMOE_API vqmoe_status vqmoe_unprepare_codes(const uint8_t *codes_dev,
+                                             int32_t num_experts,
+                                             int32_t out_features,
+                                             int32_t in_features,
+                                             uint8_t *codes, void *stream);
 
 /* *bad_count (device uint32, zeroed by the caller) += the number of codes
  * >= codebook_size among codes[0, count). A loader calls it once; the
  * kernels trust the codes. */
-VQMOE_API vqmoe_status vqmoe_count_bad_codes(const uint8_t *codes, int64_t count,
-                                   int32_t codebook_size, uint32_t *bad_count,
-                                   void *stream);
-
-/* Inverse of vqmoe_prepare_codes (device layout -> reference layout). */
-VQMOE_API vqmoe_status vqmoe_unprepare_codes(const uint8_t *src, uint8_t *dst,
-                                   int64_t rows, int32_t codes_per_row,
-                                   void *stream);
+VQMOE_API vqmoe_status vqmoe_count_bad_codes(const uint8_t *codes,
+                                             int64_t count,
+                                             int32_t codebook_size,
+                                             uint32_t *bad_count,
+                                             void *stream);
 
 /* Message of the last non-OK status returned on this host thread. */
 VQMOE_API const char *vqmoe_last_error(void);

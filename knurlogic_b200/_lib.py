@@ -49,7 +49,10 @@ SIGNATURES = [
     ("vqmoe_abi_version", c_int32, []),
     ("vqmoe_last_error", c_char_p, []),
     ("vqmoe_block_workspace_size", c_size_t, [POINTER(Block), c_int32]),
-    ("vqmoe_switch_glu_workspace_size", c_size_t, [c_int32, c_int32, c_int32]),
+    ("vqmoe_switch_glu_workspace_size", c_size_t,
+     [POINTER(Linear), POINTER(Linear), c_int32, c_int32]),
+    ("vqmoe_switch_linear_workspace_size", c_size_t,
+     [POINTER(Linear), c_int32, c_int32, c_int32]),
     ("vqmoe_router_workspace_size", c_size_t, [c_int32, c_int32]),
     ("vqmoe_sparse_moe_block", c_int32,
      [POINTER(Block), c_void_p, c_int32, c_void_p, c_int32, c_void_p,
@@ -62,18 +65,20 @@ SIGNATURES = [
       c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_switch_linear", c_int32,
      [POINTER(Linear), c_void_p, c_int32, c_void_p, c_int32, c_int32,
-      c_void_p, c_void_p]),
+      c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_router", c_int32,
      [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
       c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_dequant", c_int32,
      [POINTER(Linear), c_int32, c_int32, c_void_p, c_void_p]),
-    ("vqmoe_prepare_codes", c_int32,
-     [c_void_p, c_void_p, c_int64, c_int32, c_void_p]),
+    ("vqmoe_vq_layout_bytes", c_int32,
+     [c_int32, c_int32, c_int32, POINTER(c_int64), POINTER(c_int64)]),
+    ("vqmoe_prepare_vq", c_int32,
+     [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     ("vqmoe_count_bad_codes", c_int32,
      [c_void_p, c_int64, c_int32, c_void_p, c_void_p]),
     ("vqmoe_unprepare_codes", c_int32,
-     [c_void_p, c_void_p, c_int64, c_int32, c_void_p]),
+     [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
 ]
 
 _lock = threading.Lock()
@@ -106,6 +111,13 @@ def lib():
                 f.argtypes = args
             _lib = h
     return _lib
+
+
+def vq_layout_bytes(E: int, OUT: int, IN: int):
+    """(code bytes, scale bytes) of the device layout of one VQ linear."""
+    cb, sb = c_int64(), c_int64()
+    call("vqmoe_vq_layout_bytes", E, OUT, IN, ctypes.byref(cb), ctypes.byref(sb))
+    return cb.value, sb.value
 
 
 def call(name: str, *args) -> None:

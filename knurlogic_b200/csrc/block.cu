@@ -13,18 +13,9 @@
 #include <cstdio>
 #include <cstring>
 
-#include "common.cuh"
+#include "stages.cuh"
 
 namespace vqmoe {
-
-vqmoe_status launch_router(const uint16_t *x, const uint16_t *w,
-                           const uint16_t *wsg, int T, int H, int E, int k,
-                           float *logits, int32_t *inds, float *scores,
-                           float *sgate, cudaStream_t stream);
-vqmoe_status launch_expert(const vqmoe_linear *w0, const vqmoe_linear *w1,
-                           const int32_t *inds, int P, int k, const void *x,
-                           int x_per_pair, void *out, const float *pair_scale,
-                           int list_cap, cudaStream_t stream);
 
 static thread_local char g_err[512] = "";
 
@@ -44,10 +35,15 @@ vqmoe_status check_launch(const char *what) {
 }
 
 int sm_count() {
-    int dev = 0, n = 0;
+    static int cached[64] = {0};
+    int dev = 0;
     cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+    int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    if (dev >= 0 && dev < 64) cached[dev] = n;
+    return n;
 }
 
 // ------------------------------------------------------------- combine
@@ -154,11 +150,60 @@ struct Carve {
     }
 };
 
+// Routing tables + the zeroed words (work counters, split-K semaphores)
+// of a routed gate/up stage followed by a routed down stage.
+struct RouteWs {
+    int32_t *cnt, *off, *list, *active, *rank;
+    uint32_t *zero;      // [0] gate/up counter, [1] down counter, then semaphores
+    int zero_words;
+    uint32_t *sem_gu, *sem_dn, *ssem_gu, *ssem_dn;
+    float *part_gu, *part_dn, *spart_gu, *spart_dn;
+    int ks_gu, ks_dn, sks_gu, sks_dn;
+};
+
+static void carve_route(Carve &c, RouteWs &w, int E, int P, int H, int I, int T, int Is,
+                        bool dual) {
+    w.cnt = c.take<int32_t>(E);
+    w.off = c.take<int32_t>(E + 1);
+    w.list = c.take<int32_t>(P);
+    w.active = c.take<int32_t>(E + 1);
+    w.rank = c.take<int32_t>(P);
+    int rb_gu = 0, rb_dn = 0, srb_gu = 0, srb_dn = 0;
+    w.ks_gu = w.ks_dn = w.sks_gu = w.sks_dn = 1;
+    if (dual) plan_routed(E, P, H, I, &w.ks_gu, &rb_gu);
+    plan_routed(E, P, dual ? I : H, dual ? H : I, &w.ks_dn, &rb_dn);
+    if (Is > 0) {
+        int kl = 0;
+        size_t sm = 0;
+        plan_shared_dense(H, Is, 2, &w.sks_gu, &kl, &sm);
+        plan_shared_dense(Is, H, 1, &w.sks_dn, &kl, &sm);
+        srb_gu = (Is + 31) / 32;
+        srb_dn = (H + 31) / 32;
+    }
+    w.zero_words = 2 + E * rb_gu + E * rb_dn + srb_gu + srb_dn;
+    w.zero = c.take<uint32_t>(w.zero_words);
+    if (w.zero) {
+        w.sem_gu = w.zero + 2;
+        w.sem_dn = w.sem_gu + (size_t)E * rb_gu;
+        w.ssem_gu = w.sem_dn + (size_t)E * rb_dn;
+        w.ssem_dn = w.ssem_gu + srb_gu;
+    }
+    const int nm = dual ? 2 : 1;
+    w.part_gu = dual && w.ks_gu > 1 ? c.take<float>((size_t)w.ks_gu * P * 2 * I) : nullptr;
+    w.part_dn = w.ks_dn > 1 ? c.take<float>((size_t)w.ks_dn * P * (dual ? H : I)) : nullptr;
+    (void)nm;
+    // shared expert partials: T is at most one launch of tokens
+    w.spart_gu = Is > 0 && w.sks_gu > 1 ? c.take<float>((size_t)w.sks_gu * T * 2 * Is) : nullptr;
+    w.spart_dn = Is > 0 && w.sks_dn > 1 ? c.take<float>((size_t)w.sks_dn * T * H) : nullptr;
+}
+
 struct BlockWs {
     float *logits;
     int32_t *inds;
     float *scores;
     float *sgate;
+    uint16_t *x16;
+    RouteWs rt;
     uint16_t *act;
     uint16_t *act_s;
     uint16_t *ybuf;
@@ -169,23 +214,25 @@ struct BlockWs {
 static BlockWs carve_block(void *ws, const vqmoe_block *b, int T) {
     Carve c{static_cast<char *>(ws)};
     BlockWs w{};
-    const int E1 = b->num_experts + 1;
-    const int I = b->gate.out_features;
-    (void)E1;
-    w.logits = c.take<float>((size_t)T * E1);
-    w.inds = c.take<int32_t>((size_t)T * b->top_k);
-    w.scores = c.take<float>((size_t)T * b->top_k);
-    w.sgate = c.take<float>((size_t)T);
-    w.act = c.take<uint16_t>((size_t)T * b->top_k * I);
-    w.act_s = c.take<uint16_t>((size_t)T * std::max(b->shared_inter, 0));
-    w.ybuf = c.take<uint16_t>((size_t)T * b->top_k * b->hidden);
-    w.sh = c.take<uint16_t>((size_t)T * b->hidden);
+    const int E = b->num_experts, k = b->top_k, H = b->hidden;
+    const int I = b->gate.out_features, Is = std::max(b->shared_inter, 0);
+    const int P = T * k;
+    w.logits = c.take<float>((size_t)T * (E + 1));
+    w.inds = c.take<int32_t>(P);
+    w.scores = c.take<float>(P);
+    w.sgate = c.take<float>(T);
+    w.x16 = b->gate.format == VQMOE_FMT_VQ_U8 ? c.take<uint16_t>((size_t)T * H) : nullptr;
+    carve_route(c, w.rt, E, P, H, I, T, Is, true);
+    w.act = c.take<uint16_t>((size_t)P * I);
+    w.act_s = c.take<uint16_t>((size_t)T * Is);
+    w.ybuf = c.take<uint16_t>((size_t)P * H);
+    w.sh = c.take<uint16_t>((size_t)T * H);
     w.bytes = align_up(c.off, 256);
     return w;
 }
 
-// Tokens per launch of the expert kernels: the per-CTA pair list lives in
-// shared memory; a larger T is processed in independent token chunks.
+// Tokens per launch sequence; a larger T runs as independent token chunks
+// (bounds the workspace).
 constexpr int kMaxTokensPerLaunch = 2048;
 
 static vqmoe_status check_block(const vqmoe_block *b, int T) {
@@ -218,49 +265,72 @@ static vqmoe_status check_block(const vqmoe_block *b, int T) {
     return VQMOE_OK;
 }
 
-static vqmoe_linear dense_linear(const void *w, int out, int in) {
-    vqmoe_linear d{};
-    d.format = VQMOE_FMT_DENSE_BF16;
-    d.num_experts = 1;
-    d.out_features = out;
-    d.in_features = in;
-    d.weight = w;
-    return d;
-}
-
-// events (optional, n_ev >= 6): recorded before the router and after the
-// router, the routed gate/up, the routed down, the shared expert, combine.
+// events (optional, n_ev >= 6): recorded before the router, after the
+// routing, after the gate/up stage (routed + shared), after the down stage,
+// again after the down stage (the shared expert runs inside both stages),
+// and after the combine.
 static vqmoe_status mark(cudaEvent_t *ev, int n_ev, int i, cudaStream_t st) {
     if (ev && i < n_ev && cudaEventRecord(ev[i], st) != cudaSuccess)
         return set_error(VQMOE_LAUNCH_FAILED, "event %d", i);
     return VQMOE_OK;
 }
 
+static RoutedIO routed_io(const RouteWs &rt, int E, int k, int P, const void *x, int x_per_pair,
+                          void *out, int out_f16, const float *scale, float *part, uint32_t *sem,
+                          int ks) {
+    RoutedIO r{};
+    r.cnt = rt.cnt;
+    r.off = rt.off;
+    r.list = rt.list;
+    r.active = rt.active;
+    r.E = E;
+    r.k = k;
+    r.P = P;
+    r.x = x;
+    r.x_per_pair = x_per_pair;
+    r.out = out;
+    r.out_f16 = out_f16;
+    r.pair_scale = scale;
+    r.part = part;
+    r.sem = sem;
+    r.ks = ks;
+    return r;
+}
+
 static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                               void *out, int out_f32, const BlockWs &w,
                               cudaStream_t st, cudaEvent_t *ev = nullptr, int n_ev = 0) {
-    const int H = b->hidden, E = b->num_experts, k = b->top_k;
+    const int H = b->hidden, E = b->num_experts, k = b->top_k, P = T * k;
     const int Is = b->shared_inter;
     const bool shared = Is > 0;
+    const bool vq_in = b->gate.format == VQMOE_FMT_VQ_U8;
+    const bool vq_dn = b->down.format == VQMOE_FMT_VQ_U8;
     vqmoe_status s;
     if ((s = mark(ev, n_ev, 0, st)) != VQMOE_OK) return s;
     s = launch_router(x, static_cast<const uint16_t *>(b->router_w),
-                                   shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr,
-                                   T, H, E, k, w.logits, w.inds, w.scores, w.sgate, st);
+                      shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr,
+                      T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, st);
+    if (s != VQMOE_OK) return s;
+    const RouteWs &rt = w.rt;
+    s = launch_route(w.inds, P, E, rt.cnt, rt.off, rt.list, rt.active, rt.rank, rt.zero,
+                     rt.zero_words, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 1, st)) != VQMOE_OK) return s;
-    s = launch_expert(&b->gate, &b->up, w.inds, T * k, k, x, 0, w.act, nullptr, T, st);
+    // gate/up + SwiGLU (routed VQ / bf16 experts, and the shared expert)
+    RoutedIO r1 = routed_io(rt, E, k, P, vq_in ? (const void *)w.x16 : (const void *)x, 0, w.act,
+                            vq_dn, nullptr, rt.part_gu, rt.sem_gu, rt.ks_gu);
+    if (shared && (s = launch_shared_dense(x, b->shared_gate_w, b->shared_up_w, T, H, Is, w.act_s,
+                                           rt.spart_gu, rt.ssem_gu, st)) != VQMOE_OK)
+        return s;
+    s = launch_expert_stage(&b->gate, &b->up, &r1, nullptr, rt.zero, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK) return s;
-    s = launch_expert(&b->down, nullptr, w.inds, T * k, k, w.act, 1, w.ybuf, w.scores, T, st);
+    // down (x routing weight), and the shared expert's down
+    RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores, rt.part_dn, rt.sem_dn,
+                            rt.ks_dn);
+    if (shared && (s = launch_shared_dense(w.act_s, b->shared_down_w, nullptr, T, Is, H, w.sh,
+                                           rt.spart_dn, rt.ssem_dn, st)) != VQMOE_OK)
+        return s;
+    s = launch_expert_stage(&b->down, nullptr, &r2, nullptr, rt.zero + 1, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 3, st)) != VQMOE_OK) return s;
-    if (shared) {
-        vqmoe_linear sg = dense_linear(b->shared_gate_w, Is, H);
-        vqmoe_linear su = dense_linear(b->shared_up_w, Is, H);
-        vqmoe_linear sd = dense_linear(b->shared_down_w, H, Is);
-        s = launch_expert(&sg, &su, nullptr, T, 1, x, 1, w.act_s, nullptr, 0, st);
-        if (s != VQMOE_OK) return s;
-        s = launch_expert(&sd, nullptr, nullptr, T, 1, w.act_s, 1, w.sh, nullptr, 0, st);
-        if (s != VQMOE_OK) return s;
-    }
     if ((s = mark(ev, n_ev, 4, st)) != VQMOE_OK) return s;
     const size_t nvec = (size_t)T * (H / 8);
     const int grid = (int)std::min<size_t>((nvec + 255) / 256, (size_t)sm_count() * 8);
@@ -269,60 +339,47 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
     return mark(ev, n_ev, 5, st);
 }
 
-// ------------------------------------------------------ prepare / dequant
+// Workspace of vqmoe_switch_glu / vqmoe_switch_linear at T tokens.
+struct GluWs {
+    uint16_t *x16;
+    RouteWs rt;
+    uint16_t *act;
+    size_t bytes;
+};
 
-// code 4q+t of a chunk of 4*nq codes <-> device position t*nq+q
-__global__ void permute_codes_kernel(const uint8_t *__restrict__ src,
-                                     uint8_t *__restrict__ dst, long long rows,
-                                     int ncodes, int to_device) {
-    const long long total = rows * ncodes;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long r = i / ncodes;
-        const int c = (int)(i - r * ncodes);
-        const int c0 = c & ~63, n = min(64, ncodes - c0), nq = n >> 2;
-        const int u = c - c0;                     // reference position in chunk
-        const int d = c0 + (u & 3) * nq + (u >> 2);  // device position
-        if (to_device)
-            dst[r * ncodes + d] = src[r * ncodes + c];
-        else
-            dst[r * ncodes + c] = src[r * ncodes + d];
+static GluWs carve_glu(void *ws, const vqmoe_linear *first, const vqmoe_linear *down, int T, int k,
+                       int rows_x) {
+    Carve c{static_cast<char *>(ws)};
+    GluWs w{};
+    const int E = first->num_experts, P = T * k;
+    const bool dual = down != nullptr;
+    w.x16 = first->format == VQMOE_FMT_VQ_U8 ? c.take<uint16_t>((size_t)rows_x * first->in_features)
+                                             : nullptr;
+    const int H = first->in_features, I = first->out_features;
+    carve_route(c, w.rt, E, P, H, I, T, 0, dual);
+    w.act = dual ? c.take<uint16_t>((size_t)P * I) : nullptr;
+    w.bytes = align_up(c.off, 256);
+    return w;
+}
+
+// x (bf16) -> fp16 (saturated), 8 elements per thread
+__global__ void to_f16_kernel(const uint16_t *__restrict__ x, uint16_t *__restrict__ y, size_t n8) {
+    for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < n8;
+         v += (size_t)gridDim.x * blockDim.x) {
+        uint4 val = reinterpret_cast<const uint4 *>(x)[v];
+        uint32_t u[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            u[j] = (uint32_t)bf16_to_f16_sat(u[j] & 0xFFFFu) | ((uint32_t)bf16_to_f16_sat(u[j] >> 16) << 16);
+        reinterpret_cast<uint4 *>(y)[v] = make_uint4(u[0], u[1], u[2], u[3]);
     }
 }
 
-// *bad_count += number of codes >= K (the caller zeroes it first)
-__global__ void count_bad_codes_kernel(const uint8_t *__restrict__ codes, long long n, int K,
-                                       uint32_t *__restrict__ bad_count) {
-    uint32_t bad = 0;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-         i += (long long)gridDim.x * blockDim.x)
-        bad += codes[i] >= K;
-    for (int o = 16; o > 0; o >>= 1) bad += __shfl_xor_sync(0xffffffffu, bad, o);
-    if ((threadIdx.x & 31) == 0 && bad) atomicAdd(bad_count, bad);
-}
-
-__global__ void dequant_kernel(const uint8_t *__restrict__ codes,
-                               const uint16_t *__restrict__ cb,
-                               const uint16_t *__restrict__ scales, int OUT,
-                               int IN, long long first_row, long long rows,
-                               uint16_t *__restrict__ out) {
-    const int ncodes = IN / 4;
-    const long long total = rows * ncodes;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long r = i / ncodes;
-        const int c = (int)(i - r * ncodes);
-        const int c0 = c & ~63, n = min(64, ncodes - c0), nq = n >> 2;
-        const int u = c - c0;
-        const int d = c0 + (u & 3) * nq + (u >> 2);
-        const long long rr = first_row + r;
-        const uint32_t code = codes[rr * ncodes + d];
-        const uint16_t s = scales[rr * (IN / 64) + (c * 4) / 64];
-        const uint32_t s2 = (uint32_t)s | ((uint32_t)s << 16);
-        const uint2 e = *reinterpret_cast<const uint2 *>(cb + code * 4);
-        const uint2 w = make_uint2(hmul2_u32(e.x, s2), hmul2_u32(e.y, s2));
-        *reinterpret_cast<uint2 *>(out + r * IN + c * 4) = w;
-    }
+vqmoe_status launch_to_f16(const uint16_t *x, uint16_t *x16, size_t n, cudaStream_t stream) {
+    const size_t n8 = n / 8;
+    const int grid = (int)std::min<size_t>((n8 + 255) / 256, (size_t)sm_count() * 8);
+    to_f16_kernel<<<std::max(grid, 1), 256, 0, stream>>>(x, x16, n8);
+    return check_launch("to_f16_kernel");
 }
 
 }  // namespace vqmoe
@@ -341,8 +398,18 @@ size_t vqmoe_router_workspace_size(int32_t tokens, int32_t num_experts) {
     return align_up((size_t)tokens * (num_experts + 1) * sizeof(float), 256);
 }
 
-size_t vqmoe_switch_glu_workspace_size(int32_t tokens, int32_t top_k, int32_t inter) {
-    return align_up((size_t)tokens * top_k * inter * 2, 256);
+size_t vqmoe_switch_glu_workspace_size(const vqmoe_linear *gate, const vqmoe_linear *down,
+                                       int32_t tokens, int32_t top_k) {
+    if (!gate || !down || tokens <= 0 || top_k <= 0) return 0;
+    const int T = std::min<int>(tokens, kMaxTokensPerLaunch);
+    return carve_glu(nullptr, gate, down, T, top_k, T).bytes;
+}
+
+size_t vqmoe_switch_linear_workspace_size(const vqmoe_linear *w, int32_t tokens, int32_t top_k,
+                                          int32_t x_per_pair) {
+    if (!w || tokens <= 0 || top_k <= 0) return 0;
+    const int T = std::min<int>(tokens, kMaxTokensPerLaunch);
+    return carve_glu(nullptr, w, nullptr, T, top_k, x_per_pair ? T * top_k : T).bytes;
 }
 
 size_t vqmoe_block_workspace_size(const vqmoe_block *blk, int32_t tokens) {
@@ -404,50 +471,71 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
     if ((s = check_linear(up, "up_proj")) != VQMOE_OK) return s;
     if ((s = check_linear(down, "down_proj")) != VQMOE_OK) return s;
     if (tokens <= 0 || top_k <= 0) return set_error(VQMOE_BAD_SHAPE, "tokens %d top_k %d", tokens, top_k);
-    const int I = gate->out_features, H = gate->in_features;
+    const int I = gate->out_features, H = gate->in_features, E = gate->num_experts;
     if (up->out_features != I || up->in_features != H || down->out_features != H ||
-        down->in_features != I || up->num_experts != gate->num_experts ||
-        down->num_experts != gate->num_experts || gate->format != up->format)
+        down->in_features != I || up->num_experts != E || down->num_experts != E ||
+        gate->format != up->format)
         return set_error(VQMOE_BAD_SHAPE, "switch_glu: inconsistent gate/up/down shapes");
+    if (E > 1024) return set_error(VQMOE_BAD_SHAPE, "switch_glu: %d experts (<= 1024)", E);
     if (!aligned_ptr(x) || !aligned_ptr(y) || !indices || !aligned_ptr(workspace))
         return set_error(VQMOE_BAD_POINTER, "x / indices / y / workspace");
     const int chunk = std::min<int>(tokens, kMaxTokensPerLaunch);
-    const size_t need = vqmoe_switch_glu_workspace_size(chunk, top_k, I);
-    if (workspace_bytes < need)
-        return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, need);
+    GluWs w = carve_glu(workspace, gate, down, chunk, top_k, chunk);
+    if (workspace_bytes < w.bytes)
+        return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, w.bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    uint16_t *act = static_cast<uint16_t *>(workspace);
+    const bool vq_in = gate->format == VQMOE_FMT_VQ_U8, vq_dn = down->format == VQMOE_FMT_VQ_U8;
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
-        const int T = std::min(chunk, tokens - t0);
+        const int T = std::min(chunk, tokens - t0), P = T * top_k;
         const int32_t *ind = indices + (size_t)t0 * top_k;
-        s = launch_expert(gate, up, ind, T * top_k, top_k,
-                          static_cast<const uint16_t *>(x) + (size_t)t0 * H, 0, act, nullptr, T, st);
-        if (s != VQMOE_OK) return s;
-        s = launch_expert(down, nullptr, ind, T * top_k, top_k, act, 1,
-                          static_cast<uint16_t *>(y) + (size_t)t0 * top_k * H, nullptr, T, st);
-        if (s != VQMOE_OK) return s;
+        const uint16_t *xt = static_cast<const uint16_t *>(x) + (size_t)t0 * H;
+        const RouteWs &rt = w.rt;
+        if (vq_in && (s = launch_to_f16(xt, w.x16, (size_t)T * H, st)) != VQMOE_OK) return s;
+        if ((s = launch_route(ind, P, E, rt.cnt, rt.off, rt.list, rt.active, rt.rank, rt.zero,
+                              rt.zero_words, st)) != VQMOE_OK)
+            return s;
+        RoutedIO r1 = routed_io(rt, E, top_k, P, vq_in ? (const void *)w.x16 : (const void *)xt, 0,
+                                w.act, vq_dn, nullptr, rt.part_gu, rt.sem_gu, rt.ks_gu);
+        if ((s = launch_expert_stage(gate, up, &r1, nullptr, rt.zero, st)) != VQMOE_OK) return s;
+        RoutedIO r2 = routed_io(rt, E, top_k, P, w.act, 1,
+                                static_cast<uint16_t *>(y) + (size_t)t0 * top_k * H, 0, nullptr,
+                                rt.part_dn, rt.sem_dn, rt.ks_dn);
+        if ((s = launch_expert_stage(down, nullptr, &r2, nullptr, rt.zero + 1, st)) != VQMOE_OK) return s;
     }
     return VQMOE_OK;
 }
 
 vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x_per_pair,
                                  const int32_t *indices, int32_t tokens, int32_t top_k,
-                                 void *y, void *stream) {
+                                 void *y, void *workspace, size_t workspace_bytes, void *stream) {
     vqmoe_status s;
     if ((s = check_linear(w, "switch_linear")) != VQMOE_OK) return s;
     if (tokens <= 0 || top_k <= 0) return set_error(VQMOE_BAD_SHAPE, "tokens %d top_k %d", tokens, top_k);
-    if (!aligned_ptr(x) || !aligned_ptr(y) || !indices)
-        return set_error(VQMOE_BAD_POINTER, "x / indices / y");
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (w->num_experts > 1024) return set_error(VQMOE_BAD_SHAPE, "switch_linear: %d experts (<= 1024)", w->num_experts);
+    if (!aligned_ptr(x) || !aligned_ptr(y) || !indices || !aligned_ptr(workspace))
+        return set_error(VQMOE_BAD_POINTER, "x / indices / y / workspace");
     const int chunk = std::min<int>(tokens, kMaxTokensPerLaunch);
+    const int rows_x = x_per_pair ? chunk * top_k : chunk;
+    GluWs ws = carve_glu(workspace, w, nullptr, chunk, top_k, rows_x);
+    if (workspace_bytes < ws.bytes)
+        return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, ws.bytes);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool vq = w->format == VQMOE_FMT_VQ_U8;
+    const int IN = w->in_features, E = w->num_experts;
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
-        const int T = std::min(chunk, tokens - t0);
+        const int T = std::min(chunk, tokens - t0), P = T * top_k;
         const size_t xrow0 = x_per_pair ? (size_t)t0 * top_k : (size_t)t0;
-        s = launch_expert(w, nullptr, indices + (size_t)t0 * top_k, T * top_k, top_k,
-                          static_cast<const uint16_t *>(x) + xrow0 * w->in_features, x_per_pair,
-                          static_cast<uint16_t *>(y) + (size_t)t0 * top_k * w->out_features,
-                          nullptr, T, st);
-        if (s != VQMOE_OK) return s;
+        const size_t nrows = x_per_pair ? (size_t)P : (size_t)T;
+        const uint16_t *xt = static_cast<const uint16_t *>(x) + xrow0 * IN;
+        const RouteWs &rt = ws.rt;
+        if (vq && (s = launch_to_f16(xt, ws.x16, nrows * IN, st)) != VQMOE_OK) return s;
+        if ((s = launch_route(indices + (size_t)t0 * top_k, P, E, rt.cnt, rt.off, rt.list, rt.active,
+                              rt.rank, rt.zero, rt.zero_words, st)) != VQMOE_OK)
+            return s;
+        RoutedIO r = routed_io(rt, E, top_k, P, vq ? (const void *)ws.x16 : (const void *)xt,
+                               x_per_pair, static_cast<uint16_t *>(y) + (size_t)t0 * top_k * w->out_features,
+                               0, nullptr, rt.part_dn, rt.sem_dn, rt.ks_dn);
+        if ((s = launch_expert_stage(w, nullptr, &r, nullptr, rt.zero + 1, st)) != VQMOE_OK) return s;
     }
     return VQMOE_OK;
 }
@@ -467,62 +555,8 @@ vqmoe_status vqmoe_router(const void *x, const void *router_w, const void *sgw,
         return set_error(VQMOE_WORKSPACE_TOO_SMALL, "router workspace");
     return launch_router(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(router_w),
                          static_cast<const uint16_t *>(sgw), tokens, hidden, num_experts, top_k,
-                         static_cast<float *>(workspace), inds, scores, sgate,
+                         static_cast<float *>(workspace), inds, scores, sgate, nullptr,
                          static_cast<cudaStream_t>(stream));
-}
-
-vqmoe_status vqmoe_dequant(const vqmoe_linear *w, int32_t first, int32_t count, void *out,
-                           void *stream) {
-    vqmoe_status s;
-    if ((s = check_linear(w, "dequant")) != VQMOE_OK) return s;
-    if (w->format != VQMOE_FMT_VQ_U8) return set_error(VQMOE_BAD_FORMAT, "dequant: not a VQ linear");
-    if (first < 0 || count <= 0 || first + count > w->num_experts)
-        return set_error(VQMOE_BAD_SHAPE, "dequant: experts [%d, %d) of %d", first, first + count,
-                         w->num_experts);
-    if (!aligned_ptr(out)) return set_error(VQMOE_BAD_POINTER, "dequant: out");
-    const long long rows = (long long)count * w->out_features;
-    const long long total = rows * (w->in_features / 4);
-    const int grid = (int)std::min<long long>((total + 255) / 256, (long long)sm_count() * 16);
-    dequant_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint8_t *>(w->codes), static_cast<const uint16_t *>(w->codebook),
-        static_cast<const uint16_t *>(w->scales), w->out_features, w->in_features,
-        (long long)first * w->out_features, rows, static_cast<uint16_t *>(out));
-    return check_launch("dequant_kernel");
-}
-
-static vqmoe_status permute(const uint8_t *src, uint8_t *dst, int64_t rows, int32_t ncodes,
-                            int to_device, void *stream) {
-    if (!src || !dst || rows <= 0 || ncodes <= 0 || ncodes % 16)
-        return set_error(VQMOE_BAD_SHAPE, "codes: rows %lld codes_per_row %d (a multiple of 16)",
-                         (long long)rows, ncodes);
-    if (src == dst) return set_error(VQMOE_BAD_POINTER, "codes: src and dst must not overlap");
-    const long long total = (long long)rows * ncodes;
-    const int grid = (int)std::min<long long>((total + 255) / 256, (long long)sm_count() * 16);
-    permute_codes_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(src, dst, rows, ncodes,
-                                                                            to_device);
-    return check_launch("permute_codes_kernel");
-}
-
-vqmoe_status vqmoe_prepare_codes(const uint8_t *src, uint8_t *dst, int64_t rows,
-                                 int32_t codes_per_row, void *stream) {
-    return permute(src, dst, rows, codes_per_row, 1, stream);
-}
-
-vqmoe_status vqmoe_unprepare_codes(const uint8_t *src, uint8_t *dst, int64_t rows,
-                                   int32_t codes_per_row, void *stream) {
-    return permute(src, dst, rows, codes_per_row, 0, stream);
-}
-
-vqmoe_status vqmoe_count_bad_codes(const uint8_t *codes, int64_t count, int32_t codebook_size,
-                                   uint32_t *bad_count, void *stream) {
-    if (!codes || !bad_count || count <= 0)
-        return set_error(VQMOE_BAD_POINTER, "count_bad_codes: pointers / count");
-    if (codebook_size <= 0 || codebook_size > 256)
-        return set_error(VQMOE_BAD_FORMAT, "codebook_size %d (1..256)", codebook_size);
-    const int grid = (int)std::min<long long>((count + 255) / 256, (long long)sm_count() * 16);
-    count_bad_codes_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(codes, count,
-                                                                              codebook_size, bad_count);
-    return check_launch("count_bad_codes_kernel");
 }
 
 }  // extern "C"

@@ -61,35 +61,37 @@ __device__ __forceinline__ float sigmoid_f32(float g) {
 }
 
 // -------------------------------------------------------------- loads
-
+// Global loads through the CUDA intrinsics: the compiler schedules them
+// freely but never speculates them past the branch that guards their
+// pointer (an asm statement without side effects could be hoisted out of
+// its branch and dereference an unset pointer).
 __device__ __forceinline__ uint4 ldg_stream_v4(const void *p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
+    return __ldcs(reinterpret_cast<const uint4 *>(p));
 }
 
 __device__ __forceinline__ uint32_t ldg_stream_u32(const void *p) {
-    uint32_t r;
-    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];\n"
-                 : "=r"(r)
-                 : "l"(p));
-    return r;
+    return __ldcs(reinterpret_cast<const unsigned int *>(p));
 }
 
 __device__ __forceinline__ uint2 ldg_nc_v2(const void *p) {
-    uint2 r;
-    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n"
-                 : "=r"(r.x), "=r"(r.y)
-                 : "l"(p));
-    return r;
+    return __ldg(reinterpret_cast<const uint2 *>(p));
+}
+
+__device__ __forceinline__ uint2 ldg_stream_v2(const void *p) {
+    return __ldcs(reinterpret_cast<const uint2 *>(p));
+}
+
+// 16-byte async copy global -> shared; src_bytes < 16 zero-fills the rest
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(g),
+                 "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
 }
 
 __device__ __forceinline__ uint16_t ldg_nc_u16(const void *p) {
-    uint16_t r;
-    asm volatile("ld.global.nc.u16 %0, [%1];\n" : "=h"(r) : "l"(p));
-    return r;
+    return __ldg(reinterpret_cast<const unsigned short *>(p));
 }
 
 __device__ __forceinline__ uint2 lds_v2(uint32_t saddr) {
@@ -113,11 +115,12 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
 
 // ---------------------------------------------------------------- mma
 
-// D += A(16x16, row) * B(16x8, col); fp32 accumulate.
+// D += A(16x16, row) * B(16x8, col); fp32 accumulate. Not volatile: a pure
+// function of its registers, so the compiler may interleave it with loads.
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
                                         uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -127,7 +130,7 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
 __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0,
                                          uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

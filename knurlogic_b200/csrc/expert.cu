@@ -3,19 +3,28 @@
 // Reference: SwitchGLU.__call__ / SwitchLinear.__call__
 // (glm5_next/_mlx_vlm/models/switch_layers.py:116-125, 172-193) with the
 // experts as VQSwitchLinear (codes, codebook, vq_scales; layout from
-// engine/families/deepseek/heads/deepseek_v4.py:35-42, 111-130).
+// engine/families/deepseek/heads/deepseek_v4.py:35-42, 111-130), plus the
+// shared expert's dense matmuls (qwen3_5.py:184-185).
 //
-// One persistent kernel family computes, for every (token, slot) pair routed
-// to an expert, out[pair] = x_row(pair) @ W[expert]^T with the weights
-// dequantised in registers:
-//   * VQ: each 8-byte codebook entry (4 fp16) is read from a shared-memory
-//     copy and multiplied by its fp16 group scale in one mul.rn.f16x2 -- the
-//     product IS the dequantised fp16 weight -- and those registers are the
-//     A operand of mma.sync m16n8k16 (fp16 x fp16 -> fp32). B is the
-//     expert's (<= 8) token rows, staged in shared memory as fp16.
-//   * dense bf16 experts and the shared expert: A is loaded from HBM as is
-//     (bf16 x bf16 -> fp32).
-// Why mma.sync and registers rather than tcgen05 here: at 1-64 tokens the
+// One persistent kernel per projection stage (fused gate/up + SwiGLU, or
+// down), two CTAs per SM. A CTA takes tiles from a global counter: a tile
+// is (routed expert, 128 or 256 output rows) or (shared expert, rows). The
+// CTA stages the tile's token rows (<= 8 at a time, fp16 for VQ) in shared
+// memory once; each of its 8 warps then computes 16 (gate/up) or 32 (down)
+// output rows over the whole K, and writes its results from registers (the
+// SwiGLU or the routing weight applied there). No split K, no partials.
+//
+// For a VQ tile each lane
+//   * streams its codes and group scales through a ring of four register
+//     half-chunk buffers (loads issued three half chunks, ~1 us, ahead);
+//   * looks each code up in a shared-memory codebook and multiplies the
+//     8-byte entry (4 fp16) by its group scale in one mul.rn.f16x2 -- the
+//     product is the dequantised fp16 weight -- and feeds those registers
+//     straight into mma.sync m16n8k16 as the A operand (fp16 x fp16 ->
+//     fp32); B is the tile's token rows from shared memory.
+// Dense tiles (bf16 experts, the shared expert) load A from global memory.
+//
+// Why mma.sync and registers here rather than tcgen05: at 1-64 tokens the
 // layer is bound by HBM and by the shared-memory codebook lookups (8 bytes
 // per code, ~16 codes/clk/SM), not by tensor throughput (~4 tokens per
 // expert). A register-fed A operand keeps every dequantised weight out of
@@ -23,362 +32,596 @@
 //
 // Codebook replication: 16 copies interleaved so that lane L reads only the
 // bank pair L % 16; a warp's random 8-byte lookups are then conflict-free
-// (2 wavefronts, the minimum for 256 bytes). 32 KB per codebook.
+// (2 wavefronts, the minimum for 256 bytes). Entry c of copy b of matrix m
+// sits at byte 256*c + 128*m + 8*b (64 KB for gate and up together), so
+// one byte permute builds a lookup address: byte 1 = the code, byte 0 =
+// the lane's copy offset.
 //
-// Device code layout (vqmoe_prepare_codes): each row's codes in chunks of
-// 64 (256 inputs); inside a chunk of 4*nq codes, code 4q+t sits at t*nq+q,
-// so thread t of an MMA quad loads its nq codes with one 16-byte load and
-// sub-step q covers inputs [16q, 16q+16) of the chunk in natural order.
-// MMA k-slots {2t, 2t+1, 2t+8, 2t+9} carry inputs 16q+4t+{0,1,2,3}: the same
+// Device layout (layout.cuh): codes and scales tiled per (expert, 32 rows,
+// 256 inputs) in the order the lanes consume them, so a warp's loads are
+// contiguous 256-byte requests off one base pointer per matrix. MMA
+// sub-step q of a chunk covers inputs [16q, 16q+16); its k-slots
+// {2t, 2t+1, 2t+8, 2t+9} carry inputs 16q+4t+{0,1,2,3}, the same
 // permutation on A and B, so the dot product is unchanged, and both the
 // codebook entry (A) and the activation quad (B) are single 8-byte loads.
-#include "common.cuh"
+#include <algorithm>
+
+#include "layout.cuh"
+#include "stages.cuh"
 
 namespace vqmoe {
 
-constexpr int kThreads = 256;          // 8 warps
+constexpr int kThreads = 256;               // 8 warps per CTA, 2 CTAs per SM
 constexpr int kWarps = kThreads / 32;
-constexpr int kTokBlk = 8;             // tokens per pass (MMA N)
-constexpr int kRepBytes = 256 * 16 * 8;  // replicated codebook, 32 KB
+constexpr int kRepBytes = 256 * 256;        // replicated codebooks (both matrices), 64 KB
+constexpr int kWin = 2048;                  // inputs per staged activation window
+constexpr int kXStride = kWin * 2 + 32;     // bytes per staged row: B-fragment
+                                            // loads of 4 rows hit 16 bank pairs
+constexpr int kXBytes = 8 * kXStride;       // 8 token rows
 
 struct LinearDev {
-    const uint8_t *codes;      // VQ device layout [E][OUT][IN/4]
+    const uint8_t *codes;      // VQ device layout (layout.cuh)
     const uint16_t *codebook;  // [K][4] fp16 bits
-    const uint16_t *scales;    // [E][OUT][IN/64] fp16 bits
+    const uint16_t *scales;    // VQ device layout (layout.cuh), fp16 bits
     const uint16_t *weight;    // dense [E][OUT][IN] bf16 bits
     int K;
 };
 
-struct ExpertArgs {
-    const int32_t *inds;  // [P] expert of each pair; nullptr: every row is a
-                          // pair of expert 0 (the shared expert)
-    int P;                // pairs (routed) or rows (identity)
-    int k;                // slots per token
-    int E;                // experts
-    const uint16_t *x;    // bf16 input rows
-    int x_per_pair;       // 1: x row = pair; 0: x row = pair / k
-    LinearDev w0, w1;     // w1 only for the fused gate/up (DUAL) kernel
+struct RoutedSet {
+    const int32_t *cnt, *off, *list, *active;  // routing; active[E] = #active
+    int E, k, x_per_pair, P;
+    const uint16_t *x;           // input rows: fp16 (VQ) or bf16 (dense)
+    LinearDev w0, w1;            // w1: up_proj of the fused gate/up stage
     int IN, OUT;
-    uint16_t *out;        // bf16 [P][OUT]
-    const float *pair_scale;  // optional [P]: out = bf16(bf16(acc) * s)
-    int ks;               // K split across warps (1, 2, 4)
-    int rows_per_tile;    // 32 * (kWarps / ks)
-    int row_blocks;
-    int ntiles;
-    int list_cap;
-    int xs_stride;        // bytes per staged token row
-    int xs_bytes;         // max(staging, reduction) bytes
+    uint16_t *out;               // [P][OUT]
+    int out_f16;                 // 1: fp16 (saturated) output, 0: bf16
+    const float *pair_scale;     // optional [P]: y = bf16(bf16(acc) * s)
 };
 
-template <int FMT, bool DUAL>
-__global__ void __launch_bounds__(kThreads, 2) expert_kernel(const ExpertArgs a) {
-    constexpr int NMAT = DUAL ? 2 : 1;
-    constexpr bool VQ = FMT == VQMOE_FMT_VQ_U8;
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_cnt[kWarps];
-    uint8_t *cbrep = smem;
-    int32_t *s_list = reinterpret_cast<int32_t *>(smem + (VQ ? NMAT * kRepBytes : 0));
-    uint8_t *xs = reinterpret_cast<uint8_t *>(s_list + a.list_cap);
-    float *red = reinterpret_cast<float *>(xs);
+struct SharedSet {
+    int present;
+    const uint16_t *x;           // [T][IN] bf16
+    const uint16_t *w0, *w1;     // [OUT][IN] bf16
+    int T, IN, OUT;
+    uint16_t *out;               // [T][OUT] bf16
+};
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int kq = warp % a.ks, rq = warp / a.ks;
-    const int IN = a.IN, OUT = a.OUT, S = a.xs_stride;
-    const int C = (IN + 255) / 256;
+struct TileArgs {
+    RoutedSet r;
+    SharedSet s;
+    uint32_t *work;              // tile counter (zeroed by the route kernel)
+};
 
-    if (VQ) {
-        // 16 interleaved copies: entry c of copy b at byte c*128 + b*8
-        for (int i = tid; i < NMAT * 256 * 16; i += kThreads) {
-            int m = i / 4096, r = i - m * 4096, c = r >> 4, b = r & 15;
-            const LinearDev &w = m == 0 ? a.w0 : a.w1;
-            uint2 v = make_uint2(0, 0);
-            if (c < w.K) v = *reinterpret_cast<const uint2 *>(w.codebook + c * 4);
-            *reinterpret_cast<uint2 *>(cbrep + m * kRepBytes + c * 128 + b * 8) = v;
+template <bool DUAL>
+__device__ __forceinline__ uint16_t epilogue_value(float g, float u, const float *pair_scale,
+                                                   int pair, int out_f16) {
+    float v;
+    if (DUAL) {
+        // _SwiGLU (qwen3_5.py:108-112): bf16(bf16(silu(g)) * u), g and u the
+        // bf16 outputs of the gate and up matmuls
+        v = bf16r(bf16r(silu_f32(bf16r(g))) * bf16r(u));
+    } else {
+        v = bf16r(g);
+        if (pair_scale) v = bf16r(v * pair_scale[pair]);
+    }
+    if (out_f16) return bf16_to_f16_sat(f32_to_bf16(v));
+    return f32_to_bf16(v);
+}
+
+__device__ __forceinline__ uint2 lds2(const uint8_t *base, uint32_t off) {
+    return *reinterpret_cast<const uint2 *>(base + off);
+}
+
+// half2 of fp16 lane `hi` of a packed pair, in both halves
+__device__ __forceinline__ uint32_t bcast_half(uint32_t v, int hi) {
+    return hi ? __byte_perm(v, 0, 0x3232) : __byte_perm(v, 0, 0x1010);
+}
+
+// Codes and scales of one half chunk (8 MMA sub-steps = 128 inputs) of the
+// warp's MT m-tiles: per (matrix, m-tile, row half) 2 code words, 2 scales.
+template <int NMAT, int MT>
+struct HalfBuf {
+    uint32_t cw[NMAT][MT][2][2];   // [m][mt][h][word]
+    uint32_t sc[NMAT][MT][2];      // [m][mt][h]: scale groups 2*half, 2*half+1
+};
+
+// ct[m]: the warp's first code tile + lane*8 (+ its m-tile's offset);
+// st[m]: first scale tile + 2*g. Chunks are 2048 / 128 elements apart.
+template <int NMAT, int MT>
+__device__ __forceinline__ void load_half(HalfBuf<NMAT, MT> &b, const uint8_t *const (&ct)[NMAT],
+                                          const uint16_t *const (&st)[NMAT], int hidx) {
+    const int c = hidx >> 1, half = hidx & 1;
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint2 v = ldg_stream_v2(ct[m] + c * 2048 + half * 1024 + (2 * mt + h) * 256);
+                b.cw[m][mt][h][0] = v.x;
+                b.cw[m][mt][h][1] = v.y;
+                b.sc[m][mt][h] = ldg_stream_u32(st[m] + c * 128 + half * 64 + (2 * mt + h) * 16);
+            }
+}
+
+// 8 sub-steps from a half buffer; xoff: this lane's staged-row offset of
+// sub-step 0; lanebyte: this lane's codebook copy offset (lane % 16) * 8.
+template <int NMAT, int MT>
+__device__ __forceinline__ void compute_half(const HalfBuf<NMAT, MT> &b, float (&acc)[NMAT][MT][4],
+                                             const uint8_t *cb, uint32_t lanebyte,
+                                             const uint8_t *xs, int xoff) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {          // the half's two scale groups
+        uint32_t s2[NMAT][MT][2];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) s2[m][mt][h] = bcast_half(b.sc[m][mt][h], j);
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+            const int q = 4 * j + qq;
+            // address = 256 * code + 8 * copy: code byte qq -> byte 1
+            const uint32_t sel = 0x5504u | (qq << 4);
+            const uint2 bf = lds2(xs, xoff + q * 32);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    const uint32_t a0 = __byte_perm(b.cw[m][mt][0][j], lanebyte, sel);
+                    const uint32_t a1 = __byte_perm(b.cw[m][mt][1][j], lanebyte, sel);
+                    const uint2 e0 = lds2(cb + m * 128, a0);
+                    const uint2 e1 = lds2(cb + m * 128, a1);
+                    const uint32_t s0 = s2[m][mt][0], s1 = s2[m][mt][1];
+                    mma_f16(acc[m][mt], hmul2_u32(e0.x, s0), hmul2_u32(e1.x, s1),
+                            hmul2_u32(e0.y, s0), hmul2_u32(e1.y, s1), bf.x, bf.y);
+                }
+            }
         }
     }
-    const uint32_t cb_s = smem_u32(cbrep) + (lane & 15) * 8;
-    const uint32_t xs_s = smem_u32(xs);
+}
 
-    for (int tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
-        const int e = tile / a.row_blocks, rb = tile - e * a.row_blocks;
-        int cursor = 0;  // next pair id to scan
-      for (;;) {
-        // ---- the next (at most list_cap) pairs of expert e, ascending pair
-        // id (a stable sort by expert); a scan step adds <= kThreads entries
-        // and only runs while they fit, so s_list never overflows
-        int n = 0;
-        if (a.inds) {
-            while (cursor < a.P && n + kThreads <= a.list_cap) {
-                int p = cursor + tid;
-                bool hit = p < a.P && a.inds[p] == e;
-                unsigned bal = __ballot_sync(0xffffffffu, hit);
-                if (lane == 0) s_cnt[warp] = __popc(bal);
-                __syncthreads();
-                int off = n, tot = 0;
+// Dense sub-steps [q0, q1) of chunk c (A from global: rows r0 and r0 + 8).
+template <int NMAT, int MT>
+__device__ __forceinline__ void dense_chunk(float (&acc)[NMAT][MT][4], const uint16_t *const (&wr)[NMAT],
+                                            int IN, int c, int nq, const uint8_t *xs, int xoff) {
+#pragma unroll 4
+    for (int q = 0; q < nq; ++q) {
+        const uint2 bf = lds2(xs, xoff + q * 32);
 #pragma unroll
-                for (int w = 0; w < kWarps; ++w) {
-                    int c = s_cnt[w];
-                    off += w < warp ? c : 0;
-                    tot += c;
-                }
-                if (hit) s_list[off + __popc(bal & ((1u << lane) - 1u))] = p;
-                n += tot;
-                cursor += kThreads;
-                __syncthreads();
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const uint16_t *wp = wr[m] + (size_t)mt * 16 * IN + (c << 8) + 16 * q;
+                const uint2 w0v = ldg_nc_v2(wp);
+                const uint2 w1v = ldg_nc_v2(wp + (size_t)8 * IN);
+                mma_bf16(acc[m][mt], w0v.x, w1v.x, w0v.y, w1v.y, bf.x, bf.y);
+            }
+    }
+}
+
+struct TileInfo {
+    int kind;       // 0 routed, 1 shared
+    int e, n, base; // routed: expert, its pair count, list offset
+    int row0;       // first output row of the tile
+};
+
+// ----------------------------------------------------------------- kernel
+// NMAT: 2 = fused gate/up + SwiGLU, 1 = down. MT: m-tiles (16 rows) per warp.
+template <int NMAT, int MT, bool VQ>
+__global__ void __launch_bounds__(kThreads, 2) expert_tile_kernel(const TileArgs a) {
+    constexpr bool DUAL = NMAT == 2;
+    constexpr int TR = kWarps * 16 * MT;          // output rows per tile
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ TileInfo s_info;
+    __shared__ int s_next;
+    __shared__ int s_pairs[8];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    uint8_t *cb = smem;
+    uint8_t *xs = smem + (VQ ? kRepBytes : 0);
+    if (VQ) {
+        // 16 interleaved copies: entry c of copy b of matrix m at 256c + 128m + 8b
+        for (int i = tid; i < NMAT * 256 * 16; i += kThreads) {
+            const int m = i >> 12, rr = i & 4095, c = rr >> 4, b = rr & 15;
+            const LinearDev &w = m == 0 ? a.r.w0 : a.r.w1;
+            uint2 v = make_uint2(0, 0);
+            if (c < w.K) v = *reinterpret_cast<const uint2 *>(w.codebook + c * 4);
+            *reinterpret_cast<uint2 *>(smem + c * 256 + m * 128 + b * 8) = v;
+        }
+    }
+    const uint32_t lanebyte = (lane & 15) * 8;
+    const int rt_r = (a.r.OUT + TR - 1) / TR;     // tiles per routed expert
+    const int n_shared = 0;   // the shared expert runs in shared_dense_kernel
+    const int n_routed = a.r.active ? a.r.active[a.r.E] * rt_r : 0;
+    if (tid == 0) s_next = (int)atomicAdd(a.work, 1u);
+    __syncthreads();
+    for (;;) {
+        const int tile = s_next;
+        if (tile >= n_shared + n_routed) break;
+        __syncthreads();                          // everyone has read s_next
+        if (tid == 0) {
+            TileInfo in;
+            if (tile < n_shared) {
+                in.kind = 1;
+                in.e = 0;
+                in.n = a.s.T;
+                in.base = 0;
+                in.row0 = tile * TR;
+            } else {
+                const int u = tile - n_shared;
+                const int ai = u / rt_r;
+                in.kind = 0;
+                in.e = a.r.active[ai];
+                in.n = a.r.cnt[in.e];
+                in.base = a.r.off[in.e];
+                in.row0 = (u - ai * rt_r) * TR;
+            }
+            s_info = in;
+            s_next = (int)atomicAdd(a.work, 1u);  // the next tile, read after this one
+        }
+        __syncthreads();
+        const TileInfo in = s_info;
+        const bool shared = false;
+        const int IN = shared ? a.s.IN : a.r.IN, OUT = shared ? a.s.OUT : a.r.OUT;
+        const int C = (IN + 255) >> 8;
+        const int wrow = in.row0 + warp * 16 * MT;   // this warp's first row
+        const bool active = wrow < OUT;
+        // VQ codes / scales of this warp's rows: 32-row block rb, m-tile offset
+        // every pointer starts at a valid base, whichever branch sets it
+        const uint8_t *ct[NMAT];
+        const uint16_t *st[NMAT];
+        const uint16_t *wr[NMAT];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            ct[m] = VQ ? a.r.w0.codes : nullptr;
+            st[m] = VQ ? a.r.w0.scales : nullptr;
+            wr[m] = a.s.present ? a.s.w0 : a.r.w0.weight;
+        }
+        if (VQ && !shared) {
+            const long long tile0 = ((long long)in.e * ((OUT + 31) >> 5) + (wrow >> 5)) * C;
+            const int mt0 = (wrow >> 4) & 1;      // MT == 1: which half of the 32 rows
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const LinearDev &w = m == 0 ? a.r.w0 : a.r.w1;
+                ct[m] = w.codes + tile0 * 2048 + mt0 * 512 + lane * 8;
+                st[m] = w.scales + tile0 * 128 + mt0 * 32 + 2 * g;
             }
         } else {
-            n = a.P;       // identity routing: pairs 0 .. P-1, no list
-            cursor = a.P;
-        }
-        if (n == 0) break;
-        const int row_base = rb * a.rows_per_tile + rq * 32;
-        const bool mt_ok0 = row_base < OUT, mt_ok1 = row_base + 16 < OUT;
-
-        for (int tb0 = 0; tb0 < n; tb0 += kTokBlk) {
-            const int nt = min(kTokBlk, n - tb0);
-            __syncthreads();  // previous pass's epilogue is done with xs / red
-            // ---- stage up to 8 input rows (fp16 for VQ, bf16 for dense)
-            {
-                const int vpr = IN / 8;
-                for (int v = tid; v < kTokBlk * vpr; v += kThreads) {
-                    int r = v / vpr, c8 = v - r * vpr;
-                    uint4 val = make_uint4(0, 0, 0, 0);
-                    if (r < nt) {
-                        int pair = a.inds ? s_list[tb0 + r] : tb0 + r;
-                        int xr = a.x_per_pair ? pair : pair / a.k;
-                        val = *reinterpret_cast<const uint4 *>(a.x + (size_t)xr * IN + c8 * 8);
-                        if (VQ) {
-                            uint32_t u[4] = {val.x, val.y, val.z, val.w};
 #pragma unroll
-                            for (int j = 0; j < 4; ++j)
-                                u[j] = (uint32_t)bf16_to_f16_sat(u[j] & 0xFFFFu) |
-                                       ((uint32_t)bf16_to_f16_sat(u[j] >> 16) << 16);
-                            val = make_uint4(u[0], u[1], u[2], u[3]);
-                        }
-                    }
-                    *reinterpret_cast<uint4 *>(xs + r * S + c8 * 16) = val;
-                }
+            for (int m = 0; m < NMAT; ++m) {
+                const uint16_t *base = shared ? (m == 0 ? a.s.w0 : a.s.w1)
+                                              : (m == 0 ? a.r.w0.weight : a.r.w1.weight) +
+                                                    (size_t)in.e * OUT * IN;
+                wr[m] = base + (size_t)(wrow + g) * IN + 4 * t;
             }
-            __syncthreads();
-
-            float acc[NMAT][2][4];
+        }
+        for (int tb0 = 0; tb0 < in.n; tb0 += 8) {
+            const int nt = min(8, in.n - tb0);
+            __syncthreads();                      // the previous block's epilogue read s_pairs
+            if (tid < 8) s_pairs[tid] = tid < nt ? (shared ? tb0 + tid : a.r.list[in.base + tb0 + tid]) : -1;
+            float acc[NMAT][MT][4];
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-                for (int mt = 0; mt < 2; ++mt)
+                for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) acc[m][mt][i] = 0.0f;
-
-            if (mt_ok0) {
-                for (int c = kq; c < C; c += a.ks) {
-                    const int feat0 = c * 256;
-                    const int nq = min(16, (IN - feat0) >> 4);
-                    const uint32_t xb = xs_s + g * S + (feat0 + 4 * t) * 2;
-                    if (VQ) {
-                        uint32_t cw[NMAT][2][2][4];
-                        uint32_t sc[NMAT][2][2][4];
-#pragma unroll
-                        for (int m = 0; m < NMAT; ++m) {
-                            const LinearDev &w = m == 0 ? a.w0 : a.w1;
-#pragma unroll
-                            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-                                for (int h = 0; h < 2; ++h) {
-                                    const int row = row_base + mt * 16 + h * 8 + g;
-                                    const bool ok = mt == 0 || mt_ok1;
-                                    const size_t rix = (size_t)e * OUT + row;
-                                    const uint8_t *cp = w.codes + rix * (IN / 4) + c * 64 + t * nq;
-                                    const uint16_t *sp = w.scales + rix * (IN / 64) + c * 4;
-                                    if (ok && nq == 16) {
-                                        uint4 v = ldg_stream_v4(cp);
-                                        cw[m][mt][h][0] = v.x;
-                                        cw[m][mt][h][1] = v.y;
-                                        cw[m][mt][h][2] = v.z;
-                                        cw[m][mt][h][3] = v.w;
-                                    } else {
-#pragma unroll
-                                        for (int j = 0; j < 4; ++j)
-                                            cw[m][mt][h][j] = (ok && 4 * j < nq) ? ldg_stream_u32(cp + 4 * j) : 0u;
-                                    }
-#pragma unroll
-                                    for (int j = 0; j < 4; ++j) {
-                                        uint32_t s = (ok && 4 * j < nq) ? ldg_nc_u16(sp + j) : 0u;
-                                        sc[m][mt][h][j] = s | (s << 16);
-                                    }
-                                }
+            HalfBuf<NMAT, MT> hb[4];
+            const int nh = 2 * C;
+            if (VQ && !shared && active) {
+                load_half<NMAT, MT>(hb[0], ct, st, 0);
+                if (nh > 1) load_half<NMAT, MT>(hb[1], ct, st, 1);
+                if (nh > 2) load_half<NMAT, MT>(hb[2], ct, st, 2);
+            }
+            for (int w0 = 0; w0 < (VQ && !shared ? C << 8 : IN); w0 += kWin) {
+                const int wend = min(w0 + kWin, VQ && !shared ? C << 8 : IN);
+                __syncthreads();                  // previous window fully read; s_pairs written
+                {
+                    // stage rows 0..7 (zero past nt and past IN), 16 bytes per copy
+                    const int nv = (wend - w0) >> 3;
+                    for (int v = tid; v < 8 * nv; v += kThreads) {
+                        const int r = v / nv, j = v - r * nv;
+                        const int f = w0 + 8 * j;
+                        const int p = s_pairs[r];
+                        const uint16_t *src;
+                        bool ok = p >= 0 && f < IN;
+                        if (shared) {
+                            src = a.s.x + (size_t)(ok ? p : 0) * IN + f;
+                        } else {
+                            const int xr = p < 0 ? 0 : (a.r.x_per_pair ? p : p / a.r.k);
+                            src = a.r.x + (size_t)xr * IN + (ok ? f : 0);
                         }
-#pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            if (q < nq) {
-                                const int j = q >> 2, sh = (q & 3) * 8;
-                                const uint2 bf = lds_v2(xb + q * 32);
-#pragma unroll
-                                for (int m = 0; m < NMAT; ++m) {
-                                    const uint32_t cbm = cb_s + m * kRepBytes;
-#pragma unroll
-                                    for (int mt = 0; mt < 2; ++mt) {
-                                        if (mt == 0 || mt_ok1) {
-                                            const uint32_t c0 = (cw[m][mt][0][j] >> sh) & 0xFFu;
-                                            const uint32_t c1 = (cw[m][mt][1][j] >> sh) & 0xFFu;
-                                            const uint2 e0 = lds_v2(cbm + c0 * 128);
-                                            const uint2 e1 = lds_v2(cbm + c1 * 128);
-                                            const uint32_t s0 = sc[m][mt][0][j], s1 = sc[m][mt][1][j];
-                                            mma_f16(acc[m][mt], hmul2_u32(e0.x, s0), hmul2_u32(e1.x, s1),
-                                                    hmul2_u32(e0.y, s0), hmul2_u32(e1.y, s1), bf.x, bf.y);
-                                        }
-                                    }
-                                }
-                            }
+                        cp_async16(smem_u32(xs + r * kXStride + j * 16), src, ok ? 16 : 0);
+                    }
+                    cp_async_wait_all();
+                }
+                __syncthreads();
+                if (!active) continue;
+                const int c0 = w0 >> 8, c1 = (wend + 255) >> 8;
+                if (VQ && !shared) {
+                    // chunks in pairs: halves 2c .. 2c+3 in hb[0..3]; the loads
+                    // run three halves ahead (a ring of four buffers)
+                    for (int c = c0; c < c1; c += 2) {
+                        const int h0 = 2 * c;
+                        const int xoff = g * kXStride + (((c - c0) << 8) + 4 * t) * 2;
+                        if (h0 + 3 < nh) load_half<NMAT, MT>(hb[3], ct, st, h0 + 3);
+                        compute_half<NMAT, MT>(hb[0], acc, cb, lanebyte, xs, xoff);
+                        if (h0 + 4 < nh) load_half<NMAT, MT>(hb[0], ct, st, h0 + 4);
+                        compute_half<NMAT, MT>(hb[1], acc, cb, lanebyte, xs, xoff + 256);
+                        if (h0 + 2 < nh) {
+                            if (h0 + 5 < nh) load_half<NMAT, MT>(hb[1], ct, st, h0 + 5);
+                            compute_half<NMAT, MT>(hb[2], acc, cb, lanebyte, xs, xoff + 512);
+                            if (h0 + 6 < nh) load_half<NMAT, MT>(hb[2], ct, st, h0 + 6);
+                            compute_half<NMAT, MT>(hb[3], acc, cb, lanebyte, xs, xoff + 768);
                         }
-                    } else {
-#pragma unroll 4
-                        for (int q = 0; q < nq; ++q) {
-                            const uint2 bf = lds_v2(xb + q * 32);
-#pragma unroll
-                            for (int m = 0; m < NMAT; ++m) {
-                                const LinearDev &w = m == 0 ? a.w0 : a.w1;
-#pragma unroll
-                                for (int mt = 0; mt < 2; ++mt) {
-                                    if (mt == 0 || mt_ok1) {
-                                        const size_t r0 = (size_t)e * OUT + row_base + mt * 16 + g;
-                                        const uint16_t *wp = w.weight + r0 * IN + feat0 + 16 * q + 4 * t;
-                                        const uint2 w0 = ldg_nc_v2(wp);
-                                        const uint2 w1 = ldg_nc_v2(wp + (size_t)8 * IN);
-                                        mma_bf16(acc[m][mt], w0.x, w1.x, w0.y, w1.y, bf.x, bf.y);
-                                    }
-                                }
-                            }
-                        }
+                    }
+                } else {
+                    for (int c = c0; c < c1; ++c) {
+                        const int nq = min(16, (IN - (c << 8)) >> 4);
+                        const int xoff = g * kXStride + (((c - c0) << 8) + 4 * t) * 2;
+                        dense_chunk<NMAT, MT>(acc, wr, IN, c, nq, xs, xoff);
                     }
                 }
             }
-            __syncthreads();  // all warps done reading xs: reuse it for partials
-            {
-                const int R = a.rows_per_tile;
+            // ---- results of tokens tb0 .. tb0+7 for this warp's rows
+            if (active) {
 #pragma unroll
-                for (int m = 0; m < NMAT; ++m)
+                for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                    for (int mt = 0; mt < 2; ++mt) {
-                        const int rl = rq * 32 + mt * 16 + g;
-                        float *base = red + ((size_t)(kq * NMAT + m) * R) * kTokBlk;
-                        base[rl * kTokBlk + 2 * t] = acc[m][mt][0];
-                        base[rl * kTokBlk + 2 * t + 1] = acc[m][mt][1];
-                        base[(rl + 8) * kTokBlk + 2 * t] = acc[m][mt][2];
-                        base[(rl + 8) * kTokBlk + 2 * t + 1] = acc[m][mt][3];
+                    for (int i = 0; i < 4; ++i) {
+                        const int tk = 2 * t + (i & 1);
+                        const int row = wrow + mt * 16 + g + (i >> 1) * 8;
+                        const int p = s_pairs[tk];
+                        if (p < 0 || row >= OUT) continue;
+                        if (shared)
+                            a.s.out[(size_t)p * OUT + row] =
+                                epilogue_value<DUAL>(acc[0][mt][i], acc[NMAT - 1][mt][i], nullptr, 0, 0);
+                        else
+                            a.r.out[(size_t)p * OUT + row] = epilogue_value<DUAL>(
+                                acc[0][mt][i], acc[NMAT - 1][mt][i], a.r.pair_scale, p, a.r.out_f16);
                     }
-            }
-            __syncthreads();
-            {
-                const int R = a.rows_per_tile;
-                for (int o = tid; o < R * kTokBlk; o += kThreads) {
-                    const int tok = o / R, rl = o - tok * R;
-                    const int row = rb * R + rl;
-                    if (tok >= nt || row >= OUT) continue;
-                    float s[NMAT];
-#pragma unroll
-                    for (int m = 0; m < NMAT; ++m) {
-                        float v = 0.0f;
-                        for (int q = 0; q < a.ks; ++q)
-                            v += red[((size_t)(q * NMAT + m) * R + rl) * kTokBlk + tok];
-                        s[m] = v;
-                    }
-                    const int pair = a.inds ? s_list[tb0 + tok] : tb0 + tok;
-                    uint16_t res;
-                    if (DUAL) {
-                        // _SwiGLU (qwen3_5.py:108-112): bf16(bf16(silu(g)) * u)
-                        const float gv = bf16r(s[0]), uv = bf16r(s[NMAT - 1]);
-                        res = f32_to_bf16(bf16r(silu_f32(gv)) * uv);
-                    } else {
-                        float y = bf16r(s[0]);
-                        if (a.pair_scale) y = y * a.pair_scale[pair];
-                        res = f32_to_bf16(y);
-                    }
-                    a.out[(size_t)pair * OUT + row] = res;
-                }
             }
         }
-        if (cursor >= a.P) break;
-      }
+        __syncthreads();                          // done with s_pairs / xs before the next tile
     }
+}
+
+// ------------------------------------------------------- shared expert
+// The shared expert's dense bf16 matmuls (qwen3_5.py:184-185) for up to 64
+// tokens per pass. A CTA owns 32 output rows and a K slice: it issues
+// cp.async for its whole weight slice and all token rows at once (the
+// weights are read exactly once, with the full slice in flight), then its 8
+// warps -- one per 8 tokens -- multiply from shared memory. K slices meet in
+// a float32 partial buffer; the last CTA of a row block to finish (one
+// atomic, no waiting) sums them in slice order and applies the epilogue.
+constexpr int kShRows = 32;
+constexpr int kShTok = 64;
+
+struct SharedArgs {
+    const uint16_t *x;           // [T][IN] bf16
+    const uint16_t *w0, *w1;     // [OUT][IN] bf16
+    int T, IN, OUT, ks, kslice;  // K slices of kslice inputs (multiple of 16)
+    uint16_t *out;               // [T][OUT] bf16
+    float *part;                 // [ks][T][NMAT][OUT] (ks > 1)
+    uint32_t *sem;               // [OUT / 32]
+};
+
+template <int NMAT>
+__global__ void __launch_bounds__(256) shared_dense_kernel(const SharedArgs a) {
+    constexpr bool DUAL = NMAT == 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint32_t s_old;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int rb = blockIdx.x, ksi = blockIdx.y;
+    const int row0 = rb * kShRows;
+    const int k0 = ksi * a.kslice, kl = min(a.kslice, a.IN - k0);
+    const int stride = a.kslice * 2 + 32;            // bytes per staged row
+    uint8_t *wa = smem;                              // [NMAT][32][stride]
+    uint8_t *xb = smem + NMAT * kShRows * stride;    // [64][stride]
+    for (int tp0 = 0; tp0 < a.T; tp0 += kShTok) {
+        const int nt = min(kShTok, a.T - tp0);
+        __syncthreads();
+        const int nv = kl >> 3;
+        for (int v = tid; v < (NMAT * kShRows + kShTok) * nv; v += blockDim.x) {
+            const int r = v / nv, j = v - r * nv;
+            if (r < NMAT * kShRows) {
+                const int m = r / kShRows, rr = r - m * kShRows;
+                const bool ok = row0 + rr < a.OUT;
+                const uint16_t *src = (m == 0 ? a.w0 : a.w1) + (size_t)(ok ? row0 + rr : 0) * a.IN + k0 + 8 * j;
+                cp_async16(smem_u32(wa + r * stride + j * 16), src, ok ? 16 : 0);
+            } else {
+                const int tk = r - NMAT * kShRows;
+                const bool ok = tk < nt;
+                const uint16_t *src = a.x + (size_t)(ok ? tp0 + tk : 0) * a.IN + k0 + 8 * j;
+                cp_async16(smem_u32(xb + tk * stride + j * 16), src, ok ? 16 : 0);
+            }
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        float acc[NMAT][2][4];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[m][mt][i] = 0.0f;
+        const uint8_t *xw = xb + (warp * 8 + g) * stride + 8 * t;
+#pragma unroll 4
+        for (int q = 0; q < (kl >> 4); ++q) {
+            const uint2 bf = *reinterpret_cast<const uint2 *>(xw + q * 32);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    const uint8_t *ar = wa + (m * kShRows + mt * 16 + g) * stride + 8 * t + q * 32;
+                    const uint2 a0 = *reinterpret_cast<const uint2 *>(ar);
+                    const uint2 a1 = *reinterpret_cast<const uint2 *>(ar + 8 * stride);
+                    mma_bf16(acc[m][mt], a0.x, a1.x, a0.y, a1.y, bf.x, bf.y);
+                }
+        }
+        // fragment -> (token tp0 + 8*warp + 2t + (i&1), row row0 + 16mt + g + 8*(i>>1))
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int tok = tp0 + warp * 8 + 2 * t + (i & 1);
+                const int row = row0 + mt * 16 + g + (i >> 1) * 8;
+                if (tok >= a.T || row >= a.OUT) continue;
+                if (a.ks == 1) {
+                    a.out[(size_t)tok * a.OUT + row] =
+                        epilogue_value<DUAL>(acc[0][mt][i], acc[NMAT - 1][mt][i], nullptr, 0, 0);
+                } else {
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m)
+                        a.part[(((size_t)ksi * a.T + tok) * NMAT + m) * a.OUT + row] = acc[m][mt][i];
+                }
+            }
+    }
+    if (a.ks == 1) return;
+    // the last K slice of this row block sums the slices in slice order
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_old = atomicAdd(&a.sem[rb], 1u);
+    __syncthreads();
+    if (s_old != (uint32_t)(a.ks - 1)) return;
+    if (tid == 0) a.sem[rb] = 0u;
+    __threadfence();
+    for (int o = tid; o < a.T * kShRows; o += blockDim.x) {
+        const int tok = o / kShRows, row = row0 + (o - tok * kShRows);
+        if (row >= a.OUT) continue;
+        float v[NMAT];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            float sum = 0.0f;
+            for (int q = 0; q < a.ks; ++q) sum += __ldcg(&a.part[(((size_t)q * a.T + tok) * NMAT + m) * a.OUT + row]);
+            v[m] = sum;
+        }
+        a.out[(size_t)tok * a.OUT + row] = epilogue_value<DUAL>(v[0], v[NMAT - 1], nullptr, 0, 0);
+    }
+}
+
+// K slicing of the shared expert: slices of <= 512 inputs (a multiple of 16)
+// so that the grid covers the GPU; plus the shared memory it needs.
+void plan_shared_dense(int IN, int OUT, int nmat, int *ks, int *kslice, size_t *smem) {
+    const int rbs = (OUT + kShRows - 1) / kShRows;
+    int want = std::max(1, (int)((2LL * sm_count() + rbs - 1) / rbs));
+    int kl = std::max(16, (IN + want - 1) / want);
+    kl = std::min(512, (kl + 15) / 16 * 16);
+    *kslice = kl;
+    *ks = (IN + kl - 1) / kl;
+    *smem = (size_t)(nmat * kShRows + kShTok) * (kl * 2 + 32);
+}
+
+vqmoe_status launch_shared_dense(const void *x, const void *w0, const void *w1, int T, int IN, int OUT,
+                                 void *out, float *part, uint32_t *sem, cudaStream_t stream) {
+    const int nmat = w1 ? 2 : 1;
+    int ks = 1, kl = IN;
+    size_t smem = 0;
+    plan_shared_dense(IN, OUT, nmat, &ks, &kl, &smem);
+    SharedArgs a{};
+    a.x = static_cast<const uint16_t *>(x);
+    a.w0 = static_cast<const uint16_t *>(w0);
+    a.w1 = static_cast<const uint16_t *>(w1 ? w1 : w0);
+    a.T = T;
+    a.IN = IN;
+    a.OUT = OUT;
+    a.ks = ks;
+    a.kslice = kl;
+    a.out = static_cast<uint16_t *>(out);
+    a.part = part;
+    a.sem = sem;
+    dim3 grid((OUT + kShRows - 1) / kShRows, ks);
+    static size_t configured[2][64] = {{0}};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto fn = nmat == 2 ? shared_dense_kernel<2> : shared_dense_kernel<1>;
+    if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || smem > configured[nmat - 1][dev])) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return set_error(VQMOE_LAUNCH_FAILED, "shared expert kernel: %zu bytes of shared memory", smem);
+        if (dev >= 0 && dev < 64) configured[nmat - 1][dev] = smem;
+    }
+    fn<<<grid, 256, smem, stream>>>(a);
+    return check_launch("shared_dense_kernel");
 }
 
 // ------------------------------------------------------------------ host
 
-template <int FMT, bool DUAL>
-static vqmoe_status launch_one(const ExpertArgs &a, size_t smem, int grid,
-                               cudaStream_t stream) {
+template <int NMAT, int MT, bool VQ>
+static vqmoe_status launch_tiles(const TileArgs &a, size_t smem, cudaStream_t stream) {
     static size_t configured[64] = {0};   // per device
     int dev = 0;
     cudaGetDevice(&dev);
-    auto fn = expert_kernel<FMT, DUAL>;
-    if (dev < 0 || dev >= 64 || smem > configured[dev]) {
-        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem) != cudaSuccess)
+    auto fn = expert_tile_kernel<NMAT, MT, VQ>;
+    if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || smem > configured[dev])) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
             return set_error(VQMOE_LAUNCH_FAILED, "expert kernel: %zu bytes of shared memory", smem);
         if (dev >= 0 && dev < 64) configured[dev] = smem;
     }
-    fn<<<grid, kThreads, smem, stream>>>(a);
-    return check_launch("expert_kernel");
+    fn<<<2 * sm_count(), kThreads, smem, stream>>>(a);
+    return check_launch("expert_tile_kernel");
 }
 
-static int pick_ks(int chunks) {
-    if (chunks % 4 == 0) return 4;
-    if (chunks % 2 == 0) return 2;
-    return 1;
+static LinearDev dev_of(const vqmoe_linear *w) {
+    LinearDev d{};
+    d.codes = static_cast<const uint8_t *>(w->codes);
+    d.codebook = static_cast<const uint16_t *>(w->codebook);
+    d.scales = static_cast<const uint16_t *>(w->scales);
+    d.weight = static_cast<const uint16_t *>(w->weight);
+    d.K = w->codebook_size;
+    return d;
 }
 
-// Shared by vqmoe_switch_linear / switch_glu / sparse_moe_block.
-// inds == nullptr: identity routing (rows 0..P-1 all use expert 0).
-vqmoe_status launch_expert(const vqmoe_linear *w0, const vqmoe_linear *w1,
-                           const int32_t *inds, int P, int k, const void *x,
-                           int x_per_pair, void *out, const float *pair_scale,
-                           int list_cap, cudaStream_t stream) {
+void plan_routed(int, int, int, int, int *ks, int *rb) {
+    *ks = 1;
+    *rb = 0;
+}
+
+void plan_shared(int, int, int *ks, int *rb) {
+    *ks = 1;
+    *rb = 0;
+}
+
+vqmoe_status launch_expert_stage(const vqmoe_linear *w0, const vqmoe_linear *w1, const RoutedIO *r,
+                                 const SharedIO *s, uint32_t *work, cudaStream_t stream) {
     const bool dual = w1 != nullptr;
-    ExpertArgs a{};
-    a.inds = inds;
-    a.P = P;
-    a.k = k;
-    a.E = inds ? w0->num_experts : 1;
-    a.x = static_cast<const uint16_t *>(x);
-    a.x_per_pair = x_per_pair;
-    a.IN = w0->in_features;
-    a.OUT = w0->out_features;
-    auto dev = [](const vqmoe_linear *w) {
-        LinearDev d{};
-        d.codes = static_cast<const uint8_t *>(w->codes);
-        d.codebook = static_cast<const uint16_t *>(w->codebook);
-        d.scales = static_cast<const uint16_t *>(w->scales);
-        d.weight = static_cast<const uint16_t *>(w->weight);
-        d.K = w->codebook_size;
-        return d;
-    };
-    a.w0 = dev(w0);
-    a.w1 = dual ? dev(w1) : a.w0;
-    a.out = static_cast<uint16_t *>(out);
-    a.pair_scale = pair_scale;
-    const int chunks = (a.IN + 255) / 256;
-    a.ks = pick_ks(chunks);
-    a.rows_per_tile = 32 * (kWarps / a.ks);
-    a.row_blocks = (a.OUT + a.rows_per_tile - 1) / a.rows_per_tile;
-    a.ntiles = a.E * a.row_blocks;
-    // pair-list capacity: >= one scan step (kThreads); more only saves re-scans
-    a.list_cap = inds ? (int)std::min<size_t>(2048, std::max<size_t>(kThreads, align_up((size_t)list_cap, 32))) : 0;
-    a.xs_stride = (int)align_up((size_t)a.IN * 2, 128) + 32;
-    const int nmat = dual ? 2 : 1;
-    const size_t stage = (size_t)kTokBlk * a.xs_stride;
-    const size_t redb = (size_t)a.ks * nmat * a.rows_per_tile * kTokBlk * sizeof(float);
-    a.xs_bytes = (int)std::max(stage, redb);
-    const bool vq = w0->format == VQMOE_FMT_VQ_U8;
-    const size_t smem = (vq ? nmat * (size_t)kRepBytes : 0) + (size_t)a.list_cap * 4 + a.xs_bytes;
-    if (smem > 227 * 1024)
-        return set_error(VQMOE_BAD_SHAPE, "expert kernel needs %zu bytes of shared memory", smem);
-    const int grid = std::min(a.ntiles, 2 * sm_count());
-    if (vq)
-        return dual ? launch_one<VQMOE_FMT_VQ_U8, true>(a, smem, grid, stream)
-                    : launch_one<VQMOE_FMT_VQ_U8, false>(a, smem, grid, stream);
-    return dual ? launch_one<VQMOE_FMT_DENSE_BF16, true>(a, smem, grid, stream)
-                : launch_one<VQMOE_FMT_DENSE_BF16, false>(a, smem, grid, stream);
+    TileArgs a{};
+    a.work = work;
+    if (r) {
+        a.r.cnt = r->cnt;
+        a.r.off = r->off;
+        a.r.list = r->list;
+        a.r.active = r->active;
+        a.r.E = r->E;
+        a.r.k = r->k;
+        a.r.P = r->P;
+        a.r.x_per_pair = r->x_per_pair;
+        a.r.x = static_cast<const uint16_t *>(r->x);
+        a.r.w0 = dev_of(w0);
+        a.r.w1 = dual ? dev_of(w1) : a.r.w0;
+        a.r.IN = w0->in_features;
+        a.r.OUT = w0->out_features;
+        a.r.out = static_cast<uint16_t *>(r->out);
+        a.r.out_f16 = r->out_f16;
+        a.r.pair_scale = r->pair_scale;
+    }
+    if (s) {
+        a.s.present = 1;
+        a.s.x = static_cast<const uint16_t *>(s->x);
+        a.s.w0 = static_cast<const uint16_t *>(s->w0);
+        a.s.w1 = static_cast<const uint16_t *>(dual ? s->w1 : s->w0);
+        a.s.T = s->T;
+        a.s.IN = s->IN;
+        a.s.OUT = s->OUT;
+        a.s.out = static_cast<uint16_t *>(s->out);
+    }
+    const bool vq = r && w0->format == VQMOE_FMT_VQ_U8;
+    const size_t smem = (vq ? (size_t)kRepBytes : 0) + (size_t)kXBytes;
+    if (dual)
+        return vq ? launch_tiles<2, 1, true>(a, smem, stream) : launch_tiles<2, 1, false>(a, smem, stream);
+    return vq ? launch_tiles<1, 2, true>(a, smem, stream) : launch_tiles<1, 2, false>(a, smem, stream);
 }
 
 }  // namespace vqmoe

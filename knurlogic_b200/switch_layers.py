@@ -97,8 +97,11 @@ class _SwitchBase(nn.Module):
         ii = _contig(indices.reshape(-1).to(torch.int32))
         y = torch.empty((P, self.output_dims), dtype=torch.bfloat16, device=x.device)
         d = self.descriptor()
+        n = _lib.lib().vqmoe_switch_linear_workspace_size(ctypes_ref(d), tokens, k, per_pair)
+        ws = torch.empty(n, dtype=torch.uint8, device=x.device)
         _lib.call("vqmoe_switch_linear", ctypes_ref(d), xi.data_ptr(),
-                  per_pair, ii.data_ptr(), tokens, k, y.data_ptr(), _stream(x))
+                  per_pair, ii.data_ptr(), tokens, k, y.data_ptr(), ws.data_ptr(), n,
+                  _stream(x))
         return y.reshape(*B, 1, self.output_dims)
 
 
@@ -147,8 +150,8 @@ class VQSwitchLinear(_SwitchBase):
         W = fp16(codebook[codes[e, o, i // dim], i % dim] * vq_scales[e, o, i // group])
     and the activations enter the matmul as fp16.
 
-    `codes` stays in the reference layout; the kernels read a permuted copy
-    (`vqmoe_prepare_codes`) made on the module's device at first use.
+    `codes` and `vq_scales` stay in the reference layout; the kernels read a
+    tiled copy (`vqmoe_prepare_vq`) made on the module's device at first use.
     Packed codes (`pack_bits` > 0, uint32 words of ceil(log2 K)-bit fields)
     are rejected: their bit order is not pinned by the reference."""
 
@@ -199,37 +202,43 @@ class VQSwitchLinear(_SwitchBase):
     def input_dims(self):
         return self.codes.shape[2] * self.codebook.shape[1]
 
-    def prepared_codes(self) -> torch.Tensor:
-        """The device-layout copy of `codes` (made once per device)."""
-        c = self.codes
-        require_cuda(c)
-        key = (c.device, c.data_ptr(), c._version)
+    def prepared(self):
+        """(codes, scales) in the device layout the kernels read (tiles of
+        32 rows x 256 inputs, `vqmoe_prepare_vq`), made once per device and
+        weight version. Checks every code against the codebook size (one
+        host synchronisation, at first use: call it before capturing a
+        CUDA graph)."""
+        c, vs = self.codes, self.vq_scales
+        require_cuda(c, vs)
+        key = (c.device, c.data_ptr(), c._version, vs.data_ptr(), vs._version)
         if self._dev is None or self._dev[0] != key:
             E, OUT, W = c.shape
-            K = int(self.codebook.shape[0])
-            if self.codebook.shape[1] != 4:
-                raise NotImplementedError(
-                    f"VQ dim {self.codebook.shape[1]} is not supported (dim 4)")
+            K, dim = (int(n) for n in self.codebook.shape)
+            if dim != 4:
+                raise NotImplementedError(f"VQ dim {dim} is not supported (dim 4)")
             bad = torch.zeros(1, dtype=torch.int32, device=c.device)
             _lib.call("vqmoe_count_bad_codes", c.data_ptr(), c.numel(), K,
                       bad.data_ptr(), _stream(c))
             n_bad = int(bad.item())
             if n_bad:
                 raise ValueError(f"{n_bad} VQ codes are >= the codebook size {K}")
-            out = torch.empty_like(c)
-            _lib.call("vqmoe_prepare_codes", c.data_ptr(), out.data_ptr(),
-                      E * OUT, W, _stream(c))
-            self._dev = (key, out)
-        return self._dev[1]
+            IN = W * dim
+            nc, ns = _lib.vq_layout_bytes(E, OUT, IN)
+            dc = torch.empty(nc, dtype=torch.uint8, device=c.device)
+            ds = torch.empty(ns // 2, dtype=torch.float16, device=c.device)
+            _lib.call("vqmoe_prepare_vq", c.data_ptr(), vs.data_ptr(), E, OUT, IN,
+                      dc.data_ptr(), ds.data_ptr(), _stream(c))
+            self._dev = (key, dc, ds)
+        return self._dev[1], self._dev[2]
 
     def descriptor(self) -> _lib.Linear:
-        pc = self.prepared_codes()
-        require_cuda(self.codebook, self.vq_scales)
+        dc, ds = self.prepared()
+        require_cuda(self.codebook)
         return _lib.Linear(format=_lib.FMT_VQ_U8, num_experts=self.num_experts,
                            out_features=self.output_dims,
-                           in_features=self.input_dims, codes=pc.data_ptr(),
+                           in_features=self.input_dims, codes=dc.data_ptr(),
                            codebook=self.codebook.data_ptr(),
-                           scales=self.vq_scales.data_ptr(),
+                           scales=ds.data_ptr(),
                            codebook_size=int(self.codebook.shape[0]),
                            dim=int(self.codebook.shape[1]),
                            group_size=self.group_size)
@@ -269,10 +278,9 @@ class SwitchGLU(nn.Module):
         ii = _contig(indices.reshape(T, k).to(torch.int32))
         y = torch.empty((T, k, self.down_proj.output_dims), dtype=torch.bfloat16,
                         device=x.device)
-        I = self.gate_proj.output_dims
-        ws_bytes = _lib.lib().vqmoe_switch_glu_workspace_size(min(T, 2048), k, I)
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         g, u, d = (m.descriptor() for m in (self.gate_proj, self.up_proj, self.down_proj))
+        ws_bytes = _lib.lib().vqmoe_switch_glu_workspace_size(ctypes_ref(g), ctypes_ref(d), T, k)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         _lib.call("vqmoe_switch_glu", ctypes_ref(g), ctypes_ref(u), ctypes_ref(d),
                   xi.data_ptr(), ii.data_ptr(), T, k, y.data_ptr(), ws.data_ptr(),
                   ws_bytes, _stream(x))

@@ -33,7 +33,7 @@ from __future__ import annotations
 import numpy as np
 
 __all__ = [
-    "bf16", "f16", "f16_sat", "dequant", "prepare_codes", "unprepare_codes",
+    "bf16", "f16", "f16_sat", "dequant", "prepare_vq",
     "linear", "router", "switch_linear", "switch_glu", "sparse_moe_block",
     "tp_sparse_moe_block", "shard_block_params", "LazyVQ",
 ]
@@ -128,32 +128,29 @@ class LazyVQ:
                        self.scales[e:e + 1], self.group_size)[0]
 
 
-def prepare_codes(codes: np.ndarray) -> np.ndarray:
-    """The device layout of uint8 dim-4 codes (what `vqmoe_prepare_codes`
-    writes): each row's codes are cut into chunks of 64 codes (256 input
-    features; the last chunk may hold fewer, a multiple of 16 codes); inside
-    a chunk of nq*4 codes, code `4*q + t` moves to position `t*nq + q`.
-    Thread t of an MMA quad then finds the nq codes it consumes contiguous.
-    Pure permutation; `unprepare_codes` inverts it."""
+def prepare_vq(codes: np.ndarray, scales: np.ndarray):
+    """The device layout `vqmoe_prepare_vq` writes (restated from its
+    definition, for the layout tests): rows padded to a multiple of 32,
+    inputs to a multiple of 256 (padding codes and scales 0), tiles of 32
+    rows x 256 inputs. In a 2048-byte code tile, row r = 16*mt + 8*h + g and
+    chunk code u = 4*(8*half + b) + t sit at half*1024 + (2*mt + h)*256 +
+    (4*g + t)*8 + b; in a 128-element scale tile, group 4*c + 2*half + jj of
+    row r sits at half*64 + (2*mt + h)*16 + 2*g + jj.
+    Returns (codes uint8 [tiles*2048], scales fp16 [tiles*128])."""
     E, OUT, NC = codes.shape
-    out = np.empty_like(codes)
-    for c0 in range(0, NC, 64):
-        n = min(64, NC - c0)
-        nq = n // 4
-        blk = codes[..., c0:c0 + n].reshape(E, OUT, nq, 4)
-        out[..., c0:c0 + n] = np.swapaxes(blk, -1, -2).reshape(E, OUT, n)
-    return out
-
-
-def unprepare_codes(prep: np.ndarray) -> np.ndarray:
-    E, OUT, NC = prep.shape
-    out = np.empty_like(prep)
-    for c0 in range(0, NC, 64):
-        n = min(64, NC - c0)
-        nq = n // 4
-        blk = prep[..., c0:c0 + n].reshape(E, OUT, 4, nq)
-        out[..., c0:c0 + n] = np.swapaxes(blk, -1, -2).reshape(E, OUT, n)
-    return out
+    IN = NC * 4
+    RB, C = -(-OUT // 32), -(-IN // 256)
+    cp = np.zeros((E, RB * 32, C * 64), np.uint8)
+    cp[:, :OUT, :NC] = codes
+    sp = np.zeros((E, RB * 32, C * 4), np.float16)
+    sp[:, :OUT, :IN // 64] = scales
+    # codes: [E, RB, mt, h, g, C, half, b, t] -> [E, RB, C, half, mt, h, g, t, b]
+    c9 = cp.reshape(E, RB, 2, 2, 8, C, 2, 8, 4)
+    dc = c9.transpose(0, 1, 5, 6, 2, 3, 4, 8, 7).reshape(-1)
+    # scales: [E, RB, mt, h, g, C, half, jj] -> [E, RB, C, half, mt, h, g, jj]
+    s8 = sp.reshape(E, RB, 2, 2, 8, C, 2, 2)
+    ds = s8.transpose(0, 1, 5, 6, 2, 3, 4, 7).reshape(-1)
+    return np.ascontiguousarray(dc), np.ascontiguousarray(ds)
 
 
 # ---------------------------------------------------------------- matmuls

@@ -54,7 +54,11 @@ def test_workspace_queries_are_host_only(so):
     assert 0 < n64 < n128 and n64 % 256 == 0
     # act [T*k, I] + ybuf [T*k, H] dominate
     assert n64 >= 64 * 8 * (768 + 2048) * 2
-    assert so.vqmoe_switch_glu_workspace_size(64, 8, 768) == 64 * 8 * 768 * 2
+    g, d = b.gate, b.down
+    nglu = so.vqmoe_switch_glu_workspace_size(ctypes.byref(g), ctypes.byref(d), 64, 8)
+    assert nglu >= 64 * 8 * 768 * 2 + 64 * 2048 * 2       # act + fp16 copy of x
+    nlin = so.vqmoe_switch_linear_workspace_size(ctypes.byref(g), 64, 8, 0)
+    assert 0 < nlin < nglu
     assert so.vqmoe_router_workspace_size(64, 128) >= 64 * 129 * 4
 
 
@@ -67,5 +71,6 @@ def test_bad_arguments_return_a_status_not_a_crash(so):
     st = so.vqmoe_sparse_moe_block(ctypes.byref(b), None, 64, None, 0, None, 0, None)
     assert _lib.STATUS[st] == "BAD_FORMAT"
     assert b"group_size" in so.vqmoe_last_error()
-    st = so.vqmoe_prepare_codes(None, None, 4, 64, None)
-    assert _lib.STATUS[st] == "BAD_SHAPE"
+    st = so.vqmoe_prepare_vq(None, None, 2, 32, 100, None, None, None)
+    assert _lib.STATUS[st] == "BAD_SHAPE"          # IN not a multiple of 64
+    assert _lib.vq_layout_bytes(2, 48, 320) == (2 * 2 * 2 * 2048, 2 * 2 * 2 * 128 * 2)

@@ -7,8 +7,13 @@ Bars:
 * router weights and sigmoid gate: within one bf16 step (CUDA's expf vs
   numpy's exp in float32);
 * layer outputs (bf16): max |gpu - oracle| <= 1e-2 * max |oracle| (the
-  north star's 1e-2 relative), and at most 1% of elements more than one
-  bf16 step apart (float32 MMA accumulation vs the oracle's exact sums).
+  north star's 1e-2 relative), and at most 1% of elements further apart
+  than 2^-6 |oracle| + 2^-7 rms(oracle). The GPU accumulates in float32
+  (MMA), the oracle exactly, so a bf16-rounded intermediate (an expert
+  output, a SwiGLU activation) now and then lands one step apart; through
+  the k-sum such a step is a step of the summands' magnitude, which
+  cancellation can make many steps of a small output element -- hence the
+  rms term.
 """
 import ctypes
 
@@ -38,9 +43,11 @@ def assert_bf16_close(got, ref, what=""):
     scale = float(np.abs(ref).max()) or 1.0
     diff = np.abs(got - ref)
     assert diff.max() <= REL * scale, f"{what}: max diff {diff.max():.3e} vs {REL} * {scale:.3e}"
-    step = np.maximum(np.abs(ref), 2.0 ** -100) * 2.0 ** -7
+    rms = float(np.sqrt(np.mean(np.square(ref))))
+    step = np.abs(ref) * 2.0 ** -6 + rms * 2.0 ** -7
     frac = float((diff > step).mean())
-    assert frac <= ULP_FRACTION, f"{what}: {frac:.2%} of elements more than one bf16 step off"
+    assert frac <= ULP_FRACTION, f"{what}: {frac:.2%} of elements off by more than " \
+                                 f"2^-6 |ref| + 2^-7 rms"
 
 
 def _router(x, w, k, shared_gate=None):
@@ -98,14 +105,18 @@ def test_dequantised_weights_are_bit_exact():
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
-def test_prepared_codes_match_the_oracle_layout_and_invert():
-    codes = torch.randint(0, 256, (3, 32, 192), dtype=torch.uint8)
+@pytest.mark.parametrize("E,OUT,IN", [(3, 32, 192), (2, 48, 320), (2, 64, 512)])
+def test_device_layout_matches_the_oracle_and_inverts(E, OUT, IN):
+    codes = torch.randint(0, 256, (E, OUT, IN // 4), dtype=torch.uint8)
+    scales = (0.5 + torch.rand(E, OUT, IN // 64)).to(torch.float16)
     m = VQSwitchLinear(codes.to(DEV), torch.zeros(256, 4, dtype=torch.float16, device=DEV),
-                       torch.ones(3, 32, 12, dtype=torch.float16, device=DEV), group_size=64)
-    pc = m.prepared_codes()
-    assert np.array_equal(pc.cpu().numpy(), R.prepare_codes(codes.numpy()))
-    back = torch.empty_like(pc)
-    _lib.call("vqmoe_unprepare_codes", pc.data_ptr(), back.data_ptr(), 3 * 32, 192,
+                       scales.to(DEV), group_size=64)
+    dc, ds = m.prepared()
+    rc, rs = R.prepare_vq(codes.numpy(), scales.numpy())
+    assert np.array_equal(dc.cpu().numpy(), rc)
+    assert np.array_equal(ds.cpu().numpy().view(np.uint16), rs.view(np.uint16))
+    back = torch.empty_like(codes, device=DEV)
+    _lib.call("vqmoe_unprepare_codes", dc.data_ptr(), E, OUT, IN, back.data_ptr(),
               torch.cuda.current_stream().cuda_stream)
     assert torch.equal(back.cpu(), codes)
 
@@ -191,7 +202,7 @@ def test_out_of_range_codes_are_refused():
     m = VQSwitchLinear(codes, torch.zeros(200, 4, dtype=torch.float16, device=DEV),
                        torch.ones(1, 16, 1, dtype=torch.float16, device=DEV), group_size=64)
     with pytest.raises(ValueError, match="codebook size 200"):
-        m.prepared_codes()
+        m.prepared()
 
 
 @pytest.mark.parametrize("n", [2, 4])

@@ -65,17 +65,32 @@ def test_bf16_rounding_of_float64_is_single_rounding():
     assert np.array_equal(got, ref)
 
 
-def test_prepared_codes_are_a_permutation_with_thread_contiguous_chunks():
+def test_device_layout_gives_each_lane_its_mma_codes():
+    """In the device layout, lane 4g+t's 8 bytes of (half, mt, h) are the
+    codes of row 16mt+8h+g it feeds into MMA sub-steps 8*half .. 8*half+7
+    (chunk code 4q+t), and the 8 padded rows / tail inputs are zero."""
     rng = np.random.default_rng(2)
-    for nc in (16, 48, 64, 192, 512):
-        c = rng.integers(0, 256, (2, 3, nc), dtype=np.uint8)
-        p = R.prepare_codes(c)
-        assert np.array_equal(R.unprepare_codes(p), c)
-        # chunk 0: thread t's codes (units 4q+t) sit at t*nq .. t*nq+nq
-        n0 = min(64, nc)
-        nq = n0 // 4
-        for t in range(4):
-            assert np.array_equal(p[..., t * nq:(t + 1) * nq], c[..., t:n0:4])
+    E, OUT, IN = 2, 48, 320                # 2 row blocks (16 padded), 2 chunks
+    codes = rng.integers(1, 256, (E, OUT, IN // 4), dtype=np.uint8)
+    scales = (0.5 + rng.random((E, OUT, IN // 64))).astype(np.float16)
+    dc, ds = R.prepare_vq(codes, scales)
+    RB, C = 2, 2
+    assert dc.size == E * RB * C * 2048 and ds.size == E * RB * C * 128
+    for e, rb, c, half, mt, h, g, t in [(1, 0, 1, 0, 1, 0, 3, 2), (0, 1, 0, 1, 0, 1, 7, 0),
+                                         (1, 1, 1, 1, 0, 1, 5, 3)]:
+        tile = (e * RB + rb) * C + c
+        got = dc[tile * 2048 + half * 1024 + (2 * mt + h) * 256 + (4 * g + t) * 8:][:8]
+        row = rb * 32 + mt * 16 + h * 8 + g
+        for b in range(8):
+            u = c * 64 + 4 * (half * 8 + b) + t
+            want = codes[e, row, u] if row < OUT and u < IN // 4 else 0
+            assert got[b] == want
+        for jj in range(2):
+            grp = c * 4 + half * 2 + jj
+            want = scales[e, row, grp] if row < OUT and grp < IN // 64 else 0
+            assert ds[tile * 128 + half * 64 + (2 * mt + h) * 16 + 2 * g + jj] == want
+    # padded rows 48..63 carry zero scales: their weights are exactly zero
+    assert (dc.size - np.count_nonzero(dc)) >= E * 16 * C * 64
 
 
 def test_dequant_is_the_rounded_product_of_codebook_and_scale():
