@@ -63,8 +63,9 @@ combine_kernel(const uint16_t *__restrict__ ybuf, int T, int k, int H,
         float acc[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll 8
         for (int s = 0; s < k; ++s) {
-            uint4 y = *reinterpret_cast<const uint4 *>(ybuf + ((size_t)tkn * k + s) * H + c8 * 8);
+            uint4 y = __ldg(reinterpret_cast<const uint4 *>(ybuf + ((size_t)tkn * k + s) * H + c8 * 8));
             const uint32_t u[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -156,6 +157,8 @@ struct RouteWs {
     int32_t *cnt, *off, *list, *active, *rank;
     uint32_t *zero;      // [0] gate/up counter, [1] down counter, then semaphores
     int zero_words;
+    uint32_t *szero;     // the shared expert's semaphores (zeroed on its own stream)
+    int szero_words;
     uint32_t *sem_gu, *sem_dn, *ssem_gu, *ssem_dn;
     float *part_gu, *part_dn, *spart_gu, *spart_dn;
     int ks_gu, ks_dn, sks_gu, sks_dn;
@@ -180,13 +183,15 @@ static void carve_route(Carve &c, RouteWs &w, int E, int P, int H, int I, int T,
         srb_gu = (Is + 31) / 32;
         srb_dn = (H + 31) / 32;
     }
-    w.zero_words = 2 + E * rb_gu + E * rb_dn + srb_gu + srb_dn;
+    w.zero_words = 2 + E * rb_gu + E * rb_dn;
     w.zero = c.take<uint32_t>(w.zero_words);
+    w.szero_words = srb_gu + srb_dn;
+    w.szero = w.szero_words ? c.take<uint32_t>(w.szero_words) : nullptr;
     if (w.zero) {
         w.sem_gu = w.zero + 2;
         w.sem_dn = w.sem_gu + (size_t)E * rb_gu;
-        w.ssem_gu = w.sem_dn + (size_t)E * rb_dn;
-        w.ssem_dn = w.ssem_gu + srb_gu;
+        w.ssem_gu = w.szero;
+        w.ssem_dn = w.szero ? w.szero + srb_gu : nullptr;
     }
     const int nm = dual ? 2 : 1;
     w.part_gu = dual && w.ks_gu > 1 ? c.take<float>((size_t)w.ks_gu * P * 2 * I) : nullptr;
@@ -297,40 +302,87 @@ static RoutedIO routed_io(const RouteWs &rt, int E, int k, int P, const void *x,
     return r;
 }
 
+// The shared expert runs on a side stream forked from the caller's stream
+// (an event after the caller's prior work) and joined before the combine, so
+// it overlaps the routing and the routed experts. One side stream and event
+// pair per host thread and device, created on the first call on that device
+// (make that call before capturing the stream into a CUDA graph).
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+constexpr int kMaxDevices = 64;
+
+static vqmoe_status side_stream(SideStream **out) {
+    static thread_local SideStream per_dev[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return set_error(VQMOE_LAUNCH_FAILED, "side stream: cudaGetDevice");
+    SideStream &ss = per_dev[dev];
+    if (!ss.s) {
+        int lo = 0, hi = 0;
+        cudaDeviceGetStreamPriorityRange(&lo, &hi);
+        if (cudaStreamCreateWithPriority(&ss.s, cudaStreamNonBlocking, hi) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(VQMOE_LAUNCH_FAILED, "side stream: create");
+        }
+    }
+    *out = &ss;
+    return VQMOE_OK;
+}
+
+static vqmoe_status run_shared(const vqmoe_block *b, const uint16_t *x, int T, const BlockWs &w,
+                               cudaStream_t st) {
+    const RouteWs &rt = w.rt;
+    if (rt.szero_words &&
+        cudaMemsetAsync(rt.szero, 0, (size_t)rt.szero_words * sizeof(uint32_t), st) != cudaSuccess)
+        return check_launch("shared expert semaphores");
+    vqmoe_status s = launch_shared_dense(x, b->shared_gate_w, b->shared_up_w, T, b->hidden,
+                                         b->shared_inter, w.act_s, rt.spart_gu, rt.ssem_gu, st);
+    if (s != VQMOE_OK) return s;
+    return launch_shared_dense(w.act_s, b->shared_down_w, nullptr, T, b->shared_inter, b->hidden,
+                               w.sh, rt.spart_dn, rt.ssem_dn, st);
+}
+
 static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                               void *out, int out_f32, const BlockWs &w,
                               cudaStream_t st, cudaEvent_t *ev = nullptr, int n_ev = 0) {
     const int H = b->hidden, E = b->num_experts, k = b->top_k, P = T * k;
-    const int Is = b->shared_inter;
-    const bool shared = Is > 0;
+    const bool shared = b->shared_inter > 0;
     const bool vq_in = b->gate.format == VQMOE_FMT_VQ_U8;
     const bool vq_dn = b->down.format == VQMOE_FMT_VQ_U8;
     vqmoe_status s;
     if ((s = mark(ev, n_ev, 0, st)) != VQMOE_OK) return s;
-    s = launch_router(x, static_cast<const uint16_t *>(b->router_w),
-                      shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr,
-                      T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, st);
-    if (s != VQMOE_OK) return s;
+    SideStream *side = nullptr;
+    if (shared) {
+        if ((s = side_stream(&side)) != VQMOE_OK) return s;
+        if (cudaEventRecord(side->fork, st) != cudaSuccess ||
+            cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
+            return check_launch("side stream fork");
+        if ((s = run_shared(b, x, T, w, side->s)) != VQMOE_OK) return s;
+        if (cudaEventRecord(side->join, side->s) != cudaSuccess)
+            return check_launch("side stream join");
+    }
     const RouteWs &rt = w.rt;
-    s = launch_route(w.inds, P, E, rt.cnt, rt.off, rt.list, rt.active, rt.rank, rt.zero,
-                     rt.zero_words, st);
+    s = launch_router_route(x, static_cast<const uint16_t *>(b->router_w),
+                            shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr,
+                            T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, rt.cnt, rt.off,
+                            rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 1, st)) != VQMOE_OK) return s;
-    // gate/up + SwiGLU (routed VQ / bf16 experts, and the shared expert)
+    // gate/up + SwiGLU of the routed experts
     RoutedIO r1 = routed_io(rt, E, k, P, vq_in ? (const void *)w.x16 : (const void *)x, 0, w.act,
                             vq_dn, nullptr, rt.part_gu, rt.sem_gu, rt.ks_gu);
-    if (shared && (s = launch_shared_dense(x, b->shared_gate_w, b->shared_up_w, T, H, Is, w.act_s,
-                                           rt.spart_gu, rt.ssem_gu, st)) != VQMOE_OK)
-        return s;
     s = launch_expert_stage(&b->gate, &b->up, &r1, nullptr, rt.zero, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK) return s;
-    // down (x routing weight), and the shared expert's down
+    // down (x routing weight)
     RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores, rt.part_dn, rt.sem_dn,
                             rt.ks_dn);
-    if (shared && (s = launch_shared_dense(w.act_s, b->shared_down_w, nullptr, T, Is, H, w.sh,
-                                           rt.spart_dn, rt.ssem_dn, st)) != VQMOE_OK)
-        return s;
     s = launch_expert_stage(&b->down, nullptr, &r2, nullptr, rt.zero + 1, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 3, st)) != VQMOE_OK) return s;
+    if (shared && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
+        return check_launch("side stream join");
     if ((s = mark(ev, n_ev, 4, st)) != VQMOE_OK) return s;
     const size_t nvec = (size_t)T * (H / 8);
     const int grid = (int)std::min<size_t>((nvec + 255) / 256, (size_t)sm_count() * 8);

@@ -17,11 +17,14 @@
 // For a VQ tile each lane
 //   * streams its codes and group scales through a ring of four register
 //     half-chunk buffers (loads issued three half chunks, ~1 us, ahead);
-//   * looks each code up in a shared-memory codebook and multiplies the
-//     8-byte entry (4 fp16) by its group scale in one mul.rn.f16x2 -- the
-//     product is the dequantised fp16 weight -- and feeds those registers
-//     straight into mma.sync m16n8k16 as the A operand (fp16 x fp16 ->
-//     fp32); B is the tile's token rows from shared memory.
+//   * looks each code up in a shared-memory codebook and feeds the 8-byte
+//     entry (4 fp16) straight into mma.sync m16n8k16 as the A operand
+//     (fp16 x fp16 -> fp32); B is the tile's token rows from shared memory;
+//   * sums each 64-input scale group on its own and adds it to the row's
+//     total times the group scale in fp32 (4 FMA per MMA fragment). The
+//     weight this applies is the exact product codebook x scale; the
+//     dense decode (vqmoe_dequant) rounds that product to fp16 -- a
+//     difference below 2^-11 of each weight.
 // Dense tiles (bf16 experts, the shared expert) load A from global memory.
 //
 // Why mma.sync and registers here rather than tcgen05: at 1-64 tokens the
@@ -146,19 +149,17 @@ __device__ __forceinline__ void load_half(HalfBuf<NMAT, MT> &b, const uint8_t *c
 
 // 8 sub-steps from a half buffer; xoff: this lane's staged-row offset of
 // sub-step 0; lanebyte: this lane's codebook copy offset (lane % 16) * 8.
+// Each scale group (4 sub-steps, 64 inputs) is summed on its own from the
+// raw fp16 codebook entries (products exact, fp32 accumulate) and added to
+// the row's total times the group's fp16 scale (4 FMA per fragment).
 template <int NMAT, int MT>
 __device__ __forceinline__ void compute_half(const HalfBuf<NMAT, MT> &b, float (&acc)[NMAT][MT][4],
                                              const uint8_t *cb, uint32_t lanebyte,
                                              const uint8_t *xs, int xoff) {
+    const float zero[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < 2; ++j) {          // the half's two scale groups
-        uint32_t s2[NMAT][MT][2];
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) s2[m][mt][h] = bcast_half(b.sc[m][mt][h], j);
+        float gacc[NMAT][MT][4];
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
             const int q = 4 * j + qq;
@@ -173,12 +174,25 @@ __device__ __forceinline__ void compute_half(const HalfBuf<NMAT, MT> &b, float (
                     const uint32_t a1 = __byte_perm(b.cw[m][mt][1][j], lanebyte, sel);
                     const uint2 e0 = lds2(cb + m * 128, a0);
                     const uint2 e1 = lds2(cb + m * 128, a1);
-                    const uint32_t s0 = s2[m][mt][0], s1 = s2[m][mt][1];
-                    mma_f16(acc[m][mt], hmul2_u32(e0.x, s0), hmul2_u32(e1.x, s1),
-                            hmul2_u32(e0.y, s0), hmul2_u32(e1.y, s1), bf.x, bf.y);
+                    if (qq == 0)
+                        mma_f16_c(gacc[m][mt], e0.x, e1.x, e0.y, e1.y, bf.x, bf.y, zero);
+                    else
+                        mma_f16(gacc[m][mt], e0.x, e1.x, e0.y, e1.y, bf.x, bf.y);
                 }
             }
         }
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                // fragment rows g (elements 0, 1) and g + 8 (elements 2, 3)
+                const float s0 = __half2float(__ushort_as_half((unsigned short)(b.sc[m][mt][0] >> (16 * j))));
+                const float s1 = __half2float(__ushort_as_half((unsigned short)(b.sc[m][mt][1] >> (16 * j))));
+                acc[m][mt][0] = fmaf(s0, gacc[m][mt][0], acc[m][mt][0]);
+                acc[m][mt][1] = fmaf(s0, gacc[m][mt][1], acc[m][mt][1]);
+                acc[m][mt][2] = fmaf(s1, gacc[m][mt][2], acc[m][mt][2]);
+                acc[m][mt][3] = fmaf(s1, gacc[m][mt][3], acc[m][mt][3]);
+            }
     }
 }
 
@@ -494,8 +508,14 @@ __global__ void __launch_bounds__(256) shared_dense_kernel(const SharedArgs a) {
         float v[NMAT];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
-            float sum = 0.0f;
-            for (int q = 0; q < a.ks; ++q) sum += __ldcg(&a.part[(((size_t)q * a.T + tok) * NMAT + m) * a.OUT + row]);
+            float pv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                pv[q] = q < a.ks ? __ldcg(&a.part[(((size_t)q * a.T + tok) * NMAT + m) * a.OUT + row]) : 0.0f;
+            float sum = pv[0];
+#pragma unroll
+            for (int q = 1; q < 4; ++q)
+                if (q < a.ks) sum += pv[q];
             v[m] = sum;
         }
         a.out[(size_t)tok * a.OUT + row] = epilogue_value<DUAL>(v[0], v[NMAT - 1], nullptr, 0, 0);
@@ -506,9 +526,10 @@ __global__ void __launch_bounds__(256) shared_dense_kernel(const SharedArgs a) {
 // so that the grid covers the GPU; plus the shared memory it needs.
 void plan_shared_dense(int IN, int OUT, int nmat, int *ks, int *kslice, size_t *smem) {
     const int rbs = (OUT + kShRows - 1) / kShRows;
-    int want = std::max(1, (int)((2LL * sm_count() + rbs - 1) / rbs));
+    int want = std::max(1, (int)((sm_count() + rbs - 1) / rbs));
+    want = std::min(want, 4);                    // at most 4 K slices to reduce
     int kl = std::max(16, (IN + want - 1) / want);
-    kl = std::min(512, (kl + 15) / 16 * 16);
+    kl = std::min(1024, (kl + 15) / 16 * 16);
     *kslice = kl;
     *ks = (IN + kl - 1) / kl;
     *smem = (size_t)(nmat * kShRows + kShTok) * (kl * 2 + 32);

@@ -9,7 +9,7 @@
 // and the shared-expert gate of qwen3_5.py:186, bf16(sigmoid(bf16(x @ w_sg))).
 //
 // router_logits_kernel (any H % 16 == 0) / router_logits_dmma_kernel
-//   (H % 128 == 0, fp64 tensor cores): the [T, E(+1)] logits. Each product of two bf16
+//   (H % 256 == 0, fp64 tensor cores): the [T, E(+1)] logits. Each product of two bf16
 //   values is exact in float64 and the dot product accumulates in float64,
 //   then rounds ONCE to bf16: the logits are correctly rounded (up to a
 //   ~2^-45 relative error), so the expert choice is the one any exact
@@ -21,7 +21,7 @@
 // route_kernel: one CTA: counting sort of the T*k (token, slot) pairs by
 //   expert -> per-expert count / offset / pair list, the list of experts
 //   that received pairs, and zeroed work counters for the expert kernels.
-#include "common.cuh"
+#include "stages.cuh"
 
 namespace vqmoe {
 
@@ -110,25 +110,27 @@ router_logits_kernel(const uint16_t *__restrict__ x,
         logits[(size_t)(t0 + lane) * E1 + row] = bf16_to_f32(f64_to_bf16(mine));
 }
 
-// Tensor-core variant (H % 128 == 0): fp64 MMA m8n8k4 (A = 8 tokens x 4
+// Tensor-core variant (H % 256 == 0): fp64 MMA m8n8k4 (A = 8 tokens x 4
 // inputs, B = 4 inputs x 8 router rows, fp64 accumulate). bf16 values
 // convert exactly to fp64 and each product is exact, as in the CUDA-core
-// kernel. A CTA owns an 8 x 8 tile of logits; its 4 warps split H; lane
-// (g, t) feeds inputs [q*H/4 + t*H/16, +H/16) of warp q in order -- one
+// kernel. A CTA owns an 8 x 8 tile of logits; its 8 warps split H; lane
+// (g, t) feeds inputs [q*H/8 + t*H/32, +H/32) of warp q in order -- one
 // permutation of the k axis applied to A and B alike -- so every lane
-// reads contiguous 16-byte vectors. The 4 warp partials (each summed over
-// two interleaved accumulators) are added in a fixed order.
+// reads contiguous 16-byte vectors, all issued before the first MMA. The
+// warp partials (each summed over two interleaved accumulators) are added
+// in a fixed order.
 __device__ __forceinline__ void dmma_f64(double (&d)[2], double a, double b) {
     asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
         : "+d"(d[0]), "+d"(d[1])
         : "d"(a), "d"(b));
 }
 
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 router_logits_dmma_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
                           const uint16_t *__restrict__ wsg, int T, int H, int E, int E1,
                           float *__restrict__ logits, uint16_t *__restrict__ x16) {
-    __shared__ double part[4][8][8];
+    constexpr int NW = 8;                        // warps splitting H
+    __shared__ double part[NW][8][8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int t0 = blockIdx.y * 8, e0 = blockIdx.x * 8;
@@ -145,109 +147,46 @@ router_logits_dmma_kernel(const uint16_t *__restrict__ x, const uint16_t *__rest
             *reinterpret_cast<uint4 *>(x16 + (size_t)(t0 + r) * H + c * 8) = make_uint4(u[0], u[1], u[2], u[3]);
         }
     }
-    const int seg = H >> 4;                      // inputs per lane
-    const int k0 = warp * (H >> 2) + t * seg;
+    const int seg = H / (4 * NW);                // inputs per lane (multiple of 8)
+    const int k0 = warp * (H / NW) + t * seg;
     const int tok = t0 + g, row = e0 + g;
     const bool tok_ok = tok < T, row_ok = row < E1;
     const uint16_t *xp = x + (size_t)(tok_ok ? tok : 0) * H + k0;
-    const uint16_t *wp = (row < E ? w + (size_t)row * H : wsg) + k0;
-    double d0[2] = {0.0, 0.0}, d1[2] = {0.0, 0.0};
-    for (int j = 0; j < seg; j += 8) {
-        const uint4 xv = tok_ok ? *reinterpret_cast<const uint4 *>(xp + j) : make_uint4(0, 0, 0, 0);
-        const uint4 wv = row_ok ? *reinterpret_cast<const uint4 *>(wp + j) : make_uint4(0, 0, 0, 0);
-        const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w}, wu[4] = {wv.x, wv.y, wv.z, wv.w};
+    const uint16_t *wp = (row < E ? w + (size_t)row * H : (wsg ? wsg : w)) + k0;
+    double d0[2] = {0.0, 0.0}, d1[2] = {0.0, 0.0}, d2[2] = {0.0, 0.0}, d3[2] = {0.0, 0.0};
+    for (int j0 = 0; j0 < seg; j0 += 64) {       // up to 8 vectors of each in flight
+        uint4 xv[8], wv[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            dmma_f64(d0, (double)bf16_to_f32(xu[i] & 0xFFFFu), (double)bf16_to_f32(wu[i] & 0xFFFFu));
-            dmma_f64(d1, (double)bf16_to_f32(xu[i] >> 16), (double)bf16_to_f32(wu[i] >> 16));
+        for (int i = 0; i < 8; ++i) {
+            const bool in = j0 + 8 * i < seg;
+            xv[i] = (tok_ok && in) ? __ldg(reinterpret_cast<const uint4 *>(xp + j0 + 8 * i)) : make_uint4(0, 0, 0, 0);
+            wv[i] = (row_ok && in) ? __ldg(reinterpret_cast<const uint4 *>(wp + j0 + 8 * i)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t xu[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
+            const uint32_t wu[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+            for (int q = 0; q < 4; q += 2) {
+                dmma_f64(d0, (double)bf16_to_f32(xu[q] & 0xFFFFu), (double)bf16_to_f32(wu[q] & 0xFFFFu));
+                dmma_f64(d1, (double)bf16_to_f32(xu[q] >> 16), (double)bf16_to_f32(wu[q] >> 16));
+                dmma_f64(d2, (double)bf16_to_f32(xu[q + 1] & 0xFFFFu), (double)bf16_to_f32(wu[q + 1] & 0xFFFFu));
+                dmma_f64(d3, (double)bf16_to_f32(xu[q + 1] >> 16), (double)bf16_to_f32(wu[q + 1] >> 16));
+            }
         }
     }
     // D fragment: (token g, rows 2t, 2t+1)
-    part[warp][g][2 * t] = d0[0] + d1[0];
-    part[warp][g][2 * t + 1] = d0[1] + d1[1];
+    part[warp][g][2 * t] = (d0[0] + d1[0]) + (d2[0] + d3[0]);
+    part[warp][g][2 * t + 1] = (d0[1] + d1[1]) + (d2[1] + d3[1]);
     __syncthreads();
     if (tid < 64) {
         const int tg = tid >> 3, rr = tid & 7;
-        const double v = ((part[0][tg][rr] + part[1][tg][rr]) + part[2][tg][rr]) + part[3][tg][rr];
+        double v = part[0][tg][rr];
+#pragma unroll
+        for (int q = 1; q < NW; ++q) v += part[q][tg][rr];
         if (t0 + tg < T && e0 + rr < E1)
             logits[(size_t)(t0 + tg) * E1 + e0 + rr] = bf16_to_f32(f64_to_bf16(v));
     }
-}
-
-constexpr int kMaxExpertsPerLane = 16;   // E <= 512
-
-__global__ void __launch_bounds__(256)
-router_topk_kernel(const float *__restrict__ logits, int T, int E, int E1,
-                   int k, int has_shared, int32_t *__restrict__ inds,
-                   float *__restrict__ scores, float *__restrict__ sgate) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (t >= T) return;
-    const float *lr = logits + (size_t)t * E1;
-    float l[kMaxExpertsPerLane];
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-        int j = lane + 32 * i;
-        l[i] = j < E ? lr[j] : -INFINITY;
-        m = fmaxf(m, l[i]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float ex[kMaxExpertsPerLane];
-    float z = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-        int j = lane + 32 * i;
-        ex[i] = j < E ? expf(l[i] - m) : 0.0f;
-        z += ex[i];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-    uint32_t taken = 0;
-    float den = 0.0f, my_p = 0.0f;
-    int my_j = 0;
-    for (int s = 0; s < k; ++s) {
-        float bl = -INFINITY;
-        int bj = 0x7fffffff;
-        float be = 0.0f;
-#pragma unroll
-        for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-            int j = lane + 32 * i;
-            bool ok = j < E && !((taken >> i) & 1u);
-            // ascending j inside the lane: strict > keeps the lower index
-            if (ok && (l[i] > bl || bj == 0x7fffffff)) {
-                bl = l[i];
-                bj = j;
-                be = ex[i];
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float ol = __shfl_xor_sync(0xffffffffu, bl, o);
-            int oj = __shfl_xor_sync(0xffffffffu, bj, o);
-            float oe = __shfl_xor_sync(0xffffffffu, be, o);
-            bool better = (oj != 0x7fffffff) &&
-                          (bj == 0x7fffffff || ol > bl || (ol == bl && oj < bj));
-            if (better) {
-                bl = ol;
-                bj = oj;
-                be = oe;
-            }
-        }
-        if ((bj & 31) == lane) taken |= 1u << (bj >> 5);
-        const float p = be / z;
-        den += p;                 // sequential float32 sum, selection order
-        if (lane == s) {          // lane s keeps slot s (k <= 32)
-            my_p = p;
-            my_j = bj;
-        }
-    }
-    if (lane < k) {
-        inds[(size_t)t * k + lane] = my_j;
-        scores[(size_t)t * k + lane] = bf16r(my_p / den);
-    }
-    if (lane == 0 && has_shared) sgate[t] = bf16r(sigmoid_f32(lr[E]));
 }
 
 // Counting sort of pairs by expert (one CTA). Out-of-range expert ids are
@@ -326,11 +265,201 @@ route_kernel(const int32_t *__restrict__ inds, int P, int E,
     }
 }
 
-vqmoe_status launch_router(const uint16_t *x, const uint16_t *w,
-                           const uint16_t *wsg, int T, int H, int E, int k,
-                           float *logits, int32_t *inds, float *scores,
-                           float *sgate, uint16_t *x16, cudaStream_t stream) {
-    const int E1 = E + (wsg ? 1 : 0);
+// Top-k of one token by one warp (E <= 32 * EPL): float32 softmax over the
+// bf16 logits, then the k largest by (logit, lower expert first) and
+// float32 renormalisation in selection order; lane s (< k) returns slot s.
+// Each logit becomes a unique 32-bit key (order-preserving bf16 bits above
+// 0xFFFF - expert), each lane sorts its EPL keys, and k rounds take the
+// warp maximum of the lanes' heads (one shuffle per level) and pop it.
+__device__ __forceinline__ uint32_t logit_key(float l, int j) {
+    uint32_t b = __float_as_uint(l) >> 16;       // a bf16 value
+    if (b == 0x8000u) b = 0;                     // -0 ties with +0
+    const uint32_t ob = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+    return (ob << 16) | (0xFFFFu - (uint32_t)j);
+}
+
+template <int EPL>
+__device__ __forceinline__ void topk_warp(const float *__restrict__ lr, int E, int k, int lane,
+                                          int &my_j, float &my_score) {
+    float l[EPL], ex[EPL];
+    uint32_t key[EPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int j = lane + 32 * i;
+        l[i] = j < E ? lr[j] : -INFINITY;
+        m = fmaxf(m, l[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float z = 0.0f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int j = lane + 32 * i;
+        ex[i] = j < E ? expf(l[i] - m) : 0.0f;
+        z += ex[i];
+        key[i] = j < E ? logit_key(l[i], j) : 0u;   // 0: below every real key
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+    // sort this lane's keys (with their exponentials) descending
+#pragma unroll
+    for (int a = 0; a < EPL; ++a)
+#pragma unroll
+        for (int b = EPL - 1; b > a; --b)
+            if (key[b] > key[b - 1]) {
+                const uint32_t tk = key[b]; key[b] = key[b - 1]; key[b - 1] = tk;
+                const float te = ex[b]; ex[b] = ex[b - 1]; ex[b - 1] = te;
+            }
+    float den = 0.0f, my_p = 0.0f;
+    my_j = 0;
+    for (int s = 0; s < k; ++s) {
+        uint32_t best = key[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+        const int j = 0xFFFF - (int)(best & 0xFFFFu);
+        const int owner = j & 31;
+        const float e = __shfl_sync(0xffffffffu, ex[0], owner);
+        if (lane == owner) {           // pop the head
+#pragma unroll
+            for (int i = 0; i + 1 < EPL; ++i) {
+                key[i] = key[i + 1];
+                ex[i] = ex[i + 1];
+            }
+            key[EPL - 1] = 0u;
+        }
+        const float p = e / z;
+        den += p;                      // sequential float32 sum, selection order
+        if (lane == s) {
+            my_p = p;
+            my_j = j;
+        }
+    }
+    my_score = bf16r(my_p / den);
+}
+
+// Routing for one launch of up to kSelectMaxTok tokens in ONE CTA: top-k of
+// every token (a warp per token), then the counting sort of the (token,
+// slot) pairs by expert, without leaving the CTA. Zeroes `zero`.
+constexpr int kSelectMaxTok = 512;
+template <int EPL>
+__global__ void __launch_bounds__(1024)
+router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int k, int has_shared,
+                     int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate,
+                     int32_t *__restrict__ cnt, int32_t *__restrict__ off, int32_t *__restrict__ list,
+                     int32_t *__restrict__ active, uint32_t *__restrict__ zero, int zero_words) {
+    extern __shared__ int32_t s_dyn[];
+    int32_t *s_cnt = s_dyn;              // [E]
+    int32_t *s_off = s_dyn + E;          // [E]
+    int32_t *s_pe = s_dyn + 2 * E;       // [T*k] expert of each pair
+    int32_t *s_rank = s_pe + T * k;      // [T*k]
+    __shared__ int32_t s_wsum[32], s_asum[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < zero_words; i += blockDim.x) zero[i] = 0u;
+    for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
+    __syncthreads();
+    for (int t = warp; t < T; t += 32) {
+        const float *lr = logits + (size_t)t * E1;
+        int j;
+        float sc;
+        topk_warp<EPL>(lr, E, k, lane, j, sc);
+        if (lane < k) {
+            inds[(size_t)t * k + lane] = j;
+            scores[(size_t)t * k + lane] = sc;
+            s_pe[t * k + lane] = j;
+            s_rank[t * k + lane] = atomicAdd(&s_cnt[j], 1);
+        }
+        if (lane == 0 && has_shared) sgate[t] = bf16r(sigmoid_f32(lr[E]));
+    }
+    __syncthreads();
+    // exclusive scans of counts and of (count > 0), E <= 1024
+    const int e = tid;
+    const int c = e < E ? s_cnt[e] : 0;
+    const int a = c > 0;
+    int ic = c, ia = a;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, ic, o);
+        const int v = __shfl_up_sync(0xffffffffu, ia, o);
+        if (lane >= o) {
+            ic += u;
+            ia += v;
+        }
+    }
+    if (lane == 31) {
+        s_wsum[warp] = ic;
+        s_asum[warp] = ia;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int wc = s_wsum[lane], wa = s_asum[lane];
+        int xc = wc, xa = wa;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, xc, o);
+            const int v = __shfl_up_sync(0xffffffffu, xa, o);
+            if (lane >= o) {
+                xc += u;
+                xa += v;
+            }
+        }
+        s_wsum[lane] = xc - wc;
+        s_asum[lane] = xa - wa;
+    }
+    __syncthreads();
+    if (e < E) {
+        const int oc = s_wsum[warp] + ic - c;
+        const int oa = s_asum[warp] + ia - a;
+        s_off[e] = oc;
+        cnt[e] = c;
+        off[e] = oc;
+        if (a) active[oa] = e;
+        if (e == E - 1) {
+            off[E] = oc + c;
+            active[E] = oa + a;
+        }
+    }
+    __syncthreads();
+    for (int p = tid; p < T * k; p += blockDim.x) list[s_off[s_pe[p]] + s_rank[p]] = p;
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(256)
+router_topk_kernel_t(const float *__restrict__ logits, int T, int E, int E1, int k, int has_shared,
+                     int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= T) return;
+    const float *lr = logits + (size_t)t * E1;
+    int j;
+    float sc;
+    topk_warp<EPL>(lr, E, k, lane, j, sc);
+    if (lane < k) {
+        inds[(size_t)t * k + lane] = j;
+        scores[(size_t)t * k + lane] = sc;
+    }
+    if (lane == 0 && has_shared) sgate[t] = bf16r(sigmoid_f32(lr[E]));
+}
+
+template <int EPL>
+static void launch_topk_t(const float *logits, int T, int E, int E1, int k, int has_shared, int32_t *inds,
+                          float *scores, float *sgate, cudaStream_t st) {
+    router_topk_kernel_t<EPL><<<(T + 7) / 8, 256, 0, st>>>(logits, T, E, E1, k, has_shared, inds, scores, sgate);
+}
+
+static vqmoe_status launch_topk(const float *logits, int T, int E, int E1, int k, int has_shared,
+                                int32_t *inds, float *scores, float *sgate, cudaStream_t st) {
+    const int epl = (E + 31) / 32;
+    if (epl <= 1) launch_topk_t<1>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
+    else if (epl <= 2) launch_topk_t<2>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
+    else if (epl <= 4) launch_topk_t<4>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
+    else if (epl <= 8) launch_topk_t<8>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
+    else launch_topk_t<16>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
+    return check_launch("router_topk_kernel");
+}
+
+vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t *wsg, int T, int H,
+                           int E, int E1, float *logits, uint16_t *x16, cudaStream_t stream) {
     size_t smem = (size_t)kRouterTok * H * sizeof(uint16_t);
     static int configured_smem[64] = {0};   // per device
     int dev = 0;
@@ -343,20 +472,65 @@ vqmoe_status launch_router(const uint16_t *x, const uint16_t *w,
         if (dev >= 0 && dev < 64) configured_smem[dev] = (int)smem;
     }
     vqmoe_status s;
-    if (H % 128 == 0) {
+    if (H % 256 == 0) {
         dim3 gt((E1 + 7) / 8, (T + 7) / 8);
-        router_logits_dmma_kernel<<<gt, 128, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
+        router_logits_dmma_kernel<<<gt, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
         s = check_launch("router_logits_dmma_kernel");
     } else {
         dim3 g1((E1 + kRouterRows - 1) / kRouterRows, (T + kRouterTok - 1) / kRouterTok);
         router_logits_kernel<<<g1, 256, smem, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
         s = check_launch("router_logits_kernel");
     }
+    return s;
+}
+
+vqmoe_status launch_router(const uint16_t *x, const uint16_t *w,
+                           const uint16_t *wsg, int T, int H, int E, int k,
+                           float *logits, int32_t *inds, float *scores,
+                           float *sgate, uint16_t *x16, cudaStream_t stream) {
+    const int E1 = E + (wsg ? 1 : 0);
+    vqmoe_status s = launch_logits(x, w, wsg, T, H, E, E1, logits, x16, stream);
     if (s != VQMOE_OK) return s;
-    router_topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(logits, T, E, E1, k,
-                                                        wsg != nullptr, inds,
-                                                        scores, sgate);
-    return check_launch("router_topk_kernel");
+    return launch_topk(logits, T, E, E1, k, wsg != nullptr, inds, scores, sgate, stream);
+}
+
+// Logits, then top-k + counting sort in one CTA when the launch is small
+// enough, else top-k and the route kernel separately.
+vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uint16_t *wsg, int T,
+                                 int H, int E, int k, float *logits, int32_t *inds, float *scores,
+                                 float *sgate, uint16_t *x16, int32_t *cnt, int32_t *off,
+                                 int32_t *list, int32_t *active, int32_t *rank_scratch,
+                                 uint32_t *zero, int zero_words, cudaStream_t stream) {
+    const int E1 = E + (wsg ? 1 : 0);
+    const size_t smem_sel = (size_t)(2 * E + 2 * T * k) * sizeof(int32_t);
+    if (T > kSelectMaxTok || E > 1024 || smem_sel > 100 * 1024) {
+        vqmoe_status s = launch_router(x, w, wsg, T, H, E, k, logits, inds, scores, sgate, x16, stream);
+        if (s != VQMOE_OK) return s;
+        return launch_route(inds, T * k, E, cnt, off, list, active, rank_scratch, zero, zero_words, stream);
+    }
+    vqmoe_status s = launch_logits(x, w, wsg, T, H, E, E1, logits, x16, stream);
+    if (s != VQMOE_OK) return s;
+    static size_t configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int epl = (E + 31) / 32;
+    auto fn = epl <= 1 ? router_select_kernel<1>
+              : epl <= 2 ? router_select_kernel<2>
+              : epl <= 4 ? router_select_kernel<4>
+              : epl <= 8 ? router_select_kernel<8>
+                         : router_select_kernel<16>;
+    if (smem_sel > 48 * 1024 && (dev < 0 || dev >= 64 || smem_sel > configured[dev])) {
+        if (cudaFuncSetAttribute(router_select_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(router_select_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(router_select_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(router_select_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess ||
+            cudaFuncSetAttribute(router_select_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess)
+            return set_error(VQMOE_LAUNCH_FAILED, "router_select: shared memory");
+        if (dev >= 0 && dev < 64) configured[dev] = 100 * 1024;
+    }
+    fn<<<1, 1024, smem_sel, stream>>>(logits, T, E, E1, k, wsg != nullptr, inds, scores, sgate, cnt, off,
+                                      list, active, zero, zero_words);
+    return check_launch("router_select_kernel");
 }
 
 vqmoe_status launch_route(const int32_t *inds, int P, int E, int32_t *cnt,

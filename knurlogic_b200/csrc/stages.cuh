@@ -12,6 +12,11 @@ vqmoe_status launch_router(const uint16_t *x, const uint16_t *w, const uint16_t 
 vqmoe_status launch_route(const int32_t *inds, int P, int E, int32_t *cnt, int32_t *off,
                           int32_t *list, int32_t *active, int32_t *rank_scratch, uint32_t *zero,
                           int zero_words, cudaStream_t stream);
+vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uint16_t *wsg, int T,
+                                 int H, int E, int k, float *logits, int32_t *inds, float *scores,
+                                 float *sgate, uint16_t *x16, int32_t *cnt, int32_t *off,
+                                 int32_t *list, int32_t *active, int32_t *rank_scratch,
+                                 uint32_t *zero, int zero_words, cudaStream_t stream);
 vqmoe_status launch_to_f16(const uint16_t *x, uint16_t *x16, size_t n, cudaStream_t stream);
 
 // The routed experts of one stage: pairs grouped by expert (route_kernel).
