@@ -46,6 +46,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "VQ-MoE layer tokens/s"
 UNIT = "tokens/s"
+GATEUP_KERNEL = "expert_tile_kernel<2,1,true>"
+# kernels of one block call: router logits, top-k + routing sort, shared
+# gate/up, shared down, routed gate/up, routed down, combine
+LAUNCHES_PER_STEP = 7
 
 
 def parse():
@@ -273,10 +277,10 @@ def run_ours(args, world, rank, local):
     if stage:
         gu_bytes = stage["gateup_bytes"]
         achieved = gu_bytes / (stage["gateup_ms"] / 1e3) / 1e9
-        traffic = traffic_from_profiles("expert_units_kernel<true,true>", workload)
-        roof = {"bound": "hbm", "kernel": "fused VQ gate/up + SwiGLU (+ shared expert gate/up)",
+        traffic = traffic_from_profiles(GATEUP_KERNEL, workload)
+        roof = {"bound": "hbm", "kernel": "fused VQ gate/up + SwiGLU of the routed experts",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "kernel_name": "expert_units_kernel<true, true>",
+                "kernel_name": GATEUP_KERNEL,
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": int(gu_bytes),
                 "traffic": traffic,
@@ -301,7 +305,7 @@ def run_ours(args, world, rank, local):
         "stages_ms": stage and {k: round(v, 5) for k, v in stage.items() if k.endswith("_ms")},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "clocks": clocks.record(),
     }
     return line
@@ -336,9 +340,9 @@ def stage_profile(blocks, x, cfg, dev, args, world):
                   out.data_ptr(), odt, wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream,
                   arr, 6)
     torch.cuda.synchronize(dev)
-    # events: start | router+route | gate/up stage (routed + shared units) |
-    # down stage (routed + shared) | (same) | combine
-    names = ["router_ms", "gateup_ms", "down_ms", "shared_ms", "combine_ms"]
+    # events: start | router + routing sort | routed gate/up | routed down |
+    # join of the shared expert's side stream | combine
+    names = ["router_ms", "gateup_ms", "down_ms", "shared_wait_ms", "combine_ms"]
     acc = {k: 0.0 for k in names}
     lay = 0.0
     for row in evs[min(10, n - 1):]:
@@ -353,12 +357,11 @@ def stage_profile(blocks, x, cfg, dev, args, world):
     inds = routed_experts(blocks[0], x, dev)
     D = len(set(inds))
     H, I, k = cfg.hidden, cfg.inter // world, cfg.top_k
-    Is = cfg.shared_inter // world
     per = 2 * (I * H // cfg.dim + 2 * I * H // cfg.group)
-    # gate/up launch: routed codes + scales, the two codebooks, the shared
-    # expert's gate/up weights, x (bf16 + its fp16 copy), act out
-    st["gateup_bytes"] = (D * per + 2 * cfg.codebook_size * cfg.dim * 2 + 2 * Is * H * 2
-                          + 2 * T * H * 2 + T * k * I * 2 + T * Is * 2)
+    # routed gate/up launch: codes + scales of the D experts touched, the two
+    # codebooks, x (its fp16 copy), the SwiGLU activations out
+    st["gateup_bytes"] = (D * per + 2 * cfg.codebook_size * cfg.dim * 2 + T * H * 2
+                          + T * k * I * 2)
     c2 = synth.MoEConfig("x", cfg.experts, cfg.top_k, H, I, cfg.shared_inter // world, T)
     st["layer_bytes"] = synth.algorithmic_bytes(c2, D)
     return st, D

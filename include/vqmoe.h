@@ -29,8 +29,11 @@
  * 108-112, 170-192): bf16 matmul outputs; fp32 softmax / top-k /
  * renormalisation with weights rounded to bf16; silu / sigmoid in fp32
  * rounded once; the top-k sum in fp32 rounded once. VQ weights dequantise
- * to W = fp16(f32(codebook[code][j]) * f32(vq_scale)) and the VQ matmul
- * takes the bf16 activations as fp16 (saturated at +-65504).
+ * to W = fp16(f32(codebook[code][j]) * f32(vq_scale)) (vqmoe_dequant, bit
+ * for bit) and the VQ matmul takes the bf16 activations as fp16 (saturated
+ * at +-65504); the matmul kernels apply each 64-input group's scale to the
+ * fp32 partial sum of that group instead of to each weight, which differs
+ * from the dequantised form by at most half an fp16 step per weight.
  */
 #ifndef VQMOE_H_
 #define VQMOE_H_
@@ -125,7 +128,12 @@ VQMOE_API size_t vqmoe_switch_linear_workspace_size(const vqmoe_linear *w,
 VQMOE_API size_t vqmoe_router_workspace_size(int32_t tokens, int32_t num_experts);
 
 /* SparseMoeBlock.__call__: out[T, H] = routed combine + gated shared expert.
- * x [T, H] bf16; out bf16 or f32 (out_dtype). */
+ * x [T, H] bf16; out bf16 or f32 (out_dtype). With a shared expert, its two
+ * kernels run on a side stream forked from `stream` (an event recorded on
+ * `stream`) and joined back before the combine, so the call is still
+ * ordered on `stream` as a whole. The side stream and its two events are
+ * created by the first such call of each host thread on each device: make
+ * that call before capturing `stream` into a CUDA graph. */
 VQMOE_API vqmoe_status vqmoe_sparse_moe_block(const vqmoe_block *blk, const void *x,
                                     int32_t tokens, void *out,
                                     int32_t out_dtype, void *workspace,
@@ -133,8 +141,9 @@ VQMOE_API vqmoe_status vqmoe_sparse_moe_block(const vqmoe_block *blk, const void
 
 /* vqmoe_sparse_moe_block that also records six caller-created CUDA events
  * (cudaEvent_t, passed as void*) on `stream`: before the router, then after
- * the router, the routed gate/up + SwiGLU, the routed down, the shared
- * expert, and the combine. For profiling; tokens <= 2048. */
+ * the router and routing sort, the routed gate/up + SwiGLU, the routed
+ * down, the join of the shared expert's side stream, and the combine. For
+ * profiling; tokens <= 2048. */
 VQMOE_API vqmoe_status vqmoe_sparse_moe_block_timed(
     const vqmoe_block *blk, const void *x, int32_t tokens, void *out,
     int32_t out_dtype, void *workspace, size_t workspace_bytes, void *stream,

@@ -34,6 +34,17 @@ def _bf16_linear(weight: torch.Tensor) -> nn.Linear:
     return lin
 
 
+def tp_reduce(part: torch.Tensor, group) -> torch.Tensor:
+    """The ranks' partial block outputs (bf16 values held in float32) summed
+    in float32 over `group`, in place, and rounded once to bf16: the
+    reference's `Reduce` (`src/knurlogic/engine/split/tensor.py:159-187`)."""
+    import torch.distributed as dist
+    if part.dtype != torch.float32:
+        raise TypeError(f"partials must be float32, got {part.dtype}")
+    dist.all_reduce(part, op=dist.ReduceOp.SUM, group=group)
+    return part.to(torch.bfloat16)
+
+
 class SharedExpert(nn.Module):
     """mlx-lm's MLP weights (`qwen3_5.py:115-117`): gate/up [I_s, H], down
     [H, I_s], bf16."""
@@ -128,11 +139,9 @@ class SparseMoeBlock(nn.Module):
         if self.sharding_group is None:
             out = torch.empty_like(x2d)
             return self.forward_into(x2d, out).reshape(shape)
-        import torch.distributed as dist
         part = torch.empty(x2d.shape, dtype=torch.float32, device=x.device)
         self.forward_into(x2d, part)
-        dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.sharding_group)
-        return part.to(torch.bfloat16).reshape(shape)
+        return tp_reduce(part, self.sharding_group).reshape(shape)
 
     # ------------------------------------------------------------------
     @classmethod
