@@ -158,6 +158,26 @@ VQMOE_API vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate,
                               int32_t top_k, void *y, void *workspace,
                               size_t workspace_bytes, void *stream);
 
+/* Size of the fixed per-device scratch of vqmoe_switch_glu_noalloc. */
+#define VQMOE_NOALLOC_SCRATCH_BYTES (4 << 20)
+
+/* vqmoe_switch_glu without a caller workspace: the workspace is a fixed
+ * VQMOE_NOALLOC_SCRATCH_BYTES array of this library on each device, so the
+ * call allocates nothing. No counterpart in the reference (MLX allocates
+ * its temporaries itself); it serves callers that cannot allocate device
+ * memory at call time, such as an FFI host with no device allocator or an
+ * allocator's out-of-memory handler. Returns VQMOE_WORKSPACE_TOO_SMALL
+ * when vqmoe_switch_glu_workspace_size(gate, down, tokens, top_k) exceeds
+ * the scratch. The first call on a device takes the scratch's address
+ * (cudaGetSymbolAddress): make it before any stream capture. Nothing in the
+ * scratch needs to start at zero. One scratch per device: calls that overlap
+ * on the same device race; the caller must order them. */
+VQMOE_API vqmoe_status vqmoe_switch_glu_noalloc(const vqmoe_linear *gate,
+                              const vqmoe_linear *up,
+                              const vqmoe_linear *down, const void *x,
+                              const int32_t *indices, int32_t tokens,
+                              int32_t top_k, void *y, void *stream);
+
 /* VQSwitchLinear.__call__ / SwitchLinear.__call__: y[T, k, OUT] bf16 with
  * y[t, s] = x_row @ W[indices[t, s]]^T. x_per_pair = 0: x is [T, IN] (one
  * row per token, shared by its k slots); 1: x is [T*k, IN] (one row per

@@ -63,6 +63,9 @@ SIGNATURES = [
     ("vqmoe_switch_glu", c_int32,
      [POINTER(Linear), POINTER(Linear), POINTER(Linear), c_void_p, c_void_p,
       c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("vqmoe_switch_glu_noalloc", c_int32,
+     [POINTER(Linear), POINTER(Linear), POINTER(Linear), c_void_p, c_void_p,
+      c_int32, c_int32, c_void_p, c_void_p]),
     ("vqmoe_switch_linear", c_int32,
      [POINTER(Linear), c_void_p, c_int32, c_void_p, c_int32, c_int32,
       c_void_p, c_void_p, c_size_t, c_void_p]),
