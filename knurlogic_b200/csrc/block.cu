@@ -155,26 +155,25 @@ struct Carve {
 // of a routed gate/up stage followed by a routed down stage.
 struct RouteWs {
     int32_t *cnt, *off, *list, *active, *rank;
-    uint32_t *zero;      // [0] gate/up counter, [1] down counter, then semaphores
+    uint32_t *zero;      // the expert kernel's control block (expert_ctl_words)
     int zero_words;
     uint32_t *szero;     // the shared expert's semaphores (zeroed on its own stream)
     int szero_words;
-    uint32_t *sem_gu, *sem_dn, *ssem_gu, *ssem_dn;
-    float *part_gu, *part_dn, *spart_gu, *spart_dn;
-    int ks_gu, ks_dn, sks_gu, sks_dn;
+    uint32_t *ssem_gu, *ssem_dn;
+    float *spart_gu, *spart_dn;
+    int sks_gu, sks_dn;
 };
 
-static void carve_route(Carve &c, RouteWs &w, int E, int P, int H, int I, int T, int Is,
-                        bool dual) {
+static void carve_route(Carve &c, RouteWs &w, int E, int P, int H, int T, int Is) {
     w.cnt = c.take<int32_t>(E);
     w.off = c.take<int32_t>(E + 1);
     w.list = c.take<int32_t>(P);
     w.active = c.take<int32_t>(E + 1);
     w.rank = c.take<int32_t>(P);
-    int rb_gu = 0, rb_dn = 0, srb_gu = 0, srb_dn = 0;
-    w.ks_gu = w.ks_dn = w.sks_gu = w.sks_dn = 1;
-    if (dual) plan_routed(E, P, H, I, &w.ks_gu, &rb_gu);
-    plan_routed(E, P, dual ? I : H, dual ? H : I, &w.ks_dn, &rb_dn);
+    w.zero_words = expert_ctl_words(E);
+    w.zero = c.take<uint32_t>(w.zero_words);
+    int srb_gu = 0, srb_dn = 0;
+    w.sks_gu = w.sks_dn = 1;
     if (Is > 0) {
         int kl = 0;
         size_t sm = 0;
@@ -183,20 +182,10 @@ static void carve_route(Carve &c, RouteWs &w, int E, int P, int H, int I, int T,
         srb_gu = (Is + 31) / 32;
         srb_dn = (H + 31) / 32;
     }
-    w.zero_words = 2 + E * rb_gu + E * rb_dn;
-    w.zero = c.take<uint32_t>(w.zero_words);
     w.szero_words = srb_gu + srb_dn;
     w.szero = w.szero_words ? c.take<uint32_t>(w.szero_words) : nullptr;
-    if (w.zero) {
-        w.sem_gu = w.zero + 2;
-        w.sem_dn = w.sem_gu + (size_t)E * rb_gu;
-        w.ssem_gu = w.szero;
-        w.ssem_dn = w.szero ? w.szero + srb_gu : nullptr;
-    }
-    const int nm = dual ? 2 : 1;
-    w.part_gu = dual && w.ks_gu > 1 ? c.take<float>((size_t)w.ks_gu * P * 2 * I) : nullptr;
-    w.part_dn = w.ks_dn > 1 ? c.take<float>((size_t)w.ks_dn * P * (dual ? H : I)) : nullptr;
-    (void)nm;
+    w.ssem_gu = w.szero;
+    w.ssem_dn = w.szero ? w.szero + srb_gu : nullptr;
     // shared expert partials: T is at most one launch of tokens
     w.spart_gu = Is > 0 && w.sks_gu > 1 ? c.take<float>((size_t)w.sks_gu * T * 2 * Is) : nullptr;
     w.spart_dn = Is > 0 && w.sks_dn > 1 ? c.take<float>((size_t)w.sks_dn * T * H) : nullptr;
@@ -227,7 +216,7 @@ static BlockWs carve_block(void *ws, const vqmoe_block *b, int T) {
     w.scores = c.take<float>(P);
     w.sgate = c.take<float>(T);
     w.x16 = b->gate.format == VQMOE_FMT_VQ_U8 ? c.take<uint16_t>((size_t)T * H) : nullptr;
-    carve_route(c, w.rt, E, P, H, I, T, Is, true);
+    carve_route(c, w.rt, E, P, H, T, Is);
     w.act = c.take<uint16_t>((size_t)P * I);
     w.act_s = c.take<uint16_t>((size_t)T * Is);
     w.ybuf = c.take<uint16_t>((size_t)P * H);
@@ -281,8 +270,7 @@ static vqmoe_status mark(cudaEvent_t *ev, int n_ev, int i, cudaStream_t st) {
 }
 
 static RoutedIO routed_io(const RouteWs &rt, int E, int k, int P, const void *x, int x_per_pair,
-                          void *out, int out_f16, const float *scale, float *part, uint32_t *sem,
-                          int ks) {
+                          void *out, int out_f16, const float *scale) {
     RoutedIO r{};
     r.cnt = rt.cnt;
     r.off = rt.off;
@@ -296,9 +284,6 @@ static RoutedIO routed_io(const RouteWs &rt, int E, int k, int P, const void *x,
     r.out = out;
     r.out_f16 = out_f16;
     r.pair_scale = scale;
-    r.part = part;
-    r.sem = sem;
-    r.ks = ks;
     return r;
 }
 
@@ -371,16 +356,14 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                             T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, rt.cnt, rt.off,
                             rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 1, st)) != VQMOE_OK) return s;
-    // gate/up + SwiGLU of the routed experts
+    // the routed experts: gate/up + SwiGLU, then down (x routing weight)
     RoutedIO r1 = routed_io(rt, E, k, P, vq_in ? (const void *)w.x16 : (const void *)x, 0, w.act,
-                            vq_dn, nullptr, rt.part_gu, rt.sem_gu, rt.ks_gu);
-    s = launch_expert_stage(&b->gate, &b->up, &r1, nullptr, rt.zero, st);
-    if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK) return s;
-    // down (x routing weight)
-    RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores, rt.part_dn, rt.sem_dn,
-                            rt.ks_dn);
-    s = launch_expert_stage(&b->down, nullptr, &r2, nullptr, rt.zero + 1, st);
-    if (s != VQMOE_OK || (s = mark(ev, n_ev, 3, st)) != VQMOE_OK) return s;
+                            vq_dn, nullptr);
+    RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores);
+    s = launch_experts(&b->gate, &b->up, &r1, &b->down, r2, rt.zero, st);
+    if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK ||
+        (s = mark(ev, n_ev, 3, st)) != VQMOE_OK)
+        return s;
     if (shared && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
         return check_launch("side stream join");
     if ((s = mark(ev, n_ev, 4, st)) != VQMOE_OK) return s;
@@ -408,7 +391,7 @@ static GluWs carve_glu(void *ws, const vqmoe_linear *first, const vqmoe_linear *
     w.x16 = first->format == VQMOE_FMT_VQ_U8 ? c.take<uint16_t>((size_t)rows_x * first->in_features)
                                              : nullptr;
     const int H = first->in_features, I = first->out_features;
-    carve_route(c, w.rt, E, P, H, I, T, 0, dual);
+    carve_route(c, w.rt, E, P, H, T, 0);
     w.act = dual ? c.take<uint16_t>((size_t)P * I) : nullptr;
     w.bytes = align_up(c.off, 256);
     return w;
@@ -547,12 +530,10 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
                               rt.zero_words, st)) != VQMOE_OK)
             return s;
         RoutedIO r1 = routed_io(rt, E, top_k, P, vq_in ? (const void *)w.x16 : (const void *)xt, 0,
-                                w.act, vq_dn, nullptr, rt.part_gu, rt.sem_gu, rt.ks_gu);
-        if ((s = launch_expert_stage(gate, up, &r1, nullptr, rt.zero, st)) != VQMOE_OK) return s;
+                                w.act, vq_dn, nullptr);
         RoutedIO r2 = routed_io(rt, E, top_k, P, w.act, 1,
-                                static_cast<uint16_t *>(y) + (size_t)t0 * top_k * H, 0, nullptr,
-                                rt.part_dn, rt.sem_dn, rt.ks_dn);
-        if ((s = launch_expert_stage(down, nullptr, &r2, nullptr, rt.zero + 1, st)) != VQMOE_OK) return s;
+                                static_cast<uint16_t *>(y) + (size_t)t0 * top_k * H, 0, nullptr);
+        if ((s = launch_experts(gate, up, &r1, down, r2, rt.zero, st)) != VQMOE_OK) return s;
     }
     return VQMOE_OK;
 }
@@ -586,8 +567,8 @@ vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x
             return s;
         RoutedIO r = routed_io(rt, E, top_k, P, vq ? (const void *)ws.x16 : (const void *)xt,
                                x_per_pair, static_cast<uint16_t *>(y) + (size_t)t0 * top_k * w->out_features,
-                               0, nullptr, rt.part_dn, rt.sem_dn, rt.ks_dn);
-        if ((s = launch_expert_stage(w, nullptr, &r, nullptr, rt.zero + 1, st)) != VQMOE_OK) return s;
+                               0, nullptr);
+        if ((s = launch_experts(nullptr, nullptr, nullptr, w, r, rt.zero, st)) != VQMOE_OK) return s;
     }
     return VQMOE_OK;
 }

@@ -6,13 +6,19 @@
 // engine/families/deepseek/heads/deepseek_v4.py:35-42, 111-130), plus the
 // shared expert's dense matmuls (qwen3_5.py:184-185).
 //
-// One persistent kernel per projection stage (fused gate/up + SwiGLU, or
-// down), two CTAs per SM. A CTA takes tiles from a global counter: a tile
-// is (routed expert, 128 or 256 output rows) or (shared expert, rows). The
-// CTA stages the tile's token rows (<= 8 at a time, fp16 for VQ) in shared
-// memory once; each of its 8 warps then computes 16 (gate/up) or 32 (down)
-// output rows over the whole K, and writes its results from registers (the
-// SwiGLU or the routing weight applied there). No split K, no partials.
+// One persistent kernel runs both projection stages of the routed experts:
+// phase 1 tiles (fused gate/up + SwiGLU: an active expert and 128 output
+// rows) and then phase 2 tiles (down, or a single switch linear: an active
+// expert and 256 output rows), two CTAs per SM, all taken in order from one
+// global counter. A phase 2 tile of expert e starts once every phase 1 tile
+// of e has finished (a per-expert count, a bounded wait), so the down tiles
+// fill the end of the gate/up phase instead of a second launch.
+//
+// A CTA stages the tile's token rows (<= 8 at a time, fp16 for VQ) in shared
+// memory once; each of its 8 warps then computes 16 (phase 1) or 32
+// (phase 2) output rows over the whole K, and writes its results from
+// registers (the SwiGLU or the routing weight applied there). No split K,
+// no partials.
 //
 // For a VQ tile each lane
 //   * streams its codes and group scales through a ring of four register
@@ -25,7 +31,7 @@
 //     weight this applies is the exact product codebook x scale; the
 //     dense decode (vqmoe_dequant) rounds that product to fp16 -- a
 //     difference below 2^-11 of each weight.
-// Dense tiles (bf16 experts, the shared expert) load A from global memory.
+// Dense tiles (bf16 experts) load A from global memory.
 //
 // Why mma.sync and registers here rather than tcgen05: at 1-64 tokens the
 // layer is bound by HBM and by the shared-memory codebook lookups (8 bytes
@@ -38,7 +44,7 @@
 // (2 wavefronts, the minimum for 256 bytes). Entry c of copy b of matrix m
 // sits at byte 256*c + 128*m + 8*b (64 KB for gate and up together), so
 // one byte permute builds a lookup address: byte 1 = the code, byte 0 =
-// the lane's copy offset.
+// the lane's copy offset. Phase 2 restages matrix slot 0 with its codebook.
 //
 // Device layout (layout.cuh): codes and scales tiled per (expert, 32 rows,
 // 256 inputs) in the order the lanes consume them, so a warp's loads are
@@ -56,11 +62,14 @@ namespace vqmoe {
 
 constexpr int kThreads = 256;               // 8 warps per CTA, 2 CTAs per SM
 constexpr int kWarps = kThreads / 32;
-constexpr int kRepBytes = 256 * 256;        // replicated codebooks (both matrices), 64 KB
+constexpr int kRepBytes = 256 * 256;        // replicated codebooks (two matrices), 64 KB
 constexpr int kWin = 2048;                  // inputs per staged activation window
 constexpr int kXStride = kWin * 2 + 32;     // bytes per staged row: B-fragment
                                             // loads of 4 rows hit 16 bank pairs
 constexpr int kXBytes = 8 * kXStride;       // 8 token rows
+constexpr int kTR1 = kWarps * 16;           // phase 1 tile: 128 rows (gate and up)
+constexpr int kTR2 = kWarps * 32;           // phase 2 tile: 256 rows
+constexpr long kWaitLimit = 1L << 21;       // bounded wait for phase 1 tiles (~4 s)
 
 struct LinearDev {
     const uint8_t *codes;      // VQ device layout (layout.cuh)
@@ -81,18 +90,13 @@ struct RoutedSet {
     const float *pair_scale;     // optional [P]: y = bf16(bf16(acc) * s)
 };
 
-struct SharedSet {
-    int present;
-    const uint16_t *x;           // [T][IN] bf16
-    const uint16_t *w0, *w1;     // [OUT][IN] bf16
-    int T, IN, OUT;
-    uint16_t *out;               // [T][OUT] bf16
-};
-
-struct TileArgs {
-    RoutedSet r;
-    SharedSet s;
-    uint32_t *work;              // tile counter (zeroed by the route kernel)
+struct PipeArgs {
+    RoutedSet s1;                // phase 1: fused gate/up (when has1)
+    RoutedSet s2;                // phase 2: down, or the one switch linear
+    int has1;
+    // [0] tile counter, [1] error flag (a wait ran out), [2 + i] finished
+    // phase 1 tiles of active expert i; zeroed by the routing kernel
+    uint32_t *ctl;
 };
 
 template <bool DUAL>
@@ -113,11 +117,6 @@ __device__ __forceinline__ uint16_t epilogue_value(float g, float u, const float
 
 __device__ __forceinline__ uint2 lds2(const uint8_t *base, uint32_t off) {
     return *reinterpret_cast<const uint2 *>(base + off);
-}
-
-// half2 of fp16 lane `hi` of a packed pair, in both halves
-__device__ __forceinline__ uint32_t bcast_half(uint32_t v, int hi) {
-    return hi ? __byte_perm(v, 0, 0x3232) : __byte_perm(v, 0, 0x1010);
 }
 
 // Codes and scales of one half chunk (8 MMA sub-steps = 128 inputs) of the
@@ -196,7 +195,7 @@ __device__ __forceinline__ void compute_half(const HalfBuf<NMAT, MT> &b, float (
     }
 }
 
-// Dense sub-steps [q0, q1) of chunk c (A from global: rows r0 and r0 + 8).
+// Dense sub-steps [0, nq) of chunk c (A from global: rows r0 and r0 + 8).
 template <int NMAT, int MT>
 __device__ __forceinline__ void dense_chunk(float (&acc)[NMAT][MT][4], const uint16_t *const (&wr)[NMAT],
                                             int IN, int c, int nq, const uint8_t *xs, int xoff) {
@@ -216,188 +215,240 @@ __device__ __forceinline__ void dense_chunk(float (&acc)[NMAT][MT][4], const uin
 }
 
 struct TileInfo {
-    int kind;       // 0 routed, 1 shared
-    int e, n, base; // routed: expert, its pair count, list offset
+    int phase;      // 1: gate/up, 2: down / single linear
+    int ai;         // index among the active experts
+    int e, n, base; // expert, its pair count, list offset
     int row0;       // first output row of the tile
 };
 
-// ----------------------------------------------------------------- kernel
-// NMAT: 2 = fused gate/up + SwiGLU, 1 = down. MT: m-tiles (16 rows) per warp.
+// 16 interleaved copies of nmat codebooks: entry c of copy b of matrix m at
+// 256c + 128m + 8b (codes >= K read zeros)
+__device__ __forceinline__ void stage_codebooks(uint8_t *cb, const LinearDev &w0, const LinearDev &w1,
+                                                int nmat) {
+    for (int i = threadIdx.x; i < nmat * 4096; i += kThreads) {
+        const int m = i >> 12, rr = i & 4095, c = rr >> 4, b = rr & 15;
+        const LinearDev &w = m == 0 ? w0 : w1;
+        uint2 v = make_uint2(0, 0);
+        if (c < w.K) v = ldg_nc_v2(w.codebook + c * 4);
+        *reinterpret_cast<uint2 *>(cb + c * 256 + m * 128 + b * 8) = v;
+    }
+}
+
+// Thread 0: wait until *count >= want (acquire), at most kWaitLimit polls
+// with a growing sleep; on running out, raise the error flag and go on.
+__device__ __noinline__ void wait_count(const uint32_t *count, uint32_t want, uint32_t *err) {
+    unsigned ns = 64;
+    for (long i = 0;; ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(count) : "memory");
+        if (v >= want) return;
+        if (i >= kWaitLimit) {
+            atomicExch(err, 1u);
+            return;
+        }
+        __nanosleep(ns);
+        if (ns < 2048) ns <<= 1;
+    }
+}
+
+// One tile of one stage: this CTA's 8 warps over rows [row0, row0 + TR) of
+// expert in.e for its in.n pairs, 8 pairs at a time.
 template <int NMAT, int MT, bool VQ>
-__global__ void __launch_bounds__(kThreads, 2) expert_tile_kernel(const TileArgs a) {
+__device__ __forceinline__ void run_tile(const RoutedSet &r, const TileInfo &in, const uint8_t *cb,
+                                         uint8_t *xs, int *s_pairs) {
     constexpr bool DUAL = NMAT == 2;
-    constexpr int TR = kWarps * 16 * MT;          // output rows per tile
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t lanebyte = (lane & 15) * 8;
+    const int IN = r.IN, OUT = r.OUT;
+    const int C = (IN + 255) >> 8;
+    const int wrow = in.row0 + warp * 16 * MT;   // this warp's first row
+    const bool active = wrow < OUT;
+    // every pointer starts at a valid base, whichever branch sets it
+    const uint8_t *ct[NMAT];
+    const uint16_t *st[NMAT];
+    const uint16_t *wr[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+        const LinearDev &w = m == 0 ? r.w0 : r.w1;
+        ct[m] = w.codes;
+        st[m] = w.scales;
+        wr[m] = w.weight;
+    }
+    if (VQ) {
+        const long long tile0 = ((long long)in.e * ((OUT + 31) >> 5) + (wrow >> 5)) * C;
+        const int mt0 = (wrow >> 4) & 1;          // MT == 1: which half of the 32 rows
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            const LinearDev &w = m == 0 ? r.w0 : r.w1;
+            ct[m] = w.codes + tile0 * 2048 + mt0 * 512 + lane * 8;
+            st[m] = w.scales + tile0 * 128 + mt0 * 32 + 2 * g;
+        }
+    } else {
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            const LinearDev &w = m == 0 ? r.w0 : r.w1;
+            wr[m] = w.weight + (size_t)in.e * OUT * IN + (size_t)(wrow + g) * IN + 4 * t;
+        }
+    }
+    const int span = VQ ? C << 8 : IN;
+    for (int tb0 = 0; tb0 < in.n; tb0 += 8) {
+        const int nt = min(8, in.n - tb0);
+        __syncthreads();                          // the previous block's epilogue read s_pairs
+        if (tid < 8) s_pairs[tid] = tid < nt ? r.list[in.base + tb0 + tid] : -1;
+        float acc[NMAT][MT][4];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[m][mt][i] = 0.0f;
+        HalfBuf<NMAT, MT> hb[4];
+        const int nh = 2 * C;
+        if (VQ && active) {
+            load_half<NMAT, MT>(hb[0], ct, st, 0);
+            if (nh > 1) load_half<NMAT, MT>(hb[1], ct, st, 1);
+            if (nh > 2) load_half<NMAT, MT>(hb[2], ct, st, 2);
+        }
+        for (int w0 = 0; w0 < span; w0 += kWin) {
+            const int wend = min(w0 + kWin, span);
+            __syncthreads();                      // previous window fully read; s_pairs written
+            {
+                // stage the pairs' rows (16 bytes per copy; zero past IN). A
+                // slot without a pair keeps stale finite data: its B column
+                // only feeds outputs that are never written.
+                const int nv = (wend - w0) >> 3;
+                for (int rr = 0; rr < nt; ++rr) {
+                    const int p = s_pairs[rr];
+                    const int xr = r.x_per_pair ? p : p / r.k;
+                    const uint16_t *row = r.x + (size_t)xr * IN;
+                    uint8_t *dst = xs + rr * kXStride;
+                    for (int j = tid; j < nv; j += kThreads) {
+                        const int f = w0 + 8 * j;
+                        const bool ok = f < IN;
+                        cp_async16(smem_u32(dst + j * 16), row + (ok ? f : 0), ok ? 16 : 0);
+                    }
+                }
+                cp_async_wait_all();
+            }
+            __syncthreads();
+            if (!active) continue;
+            const int c0 = w0 >> 8, c1 = (wend + 255) >> 8;
+            if (VQ) {
+                // chunks in pairs: halves 2c .. 2c+3 in hb[0..3]; the loads
+                // run three halves ahead (a ring of four buffers)
+                for (int c = c0; c < c1; c += 2) {
+                    const int h0 = 2 * c;
+                    const int xoff = g * kXStride + (((c - c0) << 8) + 4 * t) * 2;
+                    if (h0 + 3 < nh) load_half<NMAT, MT>(hb[3], ct, st, h0 + 3);
+                    compute_half<NMAT, MT>(hb[0], acc, cb, lanebyte, xs, xoff);
+                    if (h0 + 4 < nh) load_half<NMAT, MT>(hb[0], ct, st, h0 + 4);
+                    compute_half<NMAT, MT>(hb[1], acc, cb, lanebyte, xs, xoff + 256);
+                    if (h0 + 2 < nh) {
+                        if (h0 + 5 < nh) load_half<NMAT, MT>(hb[1], ct, st, h0 + 5);
+                        compute_half<NMAT, MT>(hb[2], acc, cb, lanebyte, xs, xoff + 512);
+                        if (h0 + 6 < nh) load_half<NMAT, MT>(hb[2], ct, st, h0 + 6);
+                        compute_half<NMAT, MT>(hb[3], acc, cb, lanebyte, xs, xoff + 768);
+                    }
+                }
+            } else {
+                for (int c = c0; c < c1; ++c) {
+                    const int nq = min(16, (IN - (c << 8)) >> 4);
+                    const int xoff = g * kXStride + (((c - c0) << 8) + 4 * t) * 2;
+                    dense_chunk<NMAT, MT>(acc, wr, IN, c, nq, xs, xoff);
+                }
+            }
+        }
+        // ---- results of this block's pairs for this warp's rows
+        if (active) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int tk = 2 * t + (i & 1);
+                    const int row = wrow + mt * 16 + g + (i >> 1) * 8;
+                    const int p = s_pairs[tk];
+                    if (p < 0 || row >= OUT) continue;
+                    r.out[(size_t)p * OUT + row] = epilogue_value<DUAL>(
+                        acc[0][mt][i], acc[NMAT - 1][mt][i], r.pair_scale, p, r.out_f16);
+                }
+        }
+    }
+}
+
+// ----------------------------------------------------------------- kernel
+// Tile `tile` of phase 1 (tile < n1) or phase 2: its expert and rows.
+__device__ __forceinline__ TileInfo tile_info(const RoutedSet &r, int tile, int n1, int rt1, int rt2) {
+    TileInfo in;
+    const bool p1 = tile < n1;
+    const int u = p1 ? tile : tile - n1;
+    const int rt = p1 ? rt1 : rt2;
+    in.phase = p1 ? 1 : 2;
+    in.ai = u / rt;
+    in.e = r.active[in.ai];
+    in.n = r.cnt[in.e];
+    in.base = r.off[in.e];
+    in.row0 = (u - in.ai * rt) * (p1 ? kTR1 : kTR2);
+    return in;
+}
+
+// VQ1 / VQ2: phase 1 / phase 2 weights are VQ (else dense bf16). A CTA runs
+// the phase 1 tiles it takes, then (one codebook restage) phase 2 tiles.
+template <bool VQ1, bool VQ2>
+__global__ void __launch_bounds__(kThreads, 2) expert_kernel(const PipeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ TileInfo s_info;
     __shared__ int s_next;
     __shared__ int s_pairs[8];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, t = lane & 3;
+    const int tid = threadIdx.x;
     uint8_t *cb = smem;
-    uint8_t *xs = smem + (VQ ? kRepBytes : 0);
-    if (VQ) {
-        // 16 interleaved copies: entry c of copy b of matrix m at 256c + 128m + 8b
-        for (int i = tid; i < NMAT * 256 * 16; i += kThreads) {
-            const int m = i >> 12, rr = i & 4095, c = rr >> 4, b = rr & 15;
-            const LinearDev &w = m == 0 ? a.r.w0 : a.r.w1;
-            uint2 v = make_uint2(0, 0);
-            if (c < w.K) v = *reinterpret_cast<const uint2 *>(w.codebook + c * 4);
-            *reinterpret_cast<uint2 *>(smem + c * 256 + m * 128 + b * 8) = v;
+    uint8_t *xs = smem + ((VQ1 || VQ2) ? kRepBytes : 0);
+    const int nact = a.s2.active[a.s2.E];
+    const int rt1 = a.has1 ? (a.s1.OUT + kTR1 - 1) / kTR1 : 0;
+    const int rt2 = (a.s2.OUT + kTR2 - 1) / kTR2;
+    const int n1 = nact * rt1, n2 = nact * rt2;
+    if (tid == 0) s_next = (int)atomicAdd(a.ctl, 1u);
+    __syncthreads();
+    // ---- phase 1: gate/up + SwiGLU
+    if (s_next < n1) {
+        if (VQ1) stage_codebooks(cb, a.s1.w0, a.s1.w1, 2);
+        for (;;) {
+            const int tile = s_next;
+            if (tile >= n1) break;
+            __syncthreads();                      // everyone has read s_next; codebooks staged
+            if (tid == 0) {
+                s_info = tile_info(a.s2, tile, n1, rt1, rt2);
+                s_next = (int)atomicAdd(a.ctl, 1u);
+            }
+            __syncthreads();
+            const TileInfo in = s_info;
+            run_tile<2, 1, VQ1>(a.s1, in, cb, xs, s_pairs);
+            __syncthreads();                      // every warp's outputs are stored
+            if (tid == 0) {
+                __threadfence();
+                atomicAdd(a.ctl + 2 + in.ai, 1u);
+            }
         }
     }
-    const uint32_t lanebyte = (lane & 15) * 8;
-    const int rt_r = (a.r.OUT + TR - 1) / TR;     // tiles per routed expert
-    const int n_shared = 0;   // the shared expert runs in shared_dense_kernel
-    const int n_routed = a.r.active ? a.r.active[a.r.E] * rt_r : 0;
-    if (tid == 0) s_next = (int)atomicAdd(a.work, 1u);
-    __syncthreads();
+    // ---- phase 2: down (x routing weight), or the single linear
+    if (s_next >= n1 + n2) return;
+    __syncthreads();                              // phase 1 done with cb
+    if (VQ2) stage_codebooks(cb, a.s2.w0, a.s2.w0, 1);
     for (;;) {
         const int tile = s_next;
-        if (tile >= n_shared + n_routed) break;
-        __syncthreads();                          // everyone has read s_next
+        if (tile >= n1 + n2) break;
+        __syncthreads();                          // everyone has read s_next; codebook staged
         if (tid == 0) {
-            TileInfo in;
-            if (tile < n_shared) {
-                in.kind = 1;
-                in.e = 0;
-                in.n = a.s.T;
-                in.base = 0;
-                in.row0 = tile * TR;
-            } else {
-                const int u = tile - n_shared;
-                const int ai = u / rt_r;
-                in.kind = 0;
-                in.e = a.r.active[ai];
-                in.n = a.r.cnt[in.e];
-                in.base = a.r.off[in.e];
-                in.row0 = (u - ai * rt_r) * TR;
-            }
+            const TileInfo in = tile_info(a.s2, tile, n1, rt1, rt2);
+            // phase 2 reads what every phase 1 tile of this expert wrote;
+            // those tiles were all taken before this one, by running CTAs
+            if (a.has1) wait_count(a.ctl + 2 + in.ai, (uint32_t)rt1, a.ctl + 1);
             s_info = in;
-            s_next = (int)atomicAdd(a.work, 1u);  // the next tile, read after this one
+            s_next = (int)atomicAdd(a.ctl, 1u);
         }
         __syncthreads();
         const TileInfo in = s_info;
-        const bool shared = false;
-        const int IN = shared ? a.s.IN : a.r.IN, OUT = shared ? a.s.OUT : a.r.OUT;
-        const int C = (IN + 255) >> 8;
-        const int wrow = in.row0 + warp * 16 * MT;   // this warp's first row
-        const bool active = wrow < OUT;
-        // VQ codes / scales of this warp's rows: 32-row block rb, m-tile offset
-        // every pointer starts at a valid base, whichever branch sets it
-        const uint8_t *ct[NMAT];
-        const uint16_t *st[NMAT];
-        const uint16_t *wr[NMAT];
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-            ct[m] = VQ ? a.r.w0.codes : nullptr;
-            st[m] = VQ ? a.r.w0.scales : nullptr;
-            wr[m] = a.s.present ? a.s.w0 : a.r.w0.weight;
-        }
-        if (VQ && !shared) {
-            const long long tile0 = ((long long)in.e * ((OUT + 31) >> 5) + (wrow >> 5)) * C;
-            const int mt0 = (wrow >> 4) & 1;      // MT == 1: which half of the 32 rows
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                const LinearDev &w = m == 0 ? a.r.w0 : a.r.w1;
-                ct[m] = w.codes + tile0 * 2048 + mt0 * 512 + lane * 8;
-                st[m] = w.scales + tile0 * 128 + mt0 * 32 + 2 * g;
-            }
-        } else {
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                const uint16_t *base = shared ? (m == 0 ? a.s.w0 : a.s.w1)
-                                              : (m == 0 ? a.r.w0.weight : a.r.w1.weight) +
-                                                    (size_t)in.e * OUT * IN;
-                wr[m] = base + (size_t)(wrow + g) * IN + 4 * t;
-            }
-        }
-        for (int tb0 = 0; tb0 < in.n; tb0 += 8) {
-            const int nt = min(8, in.n - tb0);
-            __syncthreads();                      // the previous block's epilogue read s_pairs
-            if (tid < 8) s_pairs[tid] = tid < nt ? (shared ? tb0 + tid : a.r.list[in.base + tb0 + tid]) : -1;
-            float acc[NMAT][MT][4];
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) acc[m][mt][i] = 0.0f;
-            HalfBuf<NMAT, MT> hb[4];
-            const int nh = 2 * C;
-            if (VQ && !shared && active) {
-                load_half<NMAT, MT>(hb[0], ct, st, 0);
-                if (nh > 1) load_half<NMAT, MT>(hb[1], ct, st, 1);
-                if (nh > 2) load_half<NMAT, MT>(hb[2], ct, st, 2);
-            }
-            for (int w0 = 0; w0 < (VQ && !shared ? C << 8 : IN); w0 += kWin) {
-                const int wend = min(w0 + kWin, VQ && !shared ? C << 8 : IN);
-                __syncthreads();                  // previous window fully read; s_pairs written
-                {
-                    // stage rows 0..7 (zero past nt and past IN), 16 bytes per copy
-                    const int nv = (wend - w0) >> 3;
-                    for (int v = tid; v < 8 * nv; v += kThreads) {
-                        const int r = v / nv, j = v - r * nv;
-                        const int f = w0 + 8 * j;
-                        const int p = s_pairs[r];
-                        const uint16_t *src;
-                        bool ok = p >= 0 && f < IN;
-                        if (shared) {
-                            src = a.s.x + (size_t)(ok ? p : 0) * IN + f;
-                        } else {
-                            const int xr = p < 0 ? 0 : (a.r.x_per_pair ? p : p / a.r.k);
-                            src = a.r.x + (size_t)xr * IN + (ok ? f : 0);
-                        }
-                        cp_async16(smem_u32(xs + r * kXStride + j * 16), src, ok ? 16 : 0);
-                    }
-                    cp_async_wait_all();
-                }
-                __syncthreads();
-                if (!active) continue;
-                const int c0 = w0 >> 8, c1 = (wend + 255) >> 8;
-                if (VQ && !shared) {
-                    // chunks in pairs: halves 2c .. 2c+3 in hb[0..3]; the loads
-                    // run three halves ahead (a ring of four buffers)
-                    for (int c = c0; c < c1; c += 2) {
-                        const int h0 = 2 * c;
-                        const int xoff = g * kXStride + (((c - c0) << 8) + 4 * t) * 2;
-                        if (h0 + 3 < nh) load_half<NMAT, MT>(hb[3], ct, st, h0 + 3);
-                        compute_half<NMAT, MT>(hb[0], acc, cb, lanebyte, xs, xoff);
-                        if (h0 + 4 < nh) load_half<NMAT, MT>(hb[0], ct, st, h0 + 4);
-                        compute_half<NMAT, MT>(hb[1], acc, cb, lanebyte, xs, xoff + 256);
-                        if (h0 + 2 < nh) {
-                            if (h0 + 5 < nh) load_half<NMAT, MT>(hb[1], ct, st, h0 + 5);
-                            compute_half<NMAT, MT>(hb[2], acc, cb, lanebyte, xs, xoff + 512);
-                            if (h0 + 6 < nh) load_half<NMAT, MT>(hb[2], ct, st, h0 + 6);
-                            compute_half<NMAT, MT>(hb[3], acc, cb, lanebyte, xs, xoff + 768);
-                        }
-                    }
-                } else {
-                    for (int c = c0; c < c1; ++c) {
-                        const int nq = min(16, (IN - (c << 8)) >> 4);
-                        const int xoff = g * kXStride + (((c - c0) << 8) + 4 * t) * 2;
-                        dense_chunk<NMAT, MT>(acc, wr, IN, c, nq, xs, xoff);
-                    }
-                }
-            }
-            // ---- results of tokens tb0 .. tb0+7 for this warp's rows
-            if (active) {
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int tk = 2 * t + (i & 1);
-                        const int row = wrow + mt * 16 + g + (i >> 1) * 8;
-                        const int p = s_pairs[tk];
-                        if (p < 0 || row >= OUT) continue;
-                        if (shared)
-                            a.s.out[(size_t)p * OUT + row] =
-                                epilogue_value<DUAL>(acc[0][mt][i], acc[NMAT - 1][mt][i], nullptr, 0, 0);
-                        else
-                            a.r.out[(size_t)p * OUT + row] = epilogue_value<DUAL>(
-                                acc[0][mt][i], acc[NMAT - 1][mt][i], a.r.pair_scale, p, a.r.out_f16);
-                    }
-            }
-        }
+        run_tile<1, 2, VQ2>(a.s2, in, cb, xs, s_pairs);
         __syncthreads();                          // done with s_pairs / xs before the next tile
     }
 }
@@ -569,12 +620,12 @@ vqmoe_status launch_shared_dense(const void *x, const void *w0, const void *w1, 
 
 // ------------------------------------------------------------------ host
 
-template <int NMAT, int MT, bool VQ>
-static vqmoe_status launch_tiles(const TileArgs &a, size_t smem, cudaStream_t stream) {
+template <bool VQ1, bool VQ2>
+static vqmoe_status launch_pipe(const PipeArgs &a, size_t smem, cudaStream_t stream) {
     static size_t configured[64] = {0};   // per device
     int dev = 0;
     cudaGetDevice(&dev);
-    auto fn = expert_tile_kernel<NMAT, MT, VQ>;
+    auto fn = expert_kernel<VQ1, VQ2>;
     if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || smem > configured[dev])) {
         if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
@@ -582,7 +633,7 @@ static vqmoe_status launch_tiles(const TileArgs &a, size_t smem, cudaStream_t st
         if (dev >= 0 && dev < 64) configured[dev] = smem;
     }
     fn<<<2 * sm_count(), kThreads, smem, stream>>>(a);
-    return check_launch("expert_tile_kernel");
+    return check_launch("expert_kernel");
 }
 
 static LinearDev dev_of(const vqmoe_linear *w) {
@@ -595,54 +646,40 @@ static LinearDev dev_of(const vqmoe_linear *w) {
     return d;
 }
 
-void plan_routed(int, int, int, int, int *ks, int *rb) {
-    *ks = 1;
-    *rb = 0;
+static RoutedSet set_of(const RoutedIO &r, const vqmoe_linear *w0, const vqmoe_linear *w1) {
+    RoutedSet s{};
+    s.cnt = r.cnt;
+    s.off = r.off;
+    s.list = r.list;
+    s.active = r.active;
+    s.E = r.E;
+    s.k = r.k;
+    s.P = r.P;
+    s.x_per_pair = r.x_per_pair;
+    s.x = static_cast<const uint16_t *>(r.x);
+    s.w0 = dev_of(w0);
+    s.w1 = w1 ? dev_of(w1) : s.w0;
+    s.IN = w0->in_features;
+    s.OUT = w0->out_features;
+    s.out = static_cast<uint16_t *>(r.out);
+    s.out_f16 = r.out_f16;
+    s.pair_scale = r.pair_scale;
+    return s;
 }
 
-void plan_shared(int, int, int *ks, int *rb) {
-    *ks = 1;
-    *rb = 0;
-}
-
-vqmoe_status launch_expert_stage(const vqmoe_linear *w0, const vqmoe_linear *w1, const RoutedIO *r,
-                                 const SharedIO *s, uint32_t *work, cudaStream_t stream) {
-    const bool dual = w1 != nullptr;
-    TileArgs a{};
-    a.work = work;
-    if (r) {
-        a.r.cnt = r->cnt;
-        a.r.off = r->off;
-        a.r.list = r->list;
-        a.r.active = r->active;
-        a.r.E = r->E;
-        a.r.k = r->k;
-        a.r.P = r->P;
-        a.r.x_per_pair = r->x_per_pair;
-        a.r.x = static_cast<const uint16_t *>(r->x);
-        a.r.w0 = dev_of(w0);
-        a.r.w1 = dual ? dev_of(w1) : a.r.w0;
-        a.r.IN = w0->in_features;
-        a.r.OUT = w0->out_features;
-        a.r.out = static_cast<uint16_t *>(r->out);
-        a.r.out_f16 = r->out_f16;
-        a.r.pair_scale = r->pair_scale;
-    }
-    if (s) {
-        a.s.present = 1;
-        a.s.x = static_cast<const uint16_t *>(s->x);
-        a.s.w0 = static_cast<const uint16_t *>(s->w0);
-        a.s.w1 = static_cast<const uint16_t *>(dual ? s->w1 : s->w0);
-        a.s.T = s->T;
-        a.s.IN = s->IN;
-        a.s.OUT = s->OUT;
-        a.s.out = static_cast<uint16_t *>(s->out);
-    }
-    const bool vq = r && w0->format == VQMOE_FMT_VQ_U8;
-    const size_t smem = (vq ? (size_t)kRepBytes : 0) + (size_t)kXBytes;
-    if (dual)
-        return vq ? launch_tiles<2, 1, true>(a, smem, stream) : launch_tiles<2, 1, false>(a, smem, stream);
-    return vq ? launch_tiles<1, 2, true>(a, smem, stream) : launch_tiles<1, 2, false>(a, smem, stream);
+vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,
+                            const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl,
+                            cudaStream_t stream) {
+    PipeArgs a{};
+    a.ctl = ctl;
+    a.has1 = r1 != nullptr;
+    a.s2 = set_of(r2, w2, nullptr);
+    a.s1 = r1 ? set_of(*r1, gate, up) : a.s2;
+    const bool vq2 = w2->format == VQMOE_FMT_VQ_U8;
+    const bool vq1 = r1 ? gate->format == VQMOE_FMT_VQ_U8 : vq2;
+    const size_t smem = (vq1 || vq2 ? (size_t)kRepBytes : 0) + (size_t)kXBytes;
+    if (vq1) return vq2 ? launch_pipe<true, true>(a, smem, stream) : launch_pipe<true, false>(a, smem, stream);
+    return vq2 ? launch_pipe<false, true>(a, smem, stream) : launch_pipe<false, false>(a, smem, stream);
 }
 
 }  // namespace vqmoe

@@ -28,28 +28,17 @@ struct RoutedIO {
     void *out;              // [P][OUT]
     int out_f16;            // fp16 (saturated) output instead of bf16
     const float *pair_scale;
-    float *part;            // [ks][P][NMAT][OUT] when ks > 1
-    uint32_t *sem;          // [E][row blocks]
-    int ks;
 };
 
-// The shared expert of one stage: dense bf16, every token.
-struct SharedIO {
-    const void *x;          // [T][IN] bf16
-    const void *w0, *w1;    // [OUT][IN] bf16
-    int T, IN, OUT;
-    void *out;              // [T][OUT] bf16
-    float *part;            // [ks][T][NMAT][OUT] when ks > 1
-    uint32_t *sem;          // [row blocks]
-    int ks;
-};
+// Words of the expert kernel's control block: tile counter, error flag, and
+// one finished-tile count per expert. Zeroed by the routing kernel.
+inline int expert_ctl_words(int E) { return 2 + E; }
 
-vqmoe_status launch_expert_stage(const vqmoe_linear *w0, const vqmoe_linear *w1, const RoutedIO *r,
-                                 const SharedIO *s, uint32_t *work, cudaStream_t stream);
-// K slices and 32-row blocks of a routed stage; K slices and 16-row blocks
-// of a shared stage.
-void plan_routed(int E, int P, int IN, int OUT, int *ks, int *rb);
-void plan_shared(int IN, int OUT, int *ks, int *rb);
+// The routed experts of a layer in one launch: phase 1 = gate/up + SwiGLU
+// (r1, may be null), then phase 2 = w2 (down, or the only linear) on r2.
+vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,
+                            const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl,
+                            cudaStream_t stream);
 // The shared expert's dense matmul (+ SwiGLU when w1 is set): K slicing,
 // its partial buffer [ks][T][nmat][OUT] float and [ceil(OUT/32)] semaphores.
 void plan_shared_dense(int IN, int OUT, int nmat, int *ks, int *kslice, size_t *smem);
