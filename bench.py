@@ -46,10 +46,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "VQ-MoE layer tokens/s"
 UNIT = "tokens/s"
-GATEUP_KERNEL = "expert_tile_kernel<2,1,true>"
+EXPERT_KERNEL = "expert_kernel<true,true>"
 # kernels of one block call: router logits, top-k + routing sort, shared
-# gate/up, shared down, routed gate/up, routed down, combine
-LAUNCHES_PER_STEP = 7
+# gate/up, shared down, routed experts (both stages), combine
+LAUNCHES_PER_STEP = 6
 
 
 def parse():
@@ -275,14 +275,15 @@ def run_ours(args, world, rank, local):
     peak, peak_kind = peaks()
     roof = None
     if stage:
-        gu_bytes = stage["gateup_bytes"]
-        achieved = gu_bytes / (stage["gateup_ms"] / 1e3) / 1e9
-        traffic = traffic_from_profiles(GATEUP_KERNEL, workload)
-        roof = {"bound": "hbm", "kernel": "fused VQ gate/up + SwiGLU of the routed experts",
+        ex_bytes = stage["experts_bytes"]
+        achieved = ex_bytes / (stage["experts_ms"] / 1e3) / 1e9
+        traffic = traffic_from_profiles(EXPERT_KERNEL, workload)
+        roof = {"bound": "hbm",
+                "kernel": "routed experts: VQ gate/up + SwiGLU, then VQ down x routing weight",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "kernel_name": GATEUP_KERNEL,
+                "kernel_name": EXPERT_KERNEL,
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                "algorithmic_bytes_per_launch": int(gu_bytes),
+                "algorithmic_bytes_per_launch": int(ex_bytes),
                 "traffic": traffic,
                 "layer_achieved_gbs": round(stage["layer_bytes"] / (stage["layer_ms"] / 1e3) / 1e9, 1),
                 "layer_frac": round(stage["layer_bytes"] / (stage["layer_ms"] / 1e3) / 1e9 / peak, 4)}
@@ -323,7 +324,7 @@ def stage_profile(blocks, x, cfg, dev, args, world):
     T = x.shape[0]
     L = len(blocks)
     n = min(args.steps, 500)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(n)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(n)]
     out = torch.empty(T, cfg.hidden, dtype=torch.float32 if world > 1 else torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
     for row in evs:                      # create the events
@@ -335,20 +336,20 @@ def stage_profile(blocks, x, cfg, dev, args, world):
     odt = _lib.OUT_F32 if world > 1 else _lib.OUT_BF16
     for i in range(n):
         b = i % L
-        arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in evs[i]])
+        arr = (ctypes.c_void_p * 5)(*[e.cuda_event for e in evs[i]])
         _lib.call("vqmoe_sparse_moe_block_timed", ctypes.byref(descs[b]), x.data_ptr(), T,
                   out.data_ptr(), odt, wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream,
-                  arr, 6)
+                  arr, 5)
     torch.cuda.synchronize(dev)
-    # events: start | router + routing sort | routed gate/up | routed down |
+    # events: start | router + routing sort | routed experts (both stages) |
     # join of the shared expert's side stream | combine
-    names = ["router_ms", "gateup_ms", "down_ms", "shared_wait_ms", "combine_ms"]
+    names = ["router_ms", "experts_ms", "shared_wait_ms", "combine_ms"]
     acc = {k: 0.0 for k in names}
     lay = 0.0
     for row in evs[min(10, n - 1):]:
         for j, k in enumerate(names):
             acc[k] += row[j].elapsed_time(row[j + 1])
-        lay += row[0].elapsed_time(row[5])
+        lay += row[0].elapsed_time(row[4])
     m = len(evs[min(10, n - 1):])
     st = {k: v / m for k, v in acc.items()}
     st["layer_ms"] = lay / m
@@ -358,10 +359,12 @@ def stage_profile(blocks, x, cfg, dev, args, world):
     D = len(set(inds))
     H, I, k = cfg.hidden, cfg.inter // world, cfg.top_k
     per = 2 * (I * H // cfg.dim + 2 * I * H // cfg.group)
-    # routed gate/up launch: codes + scales of the D experts touched, the two
-    # codebooks, x (its fp16 copy), the SwiGLU activations out
-    st["gateup_bytes"] = (D * per + 2 * cfg.codebook_size * cfg.dim * 2 + T * H * 2
-                          + T * k * I * 2)
+    # routed-expert launch: codes + scales of the D experts touched (gate,
+    # up and down), the three codebooks, x (its fp16 copy) in, the weighted
+    # expert outputs [T*k, H] out (the SwiGLU activations between the two
+    # stages stay in L2)
+    st["experts_bytes"] = (D * per * 3 // 2 + 3 * cfg.codebook_size * cfg.dim * 2 + T * H * 2
+                           + T * k * H * 2)
     c2 = synth.MoEConfig("x", cfg.experts, cfg.top_k, H, I, cfg.shared_inter // world, T)
     st["layer_bytes"] = synth.algorithmic_bytes(c2, D)
     return st, D

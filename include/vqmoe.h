@@ -139,11 +139,11 @@ VQMOE_API vqmoe_status vqmoe_sparse_moe_block(const vqmoe_block *blk, const void
                                     int32_t out_dtype, void *workspace,
                                     size_t workspace_bytes, void *stream);
 
-/* vqmoe_sparse_moe_block that also records six caller-created CUDA events
+/* vqmoe_sparse_moe_block that also records five caller-created CUDA events
  * (cudaEvent_t, passed as void*) on `stream`: before the router, then after
- * the router and routing sort, the routed gate/up + SwiGLU, the routed
- * down, the join of the shared expert's side stream, and the combine. For
- * profiling; tokens <= 2048. */
+ * the router and routing sort, the routed experts (gate/up + SwiGLU and
+ * down, one launch), the join of the shared expert's side stream, and the
+ * combine. For profiling; tokens <= 2048. */
 VQMOE_API vqmoe_status vqmoe_sparse_moe_block_timed(
     const vqmoe_block *blk, const void *x, int32_t tokens, void *out,
     int32_t out_dtype, void *workspace, size_t workspace_bytes, void *stream,

@@ -361,17 +361,15 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                             vq_dn, nullptr);
     RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores);
     s = launch_experts(&b->gate, &b->up, &r1, &b->down, r2, rt.zero, st);
-    if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK ||
-        (s = mark(ev, n_ev, 3, st)) != VQMOE_OK)
-        return s;
+    if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK) return s;
     if (shared && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
         return check_launch("side stream join");
-    if ((s = mark(ev, n_ev, 4, st)) != VQMOE_OK) return s;
+    if ((s = mark(ev, n_ev, 3, st)) != VQMOE_OK) return s;
     const size_t nvec = (size_t)T * (H / 8);
     const int grid = (int)std::min<size_t>((nvec + 255) / 256, (size_t)sm_count() * 8);
     combine_kernel<<<grid, 256, 0, st>>>(w.ybuf, T, k, H, shared ? w.sh : nullptr, w.sgate, out, out_f32);
     if ((s = check_launch("combine_kernel")) != VQMOE_OK) return s;
-    return mark(ev, n_ev, 5, st);
+    return mark(ev, n_ev, 4, st);
 }
 
 // Workspace of vqmoe_switch_glu / vqmoe_switch_linear at T tokens.
@@ -488,8 +486,8 @@ vqmoe_status vqmoe_sparse_moe_block_timed(const vqmoe_block *blk, const void *x,
                                           void *out, int32_t out_dtype, void *workspace,
                                           size_t workspace_bytes, void *stream,
                                           void *const *events, int32_t n_events) {
-    if (!events || n_events < 6)
-        return set_error(VQMOE_BAD_POINTER, "timed block: needs 6 events");
+    if (!events || n_events < 5)
+        return set_error(VQMOE_BAD_POINTER, "timed block: needs 5 events");
     if (tokens > kMaxTokensPerLaunch)
         return set_error(VQMOE_BAD_SHAPE, "timed block: at most %d tokens", kMaxTokensPerLaunch);
     return block_impl(blk, x, tokens, out, out_dtype, workspace, workspace_bytes, stream,
