@@ -10,11 +10,16 @@ HBM GB/s as a fraction of the measured roofline.
 
 A step is one call of the Qwen3.5-MoE sparse block (router, fused VQ
 gate/up + SwiGLU, VQ down, shared expert, combine) over one batch of
-synthetic tokens. N = 1 runs configuration c2 (H 2048, 128 experts top-8,
-I 768 + shared 768, 64 tokens = 16 sequences x (1 + 3 MTP drafts)). N > 1
-runs c4 (H 4096, 256 experts top-8, I 1536, 256 tokens) tensor-split N
-ways: gate/up cut on I, down on I, float32 partials all-reduced over NCCL
-(strong scaling: the layer is fixed, each rank holds 1/N of it).
+synthetic tokens, configuration c2 (H 2048, 128 experts top-8, I 768 +
+shared 768, 64 tokens = 16 sequences x (1 + 3 MTP drafts)) at every N, so
+that the scaling run compares like with like. By default the N GPUs run N
+independent replicas of the layer, each on its own 64 tokens (tokens are
+independent: no collective on the data path; weak scaling). `--tp S`
+tensor-splits the layer S ways instead (gate/up cut on I, down on I,
+float32 partials all-reduced over NCCL), as far as the reference's cut
+rules allow -- c2's I = 768 allows 2 and 4 -- with N / S replicas of the
+split. `--workload c4` (H 4096, 256 experts top-8, I 1536, 256 tokens) is
+the tensor-split block the baseline names for 2/4/8 GPUs.
 
 Inputs larger than L2: the timed loop cycles over several independently
 seeded copies of the layer (> 3x the 126 MB L2 in total), so every step
@@ -60,6 +65,8 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor split of the layer (N / tp independent replicas)")
     return ap.parse_args()
 
 
@@ -163,29 +170,34 @@ def run_ours(args, world, rank, local):
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    group = None
-    if world > 1:
-        group = dist.group.WORLD
-    workload = args.workload or ("c2" if world == 1 else "c4")
+    workload = args.workload or "c2"
     cfg = synth.CONFIGS[workload]
     T = cfg.tokens
+    tp, dp = split_plan(cfg, world, args.tp)
+    # tensor-split groups of tp consecutive ranks; each group (a data-parallel
+    # replica) runs the layer on its own batch of tokens
+    group = None
+    if tp > 1:
+        groups = [dist.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(dp)]
+        group = groups[rank // tp]
+    tp_rank, replica = rank % tp, rank // tp
 
     # copies of the layer: > 3x L2 of weights streamed per cycle
-    per_layer = synth.algorithmic_bytes(cfg, cfg.experts) / world
+    per_layer = synth.algorithmic_bytes(cfg, cfg.experts) / tp
     L = max(2, min(16, math.ceil(3 * 126e6 / per_layer) + 1))
     blocks = []
     for i in range(L):
         w = synth.make_weights(cfg, seed=100 + i, device=dev, scales="ones")
-        blocks.append(tensor_split.build_block(w, cfg.top_k, rank=rank, n=world, group=group))
+        blocks.append(tensor_split.build_block(w, cfg.top_k, rank=tp_rank, n=tp, group=group))
         del w
-    x = synth.make_input(cfg, seed=7, device=dev)
+    x = synth.make_input(cfg, seed=7 + replica, device=dev)
     # one graph per layer copy: block (+ all-reduce under a split)
     outs = [torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device=dev) for _ in range(L)]
     parts = [torch.empty(T, cfg.hidden, dtype=torch.float32, device=dev) for _ in range(L)]
 
     def step(i):
         b = blocks[i]
-        if world == 1:
+        if tp == 1:
             b.forward_into(x, outs[i])
         else:
             b.forward_into(x, parts[i])
@@ -233,13 +245,13 @@ def run_ours(args, world, rank, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    value = T * args.steps / (ms / 1e3)
+    value = T * dp * args.steps / (ms / 1e3)
 
     # ---- stage times of the block (events between its kernels), rank 0
     stage = None
     inds_count = None
     if rank == 0:
-        stage, inds_count = stage_profile(blocks, x, cfg, dev, args, world)
+        stage, inds_count = stage_profile(blocks, x, cfg, dev, args, tp)
 
     # ---- end to end through the public captured call, host buffers
     xh = x.cpu().pin_memory()
@@ -262,7 +274,7 @@ def run_ours(args, world, rank, local):
         t = torch.tensor([ems], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ems = float(t.item())
-    e2e = {"value": T * args.steps / (ems / 1e3), "unit": UNIT,
+    e2e = {"value": T * dp * args.steps / (ems / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": xh.numel() * xh.element_size(),
            "d2h_bytes_per_step": yh.numel() * yh.element_size()}
     del cap
@@ -293,13 +305,14 @@ def run_ours(args, world, rank, local):
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "higher_is_better": True, "scaling": "weak" if dp > 1 or world == 1 else "strong",
         "vs_baseline": None, "dtype": "vq-u8 codes / fp16 dequant / bf16 io",
         "data": "synthetic (seeded; uniform codes, N(0,0.02) codebooks, N(0,1) tokens)",
         "config": {"workload": workload, "tokens": T, "hidden": cfg.hidden,
                    "experts": cfg.experts, "top_k": cfg.top_k, "inter": cfg.inter,
                    "shared_inter": cfg.shared_inter, "codebook": f"{cfg.codebook_size}x{cfg.dim} fp16",
-                   "group": cfg.group, "tensor_parallel": world, "layer_copies": L,
+                   "group": cfg.group, "tensor_parallel": tp, "replicas": dp,
+                   "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""), "layer_copies": L,
                    "l2": "inputs larger than L2 (layer copies cycled)",
                    "distinct_experts": inds_count},
         "roofline": roof,
@@ -310,6 +323,25 @@ def run_ours(args, world, rank, local):
         "clocks": clocks.record(),
     }
     return line
+
+
+def split_plan(cfg, world, tp=1):
+    """(tensor split, replicas) for `world` GPUs: the requested split of the
+    layer (at most the largest power-of-two split that the reference's cut
+    rules allow), times independent replicas of that split, each on its own
+    tokens."""
+    from knurlogic_b200 import tensor_split
+    shapes = {"mlp.switch_mlp.gate_proj.codes": (cfg.experts, cfg.inter, cfg.hidden // 4),
+              "mlp.switch_mlp.up_proj.codes": (cfg.experts, cfg.inter, cfg.hidden // 4),
+              "mlp.switch_mlp.down_proj.codes": (cfg.experts, cfg.hidden, cfg.inter // 4),
+              "mlp.switch_mlp.down_proj.vq_scales": (cfg.experts, cfg.hidden, cfg.inter // cfg.group)}
+    if cfg.shared_inter:
+        shapes["mlp.shared_expert.gate_proj.weight"] = (cfg.shared_inter, cfg.hidden)
+        shapes["mlp.shared_expert.down_proj.weight"] = (cfg.hidden, cfg.shared_inter)
+    tp = max(1, min(tp, world))
+    while tp > 1 and (world % tp or tensor_split.refusals(shapes, tp)):
+        tp //= 2
+    return tp, world // tp
 
 
 def stage_profile(blocks, x, cfg, dev, args, world):
@@ -429,8 +461,9 @@ def run_reference(args, world, rank):
 
     from knurlogic_b200 import synth
     from oracle import cpu_baseline as C
-    workload = args.workload or ("c2" if world == 1 else "c4")
+    workload = args.workload or "c2"
     cfg = synth.CONFIGS[workload]
+    tp, dp = split_plan(cfg, world, args.tp)
     x, p = _oracle_inputs(cfg)
     n = C.threads()
     from oracle import moe_ref as R
@@ -462,9 +495,9 @@ def run_reference(args, world, rank):
     return {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1e3 * secs / args.steps, 3), "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "scaling": "weak" if dp > 1 or world == 1 else "strong", "vs_baseline": None,
             "dtype": "vq-u8 codes / fp16 dequant / bf16 io", "data": "synthetic (seeded)",
-            "config": {"workload": workload, "tokens": cfg.tokens, "tensor_parallel": world},
+            "config": {"workload": workload, "tokens": cfg.tokens, "tensor_parallel": tp, "replicas": dp},
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": n, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
