@@ -55,12 +55,16 @@
 // codebook entry (A) and the activation quad (B) are single 8-byte loads.
 #include <algorithm>
 
+#include "experts.cuh"
 #include "layout.cuh"
 #include "stages.cuh"
 
 namespace vqmoe {
 
 constexpr int kThreads = 256;               // 8 warps per CTA, 2 CTAs per SM
+// average pairs per expert from which the routed experts take the tcgen05
+// prefill path (expert_prefill.cu) instead of the mma.sync decode path
+constexpr int kPrefillPairsPerExpert = 32;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRepBytes = 256 * 256;        // replicated codebooks (two matrices), 64 KB
 constexpr int kWin = 2048;                  // inputs per staged activation window
@@ -70,50 +74,6 @@ constexpr int kXBytes = 8 * kXStride;       // 8 token rows
 constexpr int kTR1 = kWarps * 16;           // phase 1 tile: 128 rows (gate and up)
 constexpr int kTR2 = kWarps * 32;           // phase 2 tile: 256 rows
 constexpr long kWaitLimit = 1L << 21;       // bounded wait for phase 1 tiles (~4 s)
-
-struct LinearDev {
-    const uint8_t *codes;      // VQ device layout (layout.cuh)
-    const uint16_t *codebook;  // [K][4] fp16 bits
-    const uint16_t *scales;    // VQ device layout (layout.cuh), fp16 bits
-    const uint16_t *weight;    // dense [E][OUT][IN] bf16 bits
-    int K;
-};
-
-struct RoutedSet {
-    const int32_t *cnt, *off, *list, *active;  // routing; active[E] = #active
-    int E, k, x_per_pair, P;
-    const uint16_t *x;           // input rows: fp16 (VQ) or bf16 (dense)
-    LinearDev w0, w1;            // w1: up_proj of the fused gate/up stage
-    int IN, OUT;
-    uint16_t *out;               // [P][OUT]
-    int out_f16;                 // 1: fp16 (saturated) output, 0: bf16
-    const float *pair_scale;     // optional [P]: y = bf16(bf16(acc) * s)
-};
-
-struct PipeArgs {
-    RoutedSet s1;                // phase 1: fused gate/up (when has1)
-    RoutedSet s2;                // phase 2: down, or the one switch linear
-    int has1;
-    // [0] tile counter, [1] error flag (a wait ran out), [2 + i] finished
-    // phase 1 tiles of active expert i; zeroed by the routing kernel
-    uint32_t *ctl;
-};
-
-template <bool DUAL>
-__device__ __forceinline__ uint16_t epilogue_value(float g, float u, const float *pair_scale,
-                                                   int pair, int out_f16) {
-    float v;
-    if (DUAL) {
-        // _SwiGLU (qwen3_5.py:108-112): bf16(bf16(silu(g)) * u), g and u the
-        // bf16 outputs of the gate and up matmuls
-        v = bf16r(bf16r(silu_f32(bf16r(g))) * bf16r(u));
-    } else {
-        v = bf16r(g);
-        if (pair_scale) v = bf16r(v * pair_scale[pair]);
-    }
-    if (out_f16) return bf16_to_f16_sat(f32_to_bf16(v));
-    return f32_to_bf16(v);
-}
 
 __device__ __forceinline__ uint2 lds2(const uint8_t *base, uint32_t off) {
     return *reinterpret_cast<const uint2 *>(base + off);
@@ -213,13 +173,6 @@ __device__ __forceinline__ void dense_chunk(float (&acc)[NMAT][MT][4], const uin
             }
     }
 }
-
-struct TileInfo {
-    int phase;      // 1: gate/up, 2: down / single linear
-    int ai;         // index among the active experts
-    int e, n, base; // expert, its pair count, list offset
-    int row0;       // first output row of the tile
-};
 
 // 16 interleaved copies of nmat codebooks: entry c of copy b of matrix m at
 // 256c + 128m + 8b (codes >= K read zeros)
@@ -677,6 +630,9 @@ vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, co
     a.s1 = r1 ? set_of(*r1, gate, up) : a.s2;
     const bool vq2 = w2->format == VQMOE_FMT_VQ_U8;
     const bool vq1 = r1 ? gate->format == VQMOE_FMT_VQ_U8 : vq2;
+    // many pairs per expert (prefill): the tcgen05 grouped GEMM
+    if (vq1 && vq2 && r2.E <= 512 && (long long)r2.P >= kPrefillPairsPerExpert * (long long)r2.E)
+        return launch_experts_prefill(a, stream);
     const size_t smem = (vq1 || vq2 ? (size_t)kRepBytes : 0) + (size_t)kXBytes;
     if (vq1) return vq2 ? launch_pipe<true, true>(a, smem, stream) : launch_pipe<true, false>(a, smem, stream);
     return vq2 ? launch_pipe<false, true>(a, smem, stream) : launch_pipe<false, false>(a, smem, stream);

@@ -1,0 +1,494 @@
+// Routed VQ experts in the prefill regime on the 5th-generation tensor cores
+// (tcgen05 + TMEM): a token-permuted grouped GEMM with the VQ dequantisation
+// fused into the operand path.
+//
+// Reference: SwitchGLU.__call__ (glm5_next/_mlx_vlm/models/switch_layers.py:
+// 172-193; with many pairs the reference sorts them by expert,
+// switch_layers.py:9-21) with VQSwitchLinear experts
+// (engine/families/deepseek/heads/deepseek_v4.py:35-42, 111-130) and the
+// _SwiGLU activation (qwen3_5.py:108-112).
+//
+// One persistent CTA of four warps per SM. It takes tiles of (expert, 128
+// weight rows, 128 of the expert's pairs) from a global counter -- phase 1
+// (gate/up + SwiGLU) tiles first, then phase 2 (down x routing weight, or a
+// single switch linear); a phase 2 tile of expert e waits until every phase
+// 1 tile of e is done (bounded wait, error flag on expiry).
+//
+// Per tile, for each 64-input window: the warps gather the pairs' input rows
+// (fp16) with cp.async into a 4-stage shared-memory ring, in the canonical
+// K-major no-swizzle layout of the MMA's B operand (loaded two windows
+// ahead). Each lane owns one weight row: it reads the row's codes from the
+// tiled VQ layout (layout.cuh), looks each code up in the shared-memory
+// codebook, multiplies the 4 fp16 weights by the group scale (one rounding:
+// fp16(codebook x scale), the dense dequantisation bit for bit) and stores
+// each 32-input batch into a TMEM slot, the MMA's A operand. Lane 0 of the
+// CTA issues tcgen05.mma M=128 x N=128 x K=16 into TMEM accumulators (gate
+// and up: 128 columns each) and commits to the slot's mbarrier (and, after a
+// window, to the window's). The epilogue reads the accumulators back
+// (tcgen05.ld) and applies the SwiGLU / routing weight.
+#include <algorithm>
+
+#include "experts.cuh"
+#include "layout.cuh"
+#include "stages.cuh"
+
+namespace vqmoe {
+namespace pf {
+
+constexpr int kThreads = 128;                 // one warpgroup: TMEM lanes 0..127
+constexpr int kN = 128;                       // pairs per tile (MMA N)
+constexpr int kSlots = 2;                     // A slots per matrix (32 inputs each)
+constexpr int kWin = 64;                      // inputs per x window
+constexpr int kStages = 4;                    // x windows in shared memory
+constexpr int kStageBytes = kN * kWin * 2;    // 16 KB
+constexpr int kLbo = (kN / 8) * 128;          // bytes from one 8-input chunk to the next
+constexpr int kCbRegion = 65536;              // gate / up codebooks, then down
+constexpr size_t kSmem = 2 * kCbRegion + (size_t)kStages * kStageBytes;
+constexpr int kDCol = 2 * kSlots * 16;        // D of matrix m at kDCol + 128m
+constexpr int kAllocCols = 512;
+constexpr int kMaxE = 512;
+constexpr long kSpin = 1L << 22;
+constexpr int kPoll = 10000;
+constexpr uint32_t kSuspendNs = 20000;
+// kind::f16, D f32, A f16, B f16, both K-major, N = 128, M = 128
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kN >> 3) << 17) | ((128u >> 4) << 24);
+
+// ---------------------------------------------------------------- PTX
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait for the phase of parity `parity`: at most kPoll try_waits of
+// at most kSuspendNs each; on running out raise the error flag and skip
+// every later wait (results then wrong, and flagged, but nothing hangs).
+__device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, bool &failed) {
+    if (failed) return;
+    const uint32_t a = smem_u32(bar);
+    for (int i = 0; i < kPoll; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(kSuspendNs)
+            : "memory");
+        if (done) return;
+    }
+    failed = true;
+    atomicExch(err, 2u);
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+        "[%32];\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+          "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+          "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+          "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+// B operand descriptor, K-major, no swizzle: core matrices of 8 pairs x 8
+// inputs (16 bytes a pair); SBO = 128 (the next 8 pairs), LBO = kLbo (the
+// next 8 inputs).
+__device__ __forceinline__ uint64_t b_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((kLbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)(128u >> 4) << 32) | (1ull << 46);
+}
+__device__ __forceinline__ uint2 lds64(uint32_t saddr) {
+    uint2 r;
+    asm("ld.shared.v2.u32 {%0, %1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(saddr));
+    return r;
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait2() {
+    asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+}
+
+// 16 interleaved copies: entry c of copy b of matrix m at region + 256c + 128m + 8b
+__device__ __forceinline__ void stage_codebook(uint8_t *region, const LinearDev &w, int m) {
+    for (int i = threadIdx.x; i < 4096; i += kThreads) {
+        const int c = i >> 4, b = i & 15;
+        uint2 v = make_uint2(0, 0);
+        if (c < w.K) v = ldg_nc_v2(w.codebook + c * 4);
+        *reinterpret_cast<uint2 *>(region + c * 256 + m * 128 + b * 8) = v;
+    }
+}
+
+struct Shared {
+    uint64_t slot[kSlots];                    // MMAs done reading an A slot
+    uint64_t stage[kStages];                  // MMAs done reading an x stage
+    TileInfo info;
+    int next;
+    int pairs[kN];
+    int pre1[kMaxE + 1], pre2[kMaxE + 1];     // tiles before active expert i, per phase
+};
+
+// The pipeline state (identical in all threads): batches issued, window
+// commits per stage, tile completions.
+struct Pipe {
+    uint32_t gb;
+    uint32_t sw[kStages];
+    uint32_t dn;
+    bool failed;
+};
+
+// Codes (32 bytes = 64 codes) and the 2 group scales of a lane's row over one
+// 128-input half chunk of matrix m.
+struct Half {
+    uint4 c0, c1;
+    uint32_t s;
+};
+
+// ----------------------------------------------------------------- tile
+template <int NMAT>
+__device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, uint32_t cb_s, uint8_t *xs,
+                                        Shared &sh, uint32_t tmem, Pipe &ps, uint32_t *err) {
+    constexpr bool DUAL = NMAT == 2;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int IN = r.IN, OUT = r.OUT;
+    const int C = (IN + 255) >> 8, RB = (OUT + 31) >> 5;
+    const int NW = (C * 256) / kWin;          // windows (a multiple of 4)
+    const int rb = (in.row0 >> 5) + warp;
+    const bool rows_ok = rb < RB;
+    const int row = rb * 32 + lane;
+    const int mt = lane >> 4, hh = (lane >> 3) & 1, g = lane & 7;
+    // this lane's row in the tiled layout: per chunk c, half: codes at
+    // tile*2048 + half*1024 + (2mt+h)*256 + 32g (32 bytes), scales at
+    // tile*128 + half*64 + (2mt+h)*16 + 2g (2 fp16)
+    const uint8_t *cbase[NMAT];
+    const uint16_t *sbase[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+        const LinearDev &w = m == 0 ? r.w0 : r.w1;
+        const long long tile0 = ((long long)in.e * RB + (rows_ok ? rb : 0)) * C;
+        cbase[m] = w.codes + tile0 * 2048 + (2 * mt + hh) * 256 + 32 * g;
+        sbase[m] = w.scales + tile0 * 128 + (2 * mt + hh) * 16 + 2 * g;
+    }
+    const uint32_t lanebyte = (lane & 15) * 8;
+    const uint32_t t_warp = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t xs_s = smem_u32(xs);
+    if (tid < kN) sh.pairs[tid] = tid < in.n ? r.list[in.base + tid] : -1;
+    __syncthreads();
+    // ---- x windows: stage s holds window w when w % kStages == s
+    auto stage_window = [&](int w) {
+        const int s = w % kStages;
+        const int f0 = w * kWin;
+        for (int it = tid; it < in.n * (kWin / 8); it += kThreads) {
+            const int n = it >> 3, ch = it & 7;
+            const int p = sh.pairs[n];
+            const int xr = r.x_per_pair ? p : p / r.k;
+            const int f = f0 + 8 * ch;
+            const bool ok = f < IN;
+            cp_async16(xs_s + s * kStageBytes + ch * kLbo + (n >> 3) * 128 + (n & 7) * 16,
+                       r.x + (size_t)xr * IN + (ok ? f : 0), ok ? 16 : 0);
+        }
+    };
+    stage_window(0);
+    cp_async_commit();
+    if (NW > 1) stage_window(1);
+    cp_async_commit();
+    // ---- codes of half chunks: hb[0] current, hb[1] next
+    Half hb[2][NMAT];
+    auto load_half = [&](Half (&h)[NMAT], int hidx) {
+        const int c = hidx >> 1, half = hidx & 1;
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            if (rows_ok && hidx < 2 * C) {
+                const uint8_t *p = cbase[m] + (long long)c * 2048 + half * 1024;
+                h[m].c0 = ldg_stream_v4(p);
+                h[m].c1 = ldg_stream_v4(p + 16);
+                h[m].s = ldg_stream_u32(sbase[m] + (long long)c * 128 + half * 64);
+            } else {
+                h[m].c0 = make_uint4(0, 0, 0, 0);
+                h[m].c1 = make_uint4(0, 0, 0, 0);
+                h[m].s = 0u;
+            }
+        }
+    };
+    load_half(hb[0], 0);
+    load_half(hb[1], 1);
+    for (int w = 0; w < NW; w += 2) {        // two windows = one half chunk
+#pragma unroll
+        for (int ww = 0; ww < 2; ++ww) {
+            const int win = w + ww;
+            // refill: window win + 2 into the stage window win - 2 used
+            if (win + 2 < NW) {
+                const int s2 = (win + 2) % kStages;
+                if (win >= 2) {
+                    mbar_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
+                    ++ps.sw[s2];
+                }
+                stage_window(win + 2);
+            }
+            cp_async_commit();
+            cp_async_wait2();                 // this thread's copies of window win
+            fence_proxy_async();
+            __syncthreads();                  // everyone's copies of window win
+            const int s = win % kStages;
+#pragma unroll
+            for (int jb = 0; jb < 2; ++jb) {
+                const int j = 2 * ww + jb;    // batch within the half chunk (32 inputs)
+                const uint32_t slot = ps.gb % kSlots;
+                uint32_t a[NMAT][16];
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    const uint32_t s2v = __byte_perm(hb[0][m].s, 0, (j >> 1) ? 0x3232 : 0x1010);
+                    const uint32_t words[8] = {hb[0][m].c0.x, hb[0][m].c0.y, hb[0][m].c0.z, hb[0][m].c0.w,
+                                               hb[0][m].c1.x, hb[0][m].c1.y, hb[0][m].c1.z, hb[0][m].c1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        // quad i of the batch: t = i & 3, b = 2j + (i >> 2) -> byte b & 3
+                        // of word 2t + (b >> 2)
+                        const int t = i & 3, b = 2 * j + (i >> 2);
+                        const uint32_t ad =
+                            __byte_perm(words[2 * t + (b >> 2)], lanebyte, 0x5504u | ((b & 3) << 4));
+                        const uint2 e = lds64(cb_s + m * 128 + ad);
+                        a[m][2 * i] = hmul2_u32(e.x, s2v);
+                        a[m][2 * i + 1] = hmul2_u32(e.y, s2v);
+                    }
+                }
+                if (ps.gb >= kSlots) mbar_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
+                tc_fence_after();
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) tmem_st16(t_warp + 16 * (kSlots * m + slot), a[m]);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncthreads();
+                if (tid == 0) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                        for (int k16 = 0; k16 < 2; ++k16) {
+                            const int k0 = 32 * jb + 16 * k16;        // input within the window
+                            tc_mma(tmem + kDCol + 128 * m, tmem + 16 * (kSlots * m + slot) + 8 * k16,
+                                   b_desc(xs_s + s * kStageBytes + (k0 >> 3) * kLbo), win > 0 || jb > 0 || k16 > 0);
+                        }
+                    tc_commit(&sh.slot[slot]);
+                    if (jb == 1) tc_commit(&sh.stage[s]);
+                }
+                ++ps.gb;
+            }
+        }
+        // next half chunk
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) hb[0][m] = hb[1][m];
+        load_half(hb[1], (w >> 1) + 2);
+    }
+    // ---- the windows still owed a stage wait (the loop waited for windows
+    // 0 .. NW-5 while refilling; NW is a multiple of 4): then all MMAs are done
+    for (int win = (NW > 4 ? NW - 4 : 0); win < NW; ++win) {
+        const int s2 = win % kStages;
+        mbar_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
+        ++ps.sw[s2];
+    }
+    tc_fence_after();
+    // ---- accumulators -> outputs, 32 pairs at a time
+#pragma unroll 1
+    for (int q = 0; q < kN / 32; ++q) {
+        uint32_t dv[NMAT][32];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) tmem_ld32(t_warp + kDCol + 128 * m + 32 * q, dv[m]);
+        tmem_wait_ld();
+        if (rows_ok && row < OUT) {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+                const int p = sh.pairs[32 * q + jj];
+                if (p < 0) continue;
+                r.out[(size_t)p * OUT + row] = epilogue_value<DUAL>(
+                    __uint_as_float(dv[0][jj]), __uint_as_float(dv[NMAT - 1][jj]), r.pair_scale, p, r.out_f16);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+}
+
+// Tiles before active expert i of each phase (pairs in blocks of kN): the
+// block counts are read in parallel, then summed in order by one thread.
+__device__ __forceinline__ void tile_prefix(const PipeArgs &a, Shared &sh, int nact, int rt1, int rt2) {
+    for (int i = threadIdx.x; i < nact; i += kThreads)
+        sh.pre2[i] = (a.s2.cnt[a.s2.active[i]] + kN - 1) / kN;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t1 = 0, t2 = 0;
+        for (int i = 0; i < nact; ++i) {
+            const int nb = sh.pre2[i];
+            sh.pre1[i] = t1;
+            sh.pre2[i] = t2;
+            t1 += nb * rt1;
+            t2 += nb * rt2;
+        }
+        sh.pre1[nact] = t1;
+        sh.pre2[nact] = t2;
+    }
+    __syncthreads();
+}
+
+// the active expert holding tile u of a phase: the last i with pre[i] <= u
+__device__ __forceinline__ int find_expert(const int *pre, int nact, int u) {
+    int lo = 0, hi = nact - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= u) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// --------------------------------------------------------------- kernel
+__global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ Shared sh;
+    __shared__ uint32_t s_tmem;
+    const int tid = threadIdx.x;
+    uint8_t *cbA = smem, *cbB = smem + kCbRegion, *xs = smem + 2 * kCbRegion;
+    if (a.has1) {
+        stage_codebook(cbA, a.s1.w0, 0);
+        stage_codebook(cbA, a.s1.w1, 1);
+    }
+    stage_codebook(cbB, a.s2.w0, 0);
+    if (tid == 0) {
+        for (int i = 0; i < kSlots; ++i) mbar_init(&sh.slot[i]);
+        for (int i = 0; i < kStages; ++i) mbar_init(&sh.stage[i]);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (tid < 32) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                         smem_u32(&s_tmem)),
+                     "r"(kAllocCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    uint32_t *err = a.ctl + 1;
+    const int nact = min(a.s2.active[a.s2.E], kMaxE);
+    const int rt1 = a.has1 ? (a.s1.OUT + 127) / 128 : 0;
+    const int rt2 = (a.s2.OUT + 127) / 128;
+    tile_prefix(a, sh, nact, rt1, rt2);
+    const int n1 = a.has1 ? sh.pre1[nact] : 0, n2 = sh.pre2[nact];
+    Pipe ps{};
+    if (tid == 0) sh.next = (int)atomicAdd(a.ctl, 1u);
+    __syncthreads();
+    for (;;) {
+        const int tile = sh.next;
+        if (tile >= n1 + n2) break;
+        __syncthreads();                      // everyone has read next
+        if (tid == 0) {
+            TileInfo in;
+            const bool p1 = tile < n1;
+            const int u = p1 ? tile : tile - n1;
+            const int *pre = p1 ? sh.pre1 : sh.pre2;
+            const int rt = p1 ? rt1 : rt2;
+            in.phase = p1 ? 1 : 2;
+            in.ai = find_expert(pre, nact, u);
+            in.e = a.s2.active[in.ai];
+            const int v = u - pre[in.ai];
+            const int blk = v / rt;
+            in.row0 = (v - blk * rt) * 128;
+            const int cnt = a.s2.cnt[in.e];
+            in.base = a.s2.off[in.e] + blk * kN;
+            in.n = min(kN, cnt - blk * kN);
+            if (!p1 && a.has1) {
+                // every phase 1 tile of this expert (all its blocks) is done;
+                // they were all taken before this one, by running CTAs
+                const uint32_t want = (uint32_t)(((cnt + kN - 1) / kN) * rt1);
+                const uint32_t *c = a.ctl + 2 + in.ai;
+                for (long i = 0;; ++i) {
+                    uint32_t val;
+                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(val) : "l"(c) : "memory");
+                    if (val >= want) break;
+                    if (i >= kSpin) {
+                        atomicExch(err, 1u);
+                        break;
+                    }
+                    __nanosleep(256);
+                }
+            }
+            sh.info = in;
+            sh.next = (int)atomicAdd(a.ctl, 1u);
+        }
+        __syncthreads();
+        const TileInfo in = sh.info;
+        if (in.phase == 1) {
+            pf_tile<2>(a.s1, in, smem_u32(cbA), xs, sh, tmem, ps, err);
+            if (tid == 0) {
+                __threadfence();
+                atomicAdd(a.ctl + 2 + in.ai, 1u);
+            }
+        } else {
+            pf_tile<1>(a.s2, in, smem_u32(cbB), xs, sh, tmem, ps, err);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid < 32) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(s_tmem),
+                     "r"(kAllocCols)
+                     : "memory");
+    }
+}
+
+}  // namespace pf
+
+vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        if (cudaFuncSetAttribute(pf::expert_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)pf::kSmem) != cudaSuccess)
+            return set_error(VQMOE_LAUNCH_FAILED, "prefill expert kernel: %zu bytes of shared memory",
+                             pf::kSmem);
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    pf::expert_prefill_kernel<<<sm_count(), pf::kThreads, pf::kSmem, stream>>>(a);
+    return check_launch("expert_prefill_kernel");
+}
+
+}  // namespace vqmoe

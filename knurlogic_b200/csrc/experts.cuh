@@ -1,0 +1,64 @@
+// Structures shared by the routed-expert kernels (expert.cu: mma.sync, the
+// decode regime; expert_prefill.cu: tcgen05, the prefill regime).
+#pragma once
+
+#include "common.cuh"
+
+namespace vqmoe {
+
+struct LinearDev {
+    const uint8_t *codes;      // VQ device layout (layout.cuh)
+    const uint16_t *codebook;  // [K][4] fp16 bits
+    const uint16_t *scales;    // VQ device layout (layout.cuh), fp16 bits
+    const uint16_t *weight;    // dense [E][OUT][IN] bf16 bits
+    int K;
+};
+
+struct RoutedSet {
+    const int32_t *cnt, *off, *list, *active;  // routing; active[E] = #active
+    int E, k, x_per_pair, P;
+    const uint16_t *x;           // input rows: fp16 (VQ) or bf16 (dense)
+    LinearDev w0, w1;            // w1: up_proj of the fused gate/up stage
+    int IN, OUT;
+    uint16_t *out;               // [P][OUT]
+    int out_f16;                 // 1: fp16 (saturated) output, 0: bf16
+    const float *pair_scale;     // optional [P]: y = bf16(bf16(acc) * s)
+};
+
+struct PipeArgs {
+    RoutedSet s1;                // phase 1: fused gate/up (when has1)
+    RoutedSet s2;                // phase 2: down, or the one switch linear
+    int has1;
+    // [0] tile counter, [1] error flag (a wait ran out), [2 + i] finished
+    // phase 1 tiles of active expert i; zeroed by the routing kernel
+    uint32_t *ctl;
+};
+
+template <bool DUAL>
+__device__ __forceinline__ uint16_t epilogue_value(float g, float u, const float *pair_scale,
+                                                   int pair, int out_f16) {
+    float v;
+    if (DUAL) {
+        // _SwiGLU (qwen3_5.py:108-112): bf16(bf16(silu(g)) * u), g and u the
+        // bf16 outputs of the gate and up matmuls
+        v = bf16r(bf16r(silu_f32(bf16r(g))) * bf16r(u));
+    } else {
+        v = bf16r(g);
+        if (pair_scale) v = bf16r(v * pair_scale[pair]);
+    }
+    if (out_f16) return bf16_to_f16_sat(f32_to_bf16(v));
+    return f32_to_bf16(v);
+}
+
+struct TileInfo {
+    int phase;      // 1: gate/up, 2: down / single linear
+    int ai;         // index among the active experts
+    int e, n, base; // expert, its pair count, list offset
+    int row0;       // first output row of the tile
+};
+
+// The prefill path (tcgen05): both stages of the routed VQ experts in one
+// launch, for layers whose experts see many tokens each.
+vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream);
+
+}  // namespace vqmoe

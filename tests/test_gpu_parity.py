@@ -174,17 +174,33 @@ def test_block_matches_oracle(name, tokens, seed):
 
 
 def test_block_beyond_one_launch_of_tokens():
-    """T > 2048 runs as independent token chunks; every token is exact to
-    the same tokens run alone."""
+    """T > 2048 runs as independent token chunks (here a dense first chunk
+    on the tcgen05 prefill path and a 52-token second chunk on the decode
+    path); tokens on either side of the cut, and the same tokens run alone
+    (decode path), match the oracle."""
     cfg = synth.MoEConfig("small", 16, 4, 256, 128, 64, 2100)
     w = synth.make_weights(cfg, seed=9, scales="random")
     x = synth.make_input(cfg, seed=9)
     blk = SparseMoeBlock.from_weights(_cuda(w), cfg.top_k)
     y = to_np(blk(x.to(DEV)))
     y_tail = to_np(blk(x[2000:].to(DEV)))
-    assert np.array_equal(y[2000:], y_tail)
-    ref = R.sparse_moe_block(to_np(x[2040:2060]), oracle_params(w), cfg.top_k, vq=True)
-    assert_bf16_close(y[2040:2060], ref, "chunked")
+    ref = R.sparse_moe_block(to_np(x[2000:]), oracle_params(w), cfg.top_k, vq=True)
+    assert_bf16_close(y[2000:], ref, "chunked")
+    assert_bf16_close(y_tail, ref, "alone")
+
+
+@pytest.mark.parametrize("zipf", [0.0, 1.1])
+def test_prefill_block_matches_oracle(zipf):
+    """Many pairs per expert (about 256 here): the routed experts take the
+    tcgen05 grouped-GEMM path (128-pair tiles, partial last tiles, a Zipf
+    load imbalance), with a shared expert beside them."""
+    cfg = synth.MoEConfig("pf", 16, 4, 512, 256, 128, 1024, router="uniform", zipf=zipf)
+    w = synth.make_weights(cfg, seed=17, scales="random")
+    x = synth.make_input(cfg, seed=17)
+    blk = SparseMoeBlock.from_weights(_cuda(w), cfg.top_k)
+    y = to_np(blk(x.to(DEV)))
+    ref = R.sparse_moe_block(to_np(x), oracle_params(w), cfg.top_k, vq=True)
+    assert_bf16_close(y, ref, f"prefill zipf={zipf}")
 
 
 def test_small_codebook_and_idle_experts():
