@@ -21,7 +21,7 @@
 // tiled VQ layout (layout.cuh), looks each code up in the shared-memory
 // codebook, multiplies the 4 fp16 weights by the group scale (one rounding:
 // fp16(codebook x scale), the dense dequantisation bit for bit) and stores
-// each 32-input batch into a TMEM slot, the MMA's A operand. Lane 0 of the
+// each 64-input window into a TMEM slot, the MMA's A operand. Lane 0 of the
 // CTA issues tcgen05.mma M=128 x N=128 x K=16 into TMEM accumulators (gate
 // and up: 128 columns each) and commits to the slot's mbarrier (and, after a
 // window, to the window's). The epilogue reads the accumulators back
@@ -37,14 +37,14 @@ namespace pf {
 
 constexpr int kThreads = 128;                 // one warpgroup: TMEM lanes 0..127
 constexpr int kN = 128;                       // pairs per tile (MMA N)
-constexpr int kSlots = 2;                     // A slots per matrix (32 inputs each)
+constexpr int kSlots = 4;                     // A slots per matrix (a 64-input window each)
 constexpr int kWin = 64;                      // inputs per x window
 constexpr int kStages = 4;                    // x windows in shared memory
 constexpr int kStageBytes = kN * kWin * 2;    // 16 KB
 constexpr int kLbo = (kN / 8) * 128;          // bytes from one 8-input chunk to the next
 constexpr int kCbRegion = 65536;              // gate / up codebooks, then down
 constexpr size_t kSmem = 2 * kCbRegion + (size_t)kStages * kStageBytes;
-constexpr int kDCol = 2 * kSlots * 16;        // D of matrix m at kDCol + 128m
+constexpr int kDCol = 2 * kSlots * 32;        // D of matrix m at kDCol + 128m (all 512 columns)
 constexpr int kAllocCols = 512;
 constexpr int kMaxE = 512;
 constexpr long kSpin = 1L << 22;
@@ -105,6 +105,17 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
         "%12, %13, %14, %15, %16};\n" ::"r"(taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
         "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, "
+        "%31, %32};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
@@ -173,14 +184,10 @@ struct Pipe {
     bool failed;
 };
 
-// Codes (32 bytes = 64 codes) and the 2 group scales of a lane's row over one
-// 128-input half chunk of matrix m.
-struct Half {
-    uint4 c0, c1;
-    uint32_t s;
-};
-
 // ----------------------------------------------------------------- tile
+// One tile. Thread tid stages, in every window, the 16-byte chunk tid % 8 of
+// the 8 pair slots tid / 8 + 16q (q = 0..7): its row pointers are computed
+// once per tile. One A batch is one 64-input window.
 template <int NMAT>
 __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, uint32_t cb_s, uint8_t *xs,
                                         Shared &sh, uint32_t tmem, Pipe &ps, uint32_t *err) {
@@ -188,7 +195,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int IN = r.IN, OUT = r.OUT;
     const int C = (IN + 255) >> 8, RB = (OUT + 31) >> 5;
-    const int NW = (C * 256) / kWin;          // windows (a multiple of 4)
+    const int NW = C * 4;                     // 64-input windows
     const int rb = (in.row0 >> 5) + warp;
     const bool rows_ok = rb < RB;
     const int row = rb * 32 + lane;
@@ -210,48 +217,49 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     const uint32_t xs_s = smem_u32(xs);
     if (tid < kN) sh.pairs[tid] = tid < in.n ? r.list[in.base + tid] : -1;
     __syncthreads();
-    // ---- x windows: stage s holds window w when w % kStages == s
-    auto stage_window = [&](int w) {
-        const int s = w % kStages;
-        const int f0 = w * kWin;
-        for (int it = tid; it < in.n * (kWin / 8); it += kThreads) {
-            const int n = it >> 3, ch = it & 7;
-            const int p = sh.pairs[n];
-            const int xr = r.x_per_pair ? p : p / r.k;
-            const int f = f0 + 8 * ch;
-            const bool ok = f < IN;
-            cp_async16(xs_s + s * kStageBytes + ch * kLbo + (n >> 3) * 128 + (n & 7) * 16,
-                       r.x + (size_t)xr * IN + (ok ? f : 0), ok ? 16 : 0);
-        }
-    };
-    stage_window(0);
-    cp_async_commit();
-    if (NW > 1) stage_window(1);
-    cp_async_commit();
-    // ---- codes of half chunks: hb[0] current, hb[1] next
-    Half hb[2][NMAT];
-    auto load_half = [&](Half (&h)[NMAT], int hidx) {
-        const int c = hidx >> 1, half = hidx & 1;
+    // ---- this thread's staging: chunk ch of slots n0 + 16q
+    const int ch = tid & 7, n0 = tid >> 3;
+    const uint16_t *src[8];
+    uint32_t dst0[8];
+    uint32_t live = 0;
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-            if (rows_ok && hidx < 2 * C) {
-                const uint8_t *p = cbase[m] + (long long)c * 2048 + half * 1024;
-                h[m].c0 = ldg_stream_v4(p);
-                h[m].c1 = ldg_stream_v4(p + 16);
-                h[m].s = ldg_stream_u32(sbase[m] + (long long)c * 128 + half * 64);
-            } else {
-                h[m].c0 = make_uint4(0, 0, 0, 0);
-                h[m].c1 = make_uint4(0, 0, 0, 0);
-                h[m].s = 0u;
-            }
+    for (int q = 0; q < 8; ++q) {
+        const int n = n0 + 16 * q;
+        const int p = sh.pairs[n];
+        const int xr = p < 0 ? 0 : (r.x_per_pair ? p : p / r.k);
+        src[q] = r.x + (size_t)xr * IN + 8 * ch;
+        dst0[q] = xs_s + ch * kLbo + (n >> 3) * 128 + (n & 7) * 16;
+        live |= (p >= 0 ? 1u : 0u) << q;
+    }
+#pragma unroll
+    for (int w0 = 0; w0 < 2; ++w0) {
+        if (w0 < NW) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (live >> q & 1) {
+                    const int f = w0 * kWin + 8 * ch;
+                    cp_async16(dst0[q] + (w0 % kStages) * kStageBytes, src[q] + w0 * kWin, f < IN ? 16 : 0);
+                }
         }
-    };
-    load_half(hb[0], 0);
-    load_half(hb[1], 1);
-    for (int w = 0; w < NW; w += 2) {        // two windows = one half chunk
+        cp_async_commit();
+    }
+    // ---- codes of half chunks: cur (windows 2h, 2h+1) and next
+    uint4 cc0[NMAT], cc1[NMAT], nc0[NMAT], nc1[NMAT];
+    uint32_t cs[NMAT], ns[NMAT];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+        const bool ok0 = rows_ok, ok1 = rows_ok && 1 < 2 * C;
+        cc0[m] = ok0 ? ldg_stream_v4(cbase[m]) : make_uint4(0, 0, 0, 0);
+        cc1[m] = ok0 ? ldg_stream_v4(cbase[m] + 16) : make_uint4(0, 0, 0, 0);
+        cs[m] = ok0 ? ldg_stream_u32(sbase[m]) : 0u;
+        nc0[m] = ok1 ? ldg_stream_v4(cbase[m] + 1024) : make_uint4(0, 0, 0, 0);
+        nc1[m] = ok1 ? ldg_stream_v4(cbase[m] + 1024 + 16) : make_uint4(0, 0, 0, 0);
+        ns[m] = ok1 ? ldg_stream_u32(sbase[m] + 64) : 0u;
+    }
+    for (int hw = 0; hw < NW; hw += 2) {     // two windows = one half chunk
 #pragma unroll
         for (int ww = 0; ww < 2; ++ww) {
-            const int win = w + ww;
+            const int win = hw + ww;
             // refill: window win + 2 into the stage window win - 2 used
             if (win + 2 < NW) {
                 const int s2 = (win + 2) % kStages;
@@ -259,62 +267,69 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
                     mbar_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
                     ++ps.sw[s2];
                 }
-                stage_window(win + 2);
+                const int fw = (win + 2) * kWin;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (live >> q & 1)
+                        cp_async16(dst0[q] + s2 * kStageBytes, src[q] + fw, fw + 8 * ch < IN ? 16 : 0);
             }
             cp_async_commit();
+            // dequantise this lane's 64 inputs of the window (while the copies fly)
+            const uint32_t slot = ps.gb % kSlots;
+            uint32_t a[NMAT][32];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const uint32_t s2v = __byte_perm(cs[m], 0, ww ? 0x3232 : 0x1010);
+                const uint32_t words[8] = {cc0[m].x, cc0[m].y, cc0[m].z, cc0[m].w,
+                                           cc1[m].x, cc1[m].y, cc1[m].z, cc1[m].w};
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    // quad i of the window: t = i & 3, b = 4ww + (i >> 2) -> byte b & 3
+                    // of word 2t + (b >> 2)
+                    const int t = i & 3, bb = 4 * ww + (i >> 2);
+                    const uint32_t ad = __byte_perm(words[2 * t + (bb >> 2)], lanebyte, 0x5504u | ((bb & 3) << 4));
+                    const uint2 e = lds64(cb_s + m * 128 + ad);
+                    a[m][2 * i] = hmul2_u32(e.x, s2v);
+                    a[m][2 * i + 1] = hmul2_u32(e.y, s2v);
+                }
+            }
+            if (ps.gb >= kSlots) mbar_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
+            tc_fence_after();
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) tmem_st32(t_warp + 32 * (kSlots * m + slot), a[m]);
             cp_async_wait2();                 // this thread's copies of window win
             fence_proxy_async();
-            __syncthreads();                  // everyone's copies of window win
-            const int s = win % kStages;
-#pragma unroll
-            for (int jb = 0; jb < 2; ++jb) {
-                const int j = 2 * ww + jb;    // batch within the half chunk (32 inputs)
-                const uint32_t slot = ps.gb % kSlots;
-                uint32_t a[NMAT][16];
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m) {
-                    const uint32_t s2v = __byte_perm(hb[0][m].s, 0, (j >> 1) ? 0x3232 : 0x1010);
-                    const uint32_t words[8] = {hb[0][m].c0.x, hb[0][m].c0.y, hb[0][m].c0.z, hb[0][m].c0.w,
-                                               hb[0][m].c1.x, hb[0][m].c1.y, hb[0][m].c1.z, hb[0][m].c1.w};
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        // quad i of the batch: t = i & 3, b = 2j + (i >> 2) -> byte b & 3
-                        // of word 2t + (b >> 2)
-                        const int t = i & 3, b = 2 * j + (i >> 2);
-                        const uint32_t ad =
-                            __byte_perm(words[2 * t + (b >> 2)], lanebyte, 0x5504u | ((b & 3) << 4));
-                        const uint2 e = lds64(cb_s + m * 128 + ad);
-                        a[m][2 * i] = hmul2_u32(e.x, s2v);
-                        a[m][2 * i + 1] = hmul2_u32(e.y, s2v);
-                    }
-                }
-                if (ps.gb >= kSlots) mbar_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncthreads();                  // A stored, window win staged, by everyone
+            if (tid == 0) {
                 tc_fence_after();
+                const int s = win % kStages;
 #pragma unroll
-                for (int m = 0; m < NMAT; ++m) tmem_st16(t_warp + 16 * (kSlots * m + slot), a[m]);
-                tmem_wait_st();
-                tc_fence_before();
-                __syncthreads();
-                if (tid == 0) {
-                    tc_fence_after();
+                for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-                    for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-                        for (int k16 = 0; k16 < 2; ++k16) {
-                            const int k0 = 32 * jb + 16 * k16;        // input within the window
-                            tc_mma(tmem + kDCol + 128 * m, tmem + 16 * (kSlots * m + slot) + 8 * k16,
-                                   b_desc(xs_s + s * kStageBytes + (k0 >> 3) * kLbo), win > 0 || jb > 0 || k16 > 0);
-                        }
-                    tc_commit(&sh.slot[slot]);
-                    if (jb == 1) tc_commit(&sh.stage[s]);
-                }
-                ++ps.gb;
+                    for (int k16 = 0; k16 < 4; ++k16)
+                        tc_mma(tmem + kDCol + 128 * m, tmem + 32 * (kSlots * m + slot) + 8 * k16,
+                               b_desc(xs_s + s * kStageBytes + (2 * k16) * kLbo), win > 0 || k16 > 0);
+                tc_commit(&sh.slot[slot]);
+                tc_commit(&sh.stage[s]);
             }
+            ++ps.gb;
         }
         // next half chunk
+        const int hn = (hw >> 1) + 2;
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) hb[0][m] = hb[1][m];
-        load_half(hb[1], (w >> 1) + 2);
+        for (int m = 0; m < NMAT; ++m) {
+            cc0[m] = nc0[m];
+            cc1[m] = nc1[m];
+            cs[m] = ns[m];
+            if (rows_ok && hn < 2 * C) {
+                const uint8_t *p = cbase[m] + (long long)(hn >> 1) * 2048 + (hn & 1) * 1024;
+                nc0[m] = ldg_stream_v4(p);
+                nc1[m] = ldg_stream_v4(p + 16);
+                ns[m] = ldg_stream_u32(sbase[m] + (long long)(hn >> 1) * 128 + (hn & 1) * 64);
+            }
+        }
     }
     // ---- the windows still owed a stage wait (the loop waited for windows
     // 0 .. NW-5 while refilling; NW is a multiple of 4): then all MMAs are done
