@@ -318,9 +318,19 @@ static vqmoe_status side_stream(SideStream **out) {
     return VQMOE_OK;
 }
 
+// From this many tokens the shared expert runs as tcgen05 dense GEMMs.
+constexpr int kDensePrefillTokens = 256;
+
 static vqmoe_status run_shared(const vqmoe_block *b, const uint16_t *x, int T, const BlockWs &w,
                                cudaStream_t st) {
     const RouteWs &rt = w.rt;
+    if (T >= kDensePrefillTokens && b->hidden % 64 == 0 && b->shared_inter % 64 == 0) {
+        vqmoe_status s = launch_dense_prefill(x, b->shared_gate_w, b->shared_up_w, T, b->hidden,
+                                              b->shared_inter, w.act_s, rt.zero + 1, st);
+        if (s != VQMOE_OK) return s;
+        return launch_dense_prefill(w.act_s, b->shared_down_w, nullptr, T, b->shared_inter, b->hidden,
+                                    w.sh, rt.zero + 1, st);
+    }
     if (rt.szero_words &&
         cudaMemsetAsync(rt.szero, 0, (size_t)rt.szero_words * sizeof(uint32_t), st) != cudaSuccess)
         return check_launch("shared expert semaphores");

@@ -489,6 +489,158 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
     }
 }
 
+// ------------------------------------------------------- dense (bf16)
+// The shared expert's matmuls for many tokens (qwen3_5.py:184-185): out[T,
+// OUT] = epilogue(x[T, IN] . W^T) with bf16 W (and a second matrix for the
+// fused gate/up + SwiGLU). Tiles of 128 weight rows x 128 tokens, spread over
+// the CTAs round robin; per 64-input window both operands -- weight rows (A)
+// and token rows (B) -- are staged with cp.async into a 4-stage ring in the
+// K-major no-swizzle layout and multiplied from shared memory
+// (tcgen05.mma.kind::f16, bf16 inputs) into TMEM.
+constexpr uint32_t kIdescBf16 =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) | ((128u >> 4) << 24);
+
+struct DenseArgs {
+    const uint16_t *x;           // [T][IN] bf16
+    const uint16_t *w0, *w1;     // [OUT][IN] bf16
+    uint16_t *out;               // [T][OUT] bf16
+    int T, IN, OUT;
+    uint32_t *err;
+};
+
+__device__ __forceinline__ void tc_mma_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdescBf16), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+template <int NMAT>
+__global__ void __launch_bounds__(kThreads, 1) dense_prefill_kernel(const DenseArgs a) {
+    constexpr bool DUAL = NMAT == 2;
+    constexpr int kStage = (NMAT + 1) * kStageBytes;       // A of each matrix, then B
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ uint64_t s_stage[kStages];
+    __shared__ uint32_t s_tmem;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) mbar_init(&s_stage[i]);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    constexpr int kCols = DUAL ? 256 : 128;
+    if (tid < 32) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                         smem_u32(&s_tmem)),
+                     "r"(kCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    const uint32_t t_warp = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t sm_s = smem_u32(smem);
+    const int rt = (a.OUT + 127) / 128, nbk = (a.T + kN - 1) / kN;
+    const int NW = a.IN / kWin;
+    uint32_t sw[kStages] = {0u, 0u, 0u, 0u};
+    bool failed = false;
+    const int ch = tid & 7, n0 = tid >> 3;
+    for (int tile = blockIdx.x; tile < rt * nbk; tile += gridDim.x) {
+        const int row0 = (tile % rt) * 128, t0 = (tile / rt) * kN;
+        // this thread's 8 weight rows / tokens (row n0 + 16q), chunk ch
+        const uint16_t *wsrc[NMAT][8];
+        const uint16_t *xsrc[8];
+        uint32_t wlive = 0, xlive = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int n = n0 + 16 * q;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) wsrc[m][q] = (m == 0 ? a.w0 : a.w1) + (size_t)min(row0 + n, a.OUT - 1) * a.IN + 8 * ch;
+            xsrc[q] = a.x + (size_t)min(t0 + n, a.T - 1) * a.IN + 8 * ch;
+            wlive |= (row0 + n < a.OUT ? 1u : 0u) << q;
+            xlive |= (t0 + n < a.T ? 1u : 0u) << q;
+        }
+        const uint32_t dofs = ch * kLbo;
+        auto stage = [&](int win) {
+            const uint32_t base = sm_s + (win % kStages) * kStage;
+            const int f = win * kWin;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int n = n0 + 16 * q;
+                const uint32_t d = dofs + (n >> 3) * 128 + (n & 7) * 16;
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+                    cp_async16(base + m * kStageBytes + d, wsrc[m][q] + f, (wlive >> q & 1) ? 16 : 0);
+                cp_async16(base + NMAT * kStageBytes + d, xsrc[q] + f, (xlive >> q & 1) ? 16 : 0);
+            }
+        };
+        stage(0);
+        cp_async_commit();
+        if (NW > 1) stage(1);
+        cp_async_commit();
+        for (int win = 0; win < NW; ++win) {
+            if (win + 2 < NW) {
+                const int s2 = (win + 2) % kStages;
+                if (win >= 2) {
+                    mbar_wait(&s_stage[s2], sw[s2] & 1, a.err, failed);
+                    ++sw[s2];
+                }
+                stage(win + 2);
+            }
+            cp_async_commit();
+            cp_async_wait2();
+            fence_proxy_async();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t base = sm_s + (win % kStages) * kStage;
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int k16 = 0; k16 < 4; ++k16)
+                        tc_mma_ss(tmem + 128 * m, b_desc(base + m * kStageBytes + 2 * k16 * kLbo),
+                                  b_desc(base + NMAT * kStageBytes + 2 * k16 * kLbo), win > 0 || k16 > 0);
+                tc_commit(&s_stage[win % kStages]);
+            }
+        }
+        for (int win = (NW > 4 ? NW - 4 : 0); win < NW; ++win) {
+            const int s2 = win % kStages;
+            mbar_wait(&s_stage[s2], sw[s2] & 1, a.err, failed);
+            ++sw[s2];
+        }
+        tc_fence_after();
+        const int row = row0 + 32 * warp + lane;
+#pragma unroll 1
+        for (int q = 0; q < kN / 32; ++q) {
+            uint32_t dv[NMAT][32];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) tmem_ld32(t_warp + 128 * m + 32 * q, dv[m]);
+            tmem_wait_ld();
+            if (row < a.OUT) {
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int t = t0 + 32 * q + jj;
+                    if (t >= a.T) continue;
+                    a.out[(size_t)t * a.OUT + row] = epilogue_value<DUAL>(
+                        __uint_as_float(dv[0][jj]), __uint_as_float(dv[NMAT - 1][jj]), nullptr, 0, 0);
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid < 32) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(s_tmem), "r"(kCols)
+                     : "memory");
+    }
+}
+
 }  // namespace pf
 
 vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream) {
@@ -504,6 +656,39 @@ vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream) {
     }
     pf::expert_prefill_kernel<<<sm_count(), pf::kThreads, pf::kSmem, stream>>>(a);
     return check_launch("expert_prefill_kernel");
+}
+
+}  // namespace vqmoe
+
+namespace vqmoe {
+
+// The shared expert's dense matmul (+ SwiGLU when w1 is set) for many tokens
+// on tcgen05; IN a multiple of 64.
+vqmoe_status launch_dense_prefill(const void *x, const void *w0, const void *w1, int T, int IN, int OUT,
+                                  void *out, uint32_t *err, cudaStream_t stream) {
+    static bool configured[2][64] = {{false}};
+    const int nmat = w1 ? 2 : 1;
+    const size_t smem = (size_t)pf::kStages * (nmat + 1) * pf::kStageBytes;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto fn = nmat == 2 ? pf::dense_prefill_kernel<2> : pf::dense_prefill_kernel<1>;
+    if (dev < 0 || dev >= 64 || !configured[nmat - 1][dev]) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return set_error(VQMOE_LAUNCH_FAILED, "dense prefill kernel: %zu bytes of shared memory", smem);
+        if (dev >= 0 && dev < 64) configured[nmat - 1][dev] = true;
+    }
+    pf::DenseArgs a{};
+    a.x = static_cast<const uint16_t *>(x);
+    a.w0 = static_cast<const uint16_t *>(w0);
+    a.w1 = static_cast<const uint16_t *>(w1 ? w1 : w0);
+    a.out = static_cast<uint16_t *>(out);
+    a.T = T;
+    a.IN = IN;
+    a.OUT = OUT;
+    a.err = err;
+    const int tiles = ((OUT + 127) / 128) * ((T + pf::kN - 1) / pf::kN);
+    fn<<<std::min(tiles, sm_count()), pf::kThreads, smem, stream>>>(a);
+    return check_launch("dense_prefill_kernel");
 }
 
 }  // namespace vqmoe

@@ -42,6 +42,10 @@ vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, co
 // The shared expert's dense matmul (+ SwiGLU when w1 is set): K slicing,
 // its partial buffer [ks][T][nmat][OUT] float and [ceil(OUT/32)] semaphores.
 void plan_shared_dense(int IN, int OUT, int nmat, int *ks, int *kslice, size_t *smem);
+// The same on tcgen05 for many tokens (IN a multiple of 64); `err` is a
+// word for the kernel's bounded waits.
+vqmoe_status launch_dense_prefill(const void *x, const void *w0, const void *w1, int T, int IN, int OUT,
+                                  void *out, uint32_t *err, cudaStream_t stream);
 vqmoe_status launch_shared_dense(const void *x, const void *w0, const void *w1, int T, int IN, int OUT,
                                  void *out, float *part, uint32_t *sem, cudaStream_t stream);
 

@@ -193,8 +193,9 @@ def test_block_beyond_one_launch_of_tokens():
 def test_prefill_block_matches_oracle(zipf):
     """Many pairs per expert (about 256 here): the routed experts take the
     tcgen05 grouped-GEMM path (128-pair tiles, partial last tiles, a Zipf
-    load imbalance), with a shared expert beside them."""
-    cfg = synth.MoEConfig("pf", 16, 4, 512, 256, 128, 1024, router="uniform", zipf=zipf)
+    load imbalance), and the shared expert (192 rows: a partial row tile) the
+    tcgen05 dense GEMMs."""
+    cfg = synth.MoEConfig("pf", 16, 4, 512, 256, 192, 1024, router="uniform", zipf=zipf)
     w = synth.make_weights(cfg, seed=17, scales="random")
     x = synth.make_input(cfg, seed=17)
     blk = SparseMoeBlock.from_weights(_cuda(w), cfg.top_k)
