@@ -8,7 +8,7 @@
 // (engine/families/deepseek/heads/deepseek_v4.py:35-42, 111-130) and the
 // _SwiGLU activation (qwen3_5.py:108-112).
 //
-// One persistent CTA of four warps per SM. It takes tiles of (expert, 128
+// One persistent CTA of two warpgroups per SM. It takes tiles of (expert, 128
 // weight rows, 128 of the expert's pairs) from a global counter -- phase 1
 // (gate/up + SwiGLU) tiles first, then phase 2 (down x routing weight, or a
 // single switch linear); a phase 2 tile of expert e waits until every phase
@@ -17,8 +17,9 @@
 // Per tile, for each 64-input window: the warps gather the pairs' input rows
 // (fp16) with cp.async into a 4-stage shared-memory ring, in the canonical
 // K-major no-swizzle layout of the MMA's B operand (loaded two windows
-// ahead). Each lane owns one weight row: it reads the row's codes from the
-// tiled VQ layout (layout.cuh), looks each code up in the shared-memory
+// ahead). Each lane owns one weight row and half of each window (the two
+// warpgroups take alternate 8-input chunks): it reads the row's codes from
+// the tiled VQ layout (layout.cuh), looks each code up in the shared-memory
 // codebook, multiplies the 4 fp16 weights by the group scale (one rounding:
 // fp16(codebook x scale), the dense dequantisation bit for bit) and stores
 // each 64-input window into a TMEM slot, the MMA's A operand. Lane 0 of the
@@ -35,7 +36,8 @@
 namespace vqmoe {
 namespace pf {
 
-constexpr int kThreads = 128;                 // one warpgroup: TMEM lanes 0..127
+constexpr int kThreads = 256;                 // two warpgroups, each over TMEM lanes 0..127
+constexpr int kDenseThreads = 128;            // the dense kernel: one warpgroup
 constexpr int kN = 128;                       // pairs per tile (MMA N)
 constexpr int kSlots = 4;                     // A slots per matrix (a 64-input window each)
 constexpr int kWin = 64;                      // inputs per x window
@@ -186,13 +188,14 @@ struct Pipe {
 
 // ----------------------------------------------------------------- tile
 // One tile. Thread tid stages, in every window, the 16-byte chunk tid % 8 of
-// the 8 pair slots tid / 8 + 16q (q = 0..7): its row pointers are computed
+// the 4 pair slots tid / 8 + 32q (q = 0..3): its row pointers are computed
 // once per tile. One A batch is one 64-input window.
 template <int NMAT>
 __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, uint32_t cb_s, uint8_t *xs,
                                         Shared &sh, uint32_t tmem, Pipe &ps, uint32_t *err) {
     constexpr bool DUAL = NMAT == 2;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = (tid >> 5) & 3, lane = tid & 31;
+    const int wgi = tid >> 7;                 // warpgroup: 8-input chunks 2j + wgi of each window
     const int IN = r.IN, OUT = r.OUT;
     const int C = (IN + 255) >> 8, RB = (OUT + 31) >> 5;
     const int NW = C * 4;                     // 64-input windows
@@ -209,7 +212,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     for (int m = 0; m < NMAT; ++m) {
         const LinearDev &w = m == 0 ? r.w0 : r.w1;
         const long long tile0 = ((long long)in.e * RB + (rows_ok ? rb : 0)) * C;
-        cbase[m] = w.codes + tile0 * 2048 + (2 * mt + hh) * 256 + 32 * g;
+        cbase[m] = w.codes + tile0 * 2048 + (2 * mt + hh) * 256 + 32 * g + 16 * wgi;
         sbase[m] = w.scales + tile0 * 128 + (2 * mt + hh) * 16 + 2 * g;
     }
     const uint32_t lanebyte = (lane & 15) * 8;
@@ -217,25 +220,30 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     const uint32_t xs_s = smem_u32(xs);
     if (tid < kN) sh.pairs[tid] = tid < in.n ? r.list[in.base + tid] : -1;
     __syncthreads();
-    // ---- this thread's staging: chunk ch of slots n0 + 16q
+    // ---- this thread's staging: input chunk ch of slots n0 + 32q. The MMA's K
+    // order within a window is permuted -- input chunk ch sits at K chunk
+    // kch(ch) = 4 (ch & 1) + ch / 2 in both operands -- so that warpgroup wgi
+    // dequantises the contiguous A columns 16 wgi .. 16 wgi + 15.
+    constexpr int kQ = kN * 8 / kThreads;     // slots a thread stages per window
     const int ch = tid & 7, n0 = tid >> 3;
-    const uint16_t *src[8];
-    uint32_t dst0[8];
+    const int kch = 4 * (ch & 1) + (ch >> 1);
+    const uint16_t *src[kQ];
+    uint32_t dst0[kQ];
     uint32_t live = 0;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        const int n = n0 + 16 * q;
+    for (int q = 0; q < kQ; ++q) {
+        const int n = n0 + (kThreads / 8) * q;
         const int p = sh.pairs[n];
         const int xr = p < 0 ? 0 : (r.x_per_pair ? p : p / r.k);
         src[q] = r.x + (size_t)xr * IN + 8 * ch;
-        dst0[q] = xs_s + ch * kLbo + (n >> 3) * 128 + (n & 7) * 16;
+        dst0[q] = xs_s + kch * kLbo + (n >> 3) * 128 + (n & 7) * 16;
         live |= (p >= 0 ? 1u : 0u) << q;
     }
 #pragma unroll
     for (int w0 = 0; w0 < 2; ++w0) {
         if (w0 < NW) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
+            for (int q = 0; q < kQ; ++q)
                 if (live >> q & 1) {
                     const int f = w0 * kWin + 8 * ch;
                     cp_async16(dst0[q] + (w0 % kStages) * kStageBytes, src[q] + w0 * kWin, f < IN ? 16 : 0);
@@ -243,17 +251,16 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
         }
         cp_async_commit();
     }
-    // ---- codes of half chunks: cur (windows 2h, 2h+1) and next
-    uint4 cc0[NMAT], cc1[NMAT], nc0[NMAT], nc1[NMAT];
+    // ---- this warpgroup's codes of half chunks (t = 2wgi, 2wgi+1: 16 bytes):
+    // cur (windows 2h, 2h+1) and next
+    uint4 cc[NMAT], nc[NMAT];
     uint32_t cs[NMAT], ns[NMAT];
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
         const bool ok0 = rows_ok, ok1 = rows_ok && 1 < 2 * C;
-        cc0[m] = ok0 ? ldg_stream_v4(cbase[m]) : make_uint4(0, 0, 0, 0);
-        cc1[m] = ok0 ? ldg_stream_v4(cbase[m] + 16) : make_uint4(0, 0, 0, 0);
+        cc[m] = ok0 ? ldg_stream_v4(cbase[m]) : make_uint4(0, 0, 0, 0);
         cs[m] = ok0 ? ldg_stream_u32(sbase[m]) : 0u;
-        nc0[m] = ok1 ? ldg_stream_v4(cbase[m] + 1024) : make_uint4(0, 0, 0, 0);
-        nc1[m] = ok1 ? ldg_stream_v4(cbase[m] + 1024 + 16) : make_uint4(0, 0, 0, 0);
+        nc[m] = ok1 ? ldg_stream_v4(cbase[m] + 1024) : make_uint4(0, 0, 0, 0);
         ns[m] = ok1 ? ldg_stream_u32(sbase[m] + 64) : 0u;
     }
     for (int hw = 0; hw < NW; hw += 2) {     // two windows = one half chunk
@@ -269,34 +276,34 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
                 }
                 const int fw = (win + 2) * kWin;
 #pragma unroll
-                for (int q = 0; q < 8; ++q)
+                for (int q = 0; q < kQ; ++q)
                     if (live >> q & 1)
                         cp_async16(dst0[q] + s2 * kStageBytes, src[q] + fw, fw + 8 * ch < IN ? 16 : 0);
             }
             cp_async_commit();
-            // dequantise this lane's 64 inputs of the window (while the copies fly)
+            // dequantise this lane's 32 inputs of the window (while the copies
+            // fly): local quad l = 2j + s is code t = 2wgi + s, b = 4ww + j --
+            // byte j of word 2s + ww of this warpgroup's 16 bytes -- and goes to
+            // A columns 16wgi + 2l, 2l + 1 (K chunk 4wgi + j = input chunk 2j + wgi)
             const uint32_t slot = ps.gb % kSlots;
-            uint32_t a[NMAT][32];
+            uint32_t a[NMAT][16];
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) {
                 const uint32_t s2v = __byte_perm(cs[m], 0, ww ? 0x3232 : 0x1010);
-                const uint32_t words[8] = {cc0[m].x, cc0[m].y, cc0[m].z, cc0[m].w,
-                                           cc1[m].x, cc1[m].y, cc1[m].z, cc1[m].w};
+                const uint32_t words[4] = {cc[m].x, cc[m].y, cc[m].z, cc[m].w};
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    // quad i of the window: t = i & 3, b = 4ww + (i >> 2) -> byte b & 3
-                    // of word 2t + (b >> 2)
-                    const int t = i & 3, bb = 4 * ww + (i >> 2);
-                    const uint32_t ad = __byte_perm(words[2 * t + (bb >> 2)], lanebyte, 0x5504u | ((bb & 3) << 4));
+                for (int l = 0; l < 8; ++l) {
+                    const int j = l >> 1, sb = l & 1;
+                    const uint32_t ad = __byte_perm(words[2 * sb + ww], lanebyte, 0x5504u | (j << 4));
                     const uint2 e = lds64(cb_s + m * 128 + ad);
-                    a[m][2 * i] = hmul2_u32(e.x, s2v);
-                    a[m][2 * i + 1] = hmul2_u32(e.y, s2v);
+                    a[m][2 * l] = hmul2_u32(e.x, s2v);
+                    a[m][2 * l + 1] = hmul2_u32(e.y, s2v);
                 }
             }
             if (ps.gb >= kSlots) mbar_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
             tc_fence_after();
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) tmem_st32(t_warp + 32 * (kSlots * m + slot), a[m]);
+            for (int m = 0; m < NMAT; ++m) tmem_st16(t_warp + 32 * (kSlots * m + slot) + 16 * wgi, a[m]);
             cp_async_wait2();                 // this thread's copies of window win
             fence_proxy_async();
             tmem_wait_st();
@@ -320,13 +327,11 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
         const int hn = (hw >> 1) + 2;
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
-            cc0[m] = nc0[m];
-            cc1[m] = nc1[m];
+            cc[m] = nc[m];
             cs[m] = ns[m];
             if (rows_ok && hn < 2 * C) {
                 const uint8_t *p = cbase[m] + (long long)(hn >> 1) * 2048 + (hn & 1) * 1024;
-                nc0[m] = ldg_stream_v4(p);
-                nc1[m] = ldg_stream_v4(p + 16);
+                nc[m] = ldg_stream_v4(p);
                 ns[m] = ldg_stream_u32(sbase[m] + (long long)(hn >> 1) * 128 + (hn & 1) * 64);
             }
         }
@@ -339,9 +344,10 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
         ++ps.sw[s2];
     }
     tc_fence_after();
-    // ---- accumulators -> outputs, 32 pairs at a time
+    // ---- accumulators -> outputs, 32 pairs at a time; warpgroup wgi takes
+    // pairs 64 wgi .. 64 wgi + 63
 #pragma unroll 1
-    for (int q = 0; q < kN / 32; ++q) {
+    for (int q = 2 * wgi; q < 2 * wgi + 2; ++q) {
         uint32_t dv[NMAT][32];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) tmem_ld32(t_warp + kDCol + 128 * m + 32 * q, dv[m]);
@@ -518,7 +524,7 @@ __device__ __forceinline__ void tc_mma_ss(uint32_t tmem_d, uint64_t adesc, uint6
 }
 
 template <int NMAT>
-__global__ void __launch_bounds__(kThreads, 1) dense_prefill_kernel(const DenseArgs a) {
+__global__ void __launch_bounds__(kDenseThreads, 1) dense_prefill_kernel(const DenseArgs a) {
     constexpr bool DUAL = NMAT == 2;
     constexpr int kStage = (NMAT + 1) * kStageBytes;       // A of each matrix, then B
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -687,7 +693,7 @@ vqmoe_status launch_dense_prefill(const void *x, const void *w0, const void *w1,
     a.OUT = OUT;
     a.err = err;
     const int tiles = ((OUT + 127) / 128) * ((T + pf::kN - 1) / pf::kN);
-    fn<<<std::min(tiles, sm_count()), pf::kThreads, smem, stream>>>(a);
+    fn<<<std::min(tiles, sm_count()), pf::kDenseThreads, smem, stream>>>(a);
     return check_launch("dense_prefill_kernel");
 }
 
