@@ -38,14 +38,16 @@ namespace pf {
 
 constexpr int kThreads = 256;                 // two warpgroups, each over TMEM lanes 0..127
 constexpr int kDenseThreads = 128;            // the dense kernel: one warpgroup
+constexpr int kDenseStages = 4;               // its operand windows in shared memory (2 ahead)
 constexpr int kN = 128;                       // pairs per tile (MMA N)
 constexpr int kSlots = 4;                     // A slots per matrix (a 64-input window each)
 constexpr int kWin = 64;                      // inputs per x window
-constexpr int kStages = 4;                    // x windows in shared memory
+constexpr int kStages = 8;                    // x windows in shared memory
+constexpr int kAhead = kStages - 2;           // x windows gathered ahead of the one multiplied
 constexpr int kStageBytes = kN * kWin * 2;    // 16 KB
 constexpr int kLbo = (kN / 8) * 128;          // bytes from one 8-input chunk to the next
-constexpr int kCbRegion = 65536;              // gate / up codebooks, then down
-constexpr size_t kSmem = 2 * kCbRegion + (size_t)kStages * kStageBytes;
+constexpr int kCbRegion = 65536;              // the phase's codebooks: gate / up, then down
+constexpr size_t kSmem = kCbRegion + (size_t)kStages * kStageBytes;
 constexpr int kDCol = 2 * kSlots * 32;        // D of matrix m at kDCol + 128m (all 512 columns)
 constexpr int kAllocCols = 512;
 constexpr int kMaxE = 512;
@@ -154,8 +156,9 @@ __device__ __forceinline__ uint2 lds64(uint32_t saddr) {
 __device__ __forceinline__ void cp_async_commit() {
     asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
-__device__ __forceinline__ void cp_async_wait2() {
-    asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 // 16 interleaved copies: entry c of copy b of matrix m at region + 256c + 128m + 8b
@@ -174,6 +177,7 @@ struct Shared {
     TileInfo info;
     int next;
     int pairs[kN];
+    float pscale[kN];                         // the pairs' routing weights (phase 2)
     int pre1[kMaxE + 1], pre2[kMaxE + 1];     // tiles before active expert i, per phase
 };
 
@@ -218,7 +222,11 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     const uint32_t lanebyte = (lane & 15) * 8;
     const uint32_t t_warp = tmem + ((uint32_t)(warp * 32) << 16);
     const uint32_t xs_s = smem_u32(xs);
-    if (tid < kN) sh.pairs[tid] = tid < in.n ? r.list[in.base + tid] : -1;
+    if (tid < kN) {
+        const int p = tid < in.n ? r.list[in.base + tid] : -1;
+        sh.pairs[tid] = p;
+        sh.pscale[tid] = (!DUAL && r.pair_scale && p >= 0) ? r.pair_scale[p] : 1.0f;
+    }
     __syncthreads();
     // ---- this thread's staging: input chunk ch of slots n0 + 32q. The MMA's K
     // order within a window is permuted -- input chunk ch sits at K chunk
@@ -240,41 +248,48 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
         live |= (p >= 0 ? 1u : 0u) << q;
     }
 #pragma unroll
-    for (int w0 = 0; w0 < 2; ++w0) {
+    for (int w0 = 0; w0 < kAhead; ++w0) {
         if (w0 < NW) {
 #pragma unroll
             for (int q = 0; q < kQ; ++q)
                 if (live >> q & 1) {
                     const int f = w0 * kWin + 8 * ch;
-                    cp_async16(dst0[q] + (w0 % kStages) * kStageBytes, src[q] + w0 * kWin, f < IN ? 16 : 0);
+                    cp_async16(dst0[q] + w0 * kStageBytes, src[q] + w0 * kWin, f < IN ? 16 : 0);
                 }
         }
         cp_async_commit();
     }
     // ---- this warpgroup's codes of half chunks (t = 2wgi, 2wgi+1: 16 bytes):
-    // cur (windows 2h, 2h+1) and next
-    uint4 cc[NMAT], nc[NMAT];
-    uint32_t cs[NMAT], ns[NMAT];
+    // cur (windows 2h, 2h+1) and the next two
+    uint4 cc[NMAT], nc1[NMAT], nc2[NMAT];
+    uint32_t cs[NMAT], ns1[NMAT], ns2[NMAT];
+    auto load_half = [&](int hn, int m, uint4 &c, uint32_t &sc) {
+        if (rows_ok && hn < 2 * C) {
+            c = ldg_stream_v4(cbase[m] + (long long)(hn >> 1) * 2048 + (hn & 1) * 1024);
+            sc = ldg_stream_u32(sbase[m] + (long long)(hn >> 1) * 128 + (hn & 1) * 64);
+        } else {
+            c = make_uint4(0, 0, 0, 0);
+            sc = 0u;
+        }
+    };
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
-        const bool ok0 = rows_ok, ok1 = rows_ok && 1 < 2 * C;
-        cc[m] = ok0 ? ldg_stream_v4(cbase[m]) : make_uint4(0, 0, 0, 0);
-        cs[m] = ok0 ? ldg_stream_u32(sbase[m]) : 0u;
-        nc[m] = ok1 ? ldg_stream_v4(cbase[m] + 1024) : make_uint4(0, 0, 0, 0);
-        ns[m] = ok1 ? ldg_stream_u32(sbase[m] + 64) : 0u;
+        load_half(0, m, cc[m], cs[m]);
+        load_half(1, m, nc1[m], ns1[m]);
+        load_half(2, m, nc2[m], ns2[m]);
     }
     for (int hw = 0; hw < NW; hw += 2) {     // two windows = one half chunk
 #pragma unroll
         for (int ww = 0; ww < 2; ++ww) {
             const int win = hw + ww;
-            // refill: window win + 2 into the stage window win - 2 used
-            if (win + 2 < NW) {
-                const int s2 = (win + 2) % kStages;
+            // refill: window win + kAhead into the stage window win - 2 used
+            if (win + kAhead < NW) {
+                const int s2 = (win + kAhead) % kStages;
                 if (win >= 2) {
                     mbar_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
                     ++ps.sw[s2];
                 }
-                const int fw = (win + 2) * kWin;
+                const int fw = (win + kAhead) * kWin;
 #pragma unroll
                 for (int q = 0; q < kQ; ++q)
                     if (live >> q & 1)
@@ -304,7 +319,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
             tc_fence_after();
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) tmem_st16(t_warp + 32 * (kSlots * m + slot) + 16 * wgi, a[m]);
-            cp_async_wait2();                 // this thread's copies of window win
+            cp_async_wait<kAhead>();          // this thread's copies of window win
             fence_proxy_async();
             tmem_wait_st();
             tc_fence_before();
@@ -324,21 +339,18 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
             ++ps.gb;
         }
         // next half chunk
-        const int hn = (hw >> 1) + 2;
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
-            cc[m] = nc[m];
-            cs[m] = ns[m];
-            if (rows_ok && hn < 2 * C) {
-                const uint8_t *p = cbase[m] + (long long)(hn >> 1) * 2048 + (hn & 1) * 1024;
-                nc[m] = ldg_stream_v4(p);
-                ns[m] = ldg_stream_u32(sbase[m] + (long long)(hn >> 1) * 128 + (hn & 1) * 64);
-            }
+            cc[m] = nc1[m];
+            cs[m] = ns1[m];
+            nc1[m] = nc2[m];
+            ns1[m] = ns2[m];
+            load_half((hw >> 1) + 3, m, nc2[m], ns2[m]);
         }
     }
     // ---- the windows still owed a stage wait (the loop waited for windows
-    // 0 .. NW-5 while refilling; NW is a multiple of 4): then all MMAs are done
-    for (int win = (NW > 4 ? NW - 4 : 0); win < NW; ++win) {
+    // 0 .. NW - kStages - 1 while refilling): then all MMAs are done
+    for (int win = (NW > kStages ? NW - kStages : 0); win < NW; ++win) {
         const int s2 = win % kStages;
         mbar_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
         ++ps.sw[s2];
@@ -357,8 +369,9 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
             for (int jj = 0; jj < 32; ++jj) {
                 const int p = sh.pairs[32 * q + jj];
                 if (p < 0) continue;
-                r.out[(size_t)p * OUT + row] = epilogue_value<DUAL>(
-                    __uint_as_float(dv[0][jj]), __uint_as_float(dv[NMAT - 1][jj]), r.pair_scale, p, r.out_f16);
+                r.out[(size_t)p * OUT + row] =
+                    epilogue_value_s<DUAL>(__uint_as_float(dv[0][jj]), __uint_as_float(dv[NMAT - 1][jj]),
+                                           r.pair_scale != nullptr, sh.pscale[32 * q + jj], r.out_f16);
             }
         }
     }
@@ -404,12 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
     __shared__ Shared sh;
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x;
-    uint8_t *cbA = smem, *cbB = smem + kCbRegion, *xs = smem + 2 * kCbRegion;
-    if (a.has1) {
-        stage_codebook(cbA, a.s1.w0, 0);
-        stage_codebook(cbA, a.s1.w1, 1);
-    }
-    stage_codebook(cbB, a.s2.w0, 0);
+    uint8_t *cb = smem, *xs = smem + kCbRegion;
     if (tid == 0) {
         for (int i = 0; i < kSlots; ++i) mbar_init(&sh.slot[i]);
         for (int i = 0; i < kStages; ++i) mbar_init(&sh.stage[i]);
@@ -433,6 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
     tile_prefix(a, sh, nact, rt1, rt2);
     const int n1 = a.has1 ? sh.pre1[nact] : 0, n2 = sh.pre2[nact];
     Pipe ps{};
+    int cb_phase = 0;                         // the phase whose codebooks are staged
     if (tid == 0) sh.next = (int)atomicAdd(a.ctl, 1u);
     __syncthreads();
     for (;;) {
@@ -475,14 +484,26 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
         }
         __syncthreads();
         const TileInfo in = sh.info;
+        if (in.phase != cb_phase) {
+            // a CTA's tiles go phase 1, then phase 2: (re)stage the codebooks
+            // once per phase; every lookup of the previous tile is done
+            if (in.phase == 1) {
+                stage_codebook(cb, a.s1.w0, 0);
+                stage_codebook(cb, a.s1.w1, 1);
+            } else {
+                stage_codebook(cb, a.s2.w0, 0);
+            }
+            cb_phase = in.phase;
+            __syncthreads();
+        }
         if (in.phase == 1) {
-            pf_tile<2>(a.s1, in, smem_u32(cbA), xs, sh, tmem, ps, err);
+            pf_tile<2>(a.s1, in, smem_u32(cb), xs, sh, tmem, ps, err);
             if (tid == 0) {
                 __threadfence();
                 atomicAdd(a.ctl + 2 + in.ai, 1u);
             }
         } else {
-            pf_tile<1>(a.s2, in, smem_u32(cbB), xs, sh, tmem, ps, err);
+            pf_tile<1>(a.s2, in, smem_u32(cb), xs, sh, tmem, ps, err);
         }
     }
     tc_fence_before();
@@ -528,11 +549,11 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_prefill_kernel(const D
     constexpr bool DUAL = NMAT == 2;
     constexpr int kStage = (NMAT + 1) * kStageBytes;       // A of each matrix, then B
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ uint64_t s_stage[kStages];
+    __shared__ uint64_t s_stage[kDenseStages];
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) mbar_init(&s_stage[i]);
+        for (int i = 0; i < kDenseStages; ++i) mbar_init(&s_stage[i]);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     constexpr int kCols = DUAL ? 256 : 128;
@@ -551,7 +572,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_prefill_kernel(const D
     const uint32_t sm_s = smem_u32(smem);
     const int rt = (a.OUT + 127) / 128, nbk = (a.T + kN - 1) / kN;
     const int NW = a.IN / kWin;
-    uint32_t sw[kStages] = {0u, 0u, 0u, 0u};
+    uint32_t sw[kDenseStages] = {};
     bool failed = false;
     const int ch = tid & 7, n0 = tid >> 3;
     for (int tile = blockIdx.x; tile < rt * nbk; tile += gridDim.x) {
@@ -571,7 +592,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_prefill_kernel(const D
         }
         const uint32_t dofs = ch * kLbo;
         auto stage = [&](int win) {
-            const uint32_t base = sm_s + (win % kStages) * kStage;
+            const uint32_t base = sm_s + (win % kDenseStages) * kStage;
             const int f = win * kWin;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
@@ -589,7 +610,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_prefill_kernel(const D
         cp_async_commit();
         for (int win = 0; win < NW; ++win) {
             if (win + 2 < NW) {
-                const int s2 = (win + 2) % kStages;
+                const int s2 = (win + 2) % kDenseStages;
                 if (win >= 2) {
                     mbar_wait(&s_stage[s2], sw[s2] & 1, a.err, failed);
                     ++sw[s2];
@@ -597,23 +618,23 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_prefill_kernel(const D
                 stage(win + 2);
             }
             cp_async_commit();
-            cp_async_wait2();
+            cp_async_wait<2>();
             fence_proxy_async();
             __syncthreads();
             if (tid == 0) {
                 tc_fence_after();
-                const uint32_t base = sm_s + (win % kStages) * kStage;
+                const uint32_t base = sm_s + (win % kDenseStages) * kStage;
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m)
 #pragma unroll
                     for (int k16 = 0; k16 < 4; ++k16)
                         tc_mma_ss(tmem + 128 * m, b_desc(base + m * kStageBytes + 2 * k16 * kLbo),
                                   b_desc(base + NMAT * kStageBytes + 2 * k16 * kLbo), win > 0 || k16 > 0);
-                tc_commit(&s_stage[win % kStages]);
+                tc_commit(&s_stage[win % kDenseStages]);
             }
         }
         for (int win = (NW > 4 ? NW - 4 : 0); win < NW; ++win) {
-            const int s2 = win % kStages;
+            const int s2 = win % kDenseStages;
             mbar_wait(&s_stage[s2], sw[s2] & 1, a.err, failed);
             ++sw[s2];
         }
@@ -674,7 +695,7 @@ vqmoe_status launch_dense_prefill(const void *x, const void *w0, const void *w1,
                                   void *out, uint32_t *err, cudaStream_t stream) {
     static bool configured[2][64] = {{false}};
     const int nmat = w1 ? 2 : 1;
-    const size_t smem = (size_t)pf::kStages * (nmat + 1) * pf::kStageBytes;
+    const size_t smem = (size_t)pf::kDenseStages * (nmat + 1) * pf::kStageBytes;
     int dev = 0;
     cudaGetDevice(&dev);
     auto fn = nmat == 2 ? pf::dense_prefill_kernel<2> : pf::dense_prefill_kernel<1>;

@@ -50,6 +50,21 @@ __device__ __forceinline__ uint16_t epilogue_value(float g, float u, const float
     return f32_to_bf16(v);
 }
 
+// epilogue_value with the routing weight already in hand (scaled: multiply
+// by s), for callers that stage the weights of a tile in shared memory
+template <bool DUAL>
+__device__ __forceinline__ uint16_t epilogue_value_s(float g, float u, bool scaled, float s, int out_f16) {
+    float v;
+    if (DUAL) {
+        v = bf16r(bf16r(silu_f32(bf16r(g))) * bf16r(u));
+    } else {
+        v = bf16r(g);
+        if (scaled) v = bf16r(v * s);
+    }
+    if (out_f16) return bf16_to_f16_sat(f32_to_bf16(v));
+    return f32_to_bf16(v);
+}
+
 struct TileInfo {
     int phase;      // 1: gate/up, 2: down / single linear
     int ai;         // index among the active experts
