@@ -29,6 +29,8 @@
 // (tcgen05.ld) and applies the SwiGLU / routing weight.
 #include <algorithm>
 
+#include <cuda_bf16.h>
+
 #include "experts.cuh"
 #include "layout.cuh"
 #include "stages.cuh"
@@ -36,7 +38,8 @@
 namespace vqmoe {
 namespace pf {
 
-constexpr int kThreads = 256;                 // two warpgroups, each over TMEM lanes 0..127
+constexpr int kProducers = 256;               // two warpgroups, each over TMEM lanes 0..127
+constexpr int kThreads = kProducers + 32;     // + one warp that issues the MMAs
 constexpr int kDenseThreads = 128;            // the dense kernel: one warpgroup
 constexpr int kDenseStages = 4;               // its operand windows in shared memory (2 ahead)
 constexpr int kN = 128;                       // pairs per tile (MMA N)
@@ -67,8 +70,11 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
-__device__ __forceinline__ void mbar_init(uint64_t *bar) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(bar)) : "memory");
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
 // Bounded wait for the phase of parity `parity`: at most kPoll try_waits of
 // at most kSuspendNs each; on running out raise the error flag and skip
@@ -89,6 +95,14 @@ __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, uint32
     }
     failed = true;
     atomicExch(err, 2u);
+}
+// mbar_wait by lane 0 of the warp, the other lanes held at __syncwarp
+__device__ __forceinline__ void warp_wait(uint64_t *bar, uint32_t parity, uint32_t *err, bool &failed) {
+    if ((threadIdx.x & 31) == 0) mbar_wait(bar, parity, err, failed);
+    __syncwarp();
+}
+__device__ __forceinline__ float bf16r_hw(float f) {
+    return __bfloat162float(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ void tc_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
@@ -172,8 +186,10 @@ __device__ __forceinline__ void stage_codebook(uint8_t *region, const LinearDev 
 }
 
 struct Shared {
+    uint64_t full[kSlots];                    // an A slot and its window's x stage written
     uint64_t slot[kSlots];                    // MMAs done reading an A slot
     uint64_t stage[kStages];                  // MMAs done reading an x stage
+    uint64_t acc;                             // a tile's MMAs done: accumulators final
     TileInfo info;
     int next;
     int pairs[kN];
@@ -191,18 +207,75 @@ struct Pipe {
 };
 
 // ----------------------------------------------------------------- tile
-// One tile. Thread tid stages, in every window, the 16-byte chunk tid % 8 of
-// the 4 pair slots tid / 8 + 32q (q = 0..3): its row pointers are computed
-// once per tile. One A batch is one 64-input window.
+// The epilogue of one accumulator pair: _SwiGLU (qwen3_5.py:108-112),
+// bf16(bf16(silu(g)) * u) with g and u the bf16 outputs of the gate and up
+// matmuls, or bf16(bf16(y) * routing weight); the conversions are the
+// hardware's round-to-nearest-even (the same bits as the software rounding
+// of the other kernels for every finite value).
+template <bool DUAL>
+__device__ __forceinline__ uint16_t pf_value(float g, float u, bool scaled, float s, int out_f16) {
+    float v;
+    if (DUAL) {
+        const float gb = bf16r_hw(g);
+        v = bf16r_hw(bf16r_hw(gb / (1.0f + expf(-gb))) * bf16r_hw(u));
+    } else {
+        v = bf16r_hw(g);
+        if (scaled) v = bf16r_hw(v * s);
+    }
+    if (out_f16) return __half_as_ushort(__float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f)));
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// One tile. The producer warps (0..7): thread tid stages, in every window,
+// the 16-byte chunk tid % 8 of the 4 pair slots tid / 8 + 32q (q = 0..3),
+// with row pointers computed once per tile; each lane dequantises its weight
+// row's half of the window into the A slot; one lane per warp then arrives
+// on the slot's `full` barrier. The MMA warp (8) waits on `full`, multiplies
+// and commits the slot, the x stage and, after the last window, the
+// accumulators. One A batch is one 64-input window.
 template <int NMAT>
 __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, uint32_t cb_s, uint8_t *xs,
                                         Shared &sh, uint32_t tmem, Pipe &ps, uint32_t *err) {
     constexpr bool DUAL = NMAT == 2;
     const int tid = threadIdx.x, warp = (tid >> 5) & 3, lane = tid & 31;
-    const int wgi = tid >> 7;                 // warpgroup: 8-input chunks 2j + wgi of each window
     const int IN = r.IN, OUT = r.OUT;
     const int C = (IN + 255) >> 8, RB = (OUT + 31) >> 5;
     const int NW = C * 4;                     // 64-input windows
+    const uint32_t xs_s = smem_u32(xs);
+    if (tid < kN) {
+        const int p = tid < in.n ? r.list[in.base + tid] : -1;
+        sh.pairs[tid] = p;
+        sh.pscale[tid] = (!DUAL && r.pair_scale && p >= 0) ? r.pair_scale[p] : 1.0f;
+    }
+    __syncthreads();
+    if (tid >= kProducers) {
+        // ---- the MMA warp
+        if (lane == 0) {
+            uint32_t gb = ps.gb;
+            for (int win = 0; win < NW; ++win, ++gb) {
+                const uint32_t slot = gb % kSlots;
+                mbar_wait(&sh.full[slot], (gb / kSlots) & 1, err, ps.failed);
+                tc_fence_after();
+                const int s = win % kStages;
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                    for (int k16 = 0; k16 < 4; ++k16)
+                        tc_mma(tmem + kDCol + 128 * m, tmem + 32 * (kSlots * m + slot) + 8 * k16,
+                               b_desc(xs_s + s * kStageBytes + (2 * k16) * kLbo), win > 0 || k16 > 0);
+                tc_commit(&sh.slot[slot]);
+                tc_commit(&sh.stage[s]);
+            }
+            tc_commit(&sh.acc);
+        }
+        __syncwarp();
+        ps.gb += NW;
+        tc_fence_before();
+        __syncthreads();
+        return;
+    }
+    // ---- the producer warps
+    const int wgi = tid >> 7;                 // warpgroup: 8-input chunks 2j + wgi of each window
     const int rb = (in.row0 >> 5) + warp;
     const bool rows_ok = rb < RB;
     const int row = rb * 32 + lane;
@@ -221,18 +294,11 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     }
     const uint32_t lanebyte = (lane & 15) * 8;
     const uint32_t t_warp = tmem + ((uint32_t)(warp * 32) << 16);
-    const uint32_t xs_s = smem_u32(xs);
-    if (tid < kN) {
-        const int p = tid < in.n ? r.list[in.base + tid] : -1;
-        sh.pairs[tid] = p;
-        sh.pscale[tid] = (!DUAL && r.pair_scale && p >= 0) ? r.pair_scale[p] : 1.0f;
-    }
-    __syncthreads();
     // ---- this thread's staging: input chunk ch of slots n0 + 32q. The MMA's K
     // order within a window is permuted -- input chunk ch sits at K chunk
     // kch(ch) = 4 (ch & 1) + ch / 2 in both operands -- so that warpgroup wgi
     // dequantises the contiguous A columns 16 wgi .. 16 wgi + 15.
-    constexpr int kQ = kN * 8 / kThreads;     // slots a thread stages per window
+    constexpr int kQ = kN * 8 / kProducers;   // slots a thread stages per window
     const int ch = tid & 7, n0 = tid >> 3;
     const int kch = 4 * (ch & 1) + (ch >> 1);
     const uint16_t *src[kQ];
@@ -240,7 +306,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     uint32_t live = 0;
 #pragma unroll
     for (int q = 0; q < kQ; ++q) {
-        const int n = n0 + (kThreads / 8) * q;
+        const int n = n0 + (kProducers / 8) * q;
         const int p = sh.pairs[n];
         const int xr = p < 0 ? 0 : (r.x_per_pair ? p : p / r.k);
         src[q] = r.x + (size_t)xr * IN + 8 * ch;
@@ -286,7 +352,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
             if (win + kAhead < NW) {
                 const int s2 = (win + kAhead) % kStages;
                 if (win >= 2) {
-                    mbar_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
+                    warp_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
                     ++ps.sw[s2];
                 }
                 const int fw = (win + kAhead) * kWin;
@@ -315,7 +381,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
                     a[m][2 * l + 1] = hmul2_u32(e.y, s2v);
                 }
             }
-            if (ps.gb >= kSlots) mbar_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
+            if (ps.gb >= kSlots) warp_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
             tc_fence_after();
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) tmem_st16(t_warp + 32 * (kSlots * m + slot) + 16 * wgi, a[m]);
@@ -323,19 +389,8 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
             fence_proxy_async();
             tmem_wait_st();
             tc_fence_before();
-            __syncthreads();                  // A stored, window win staged, by everyone
-            if (tid == 0) {
-                tc_fence_after();
-                const int s = win % kStages;
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-                    for (int k16 = 0; k16 < 4; ++k16)
-                        tc_mma(tmem + kDCol + 128 * m, tmem + 32 * (kSlots * m + slot) + 8 * k16,
-                               b_desc(xs_s + s * kStageBytes + (2 * k16) * kLbo), win > 0 || k16 > 0);
-                tc_commit(&sh.slot[slot]);
-                tc_commit(&sh.stage[s]);
-            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.full[slot]);
             ++ps.gb;
         }
         // next half chunk
@@ -348,11 +403,13 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
             load_half((hw >> 1) + 3, m, nc2[m], ns2[m]);
         }
     }
-    // ---- the windows still owed a stage wait (the loop waited for windows
-    // 0 .. NW - kStages - 1 while refilling): then all MMAs are done
+    // ---- the tile's MMAs done; then the stage commits the loop did not wait
+    // for (windows NW - kStages .. NW - 1), already complete
+    warp_wait(&sh.acc, ps.dn & 1, err, ps.failed);
+    ++ps.dn;
     for (int win = (NW > kStages ? NW - kStages : 0); win < NW; ++win) {
         const int s2 = win % kStages;
-        mbar_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
+        warp_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
         ++ps.sw[s2];
     }
     tc_fence_after();
@@ -365,13 +422,15 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
         for (int m = 0; m < NMAT; ++m) tmem_ld32(t_warp + kDCol + 128 * m + 32 * q, dv[m]);
         tmem_wait_ld();
         if (rows_ok && row < OUT) {
+            uint16_t ov[32];
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj)
+                ov[jj] = pf_value<DUAL>(__uint_as_float(dv[0][jj]), __uint_as_float(dv[NMAT - 1][jj]),
+                                        r.pair_scale != nullptr, sh.pscale[32 * q + jj], r.out_f16);
 #pragma unroll
             for (int jj = 0; jj < 32; ++jj) {
                 const int p = sh.pairs[32 * q + jj];
-                if (p < 0) continue;
-                r.out[(size_t)p * OUT + row] =
-                    epilogue_value_s<DUAL>(__uint_as_float(dv[0][jj]), __uint_as_float(dv[NMAT - 1][jj]),
-                                           r.pair_scale != nullptr, sh.pscale[32 * q + jj], r.out_f16);
+                if (p >= 0) r.out[(size_t)p * OUT + row] = ov[jj];
             }
         }
     }
@@ -419,8 +478,12 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
     const int tid = threadIdx.x;
     uint8_t *cb = smem, *xs = smem + kCbRegion;
     if (tid == 0) {
-        for (int i = 0; i < kSlots; ++i) mbar_init(&sh.slot[i]);
-        for (int i = 0; i < kStages; ++i) mbar_init(&sh.stage[i]);
+        for (int i = 0; i < kSlots; ++i) {
+            mbar_init(&sh.full[i], kProducers / 32);
+            mbar_init(&sh.slot[i], 1);
+        }
+        for (int i = 0; i < kStages; ++i) mbar_init(&sh.stage[i], 1);
+        mbar_init(&sh.acc, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (tid < 32) {
@@ -553,7 +616,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_prefill_kernel(const D
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int i = 0; i < kDenseStages; ++i) mbar_init(&s_stage[i]);
+        for (int i = 0; i < kDenseStages; ++i) mbar_init(&s_stage[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     constexpr int kCols = DUAL ? 256 : 128;
