@@ -232,11 +232,14 @@ __device__ __forceinline__ uint16_t pf_value(float g, float u, bool scaled, floa
 // row's half of the window into the A slot; one lane per warp then arrives
 // on the slot's `full` barrier. The MMA warp (8) waits on `full`, multiplies
 // and commits the slot, the x stage and, after the last window, the
-// accumulators. One A batch is one 64-input window.
-template <int NMAT>
+// accumulators. One A batch is one 64-input window. Every tile has two A
+// operands: gate and up of 128 rows (GLU), or rows row0 .. row0 + 127 and
+// row0 + 128 .. row0 + 255 of the one matrix (a switch linear / down).
+template <bool GLU>
 __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, uint32_t cb_s, uint8_t *xs,
                                         Shared &sh, uint32_t tmem, Pipe &ps, uint32_t *err) {
-    constexpr bool DUAL = NMAT == 2;
+    constexpr int NMAT = 2;
+    constexpr bool DUAL = GLU;
     const int tid = threadIdx.x, warp = (tid >> 5) & 3, lane = tid & 31;
     const int IN = r.IN, OUT = r.OUT;
     const int C = (IN + 255) >> 8, RB = (OUT + 31) >> 5;
@@ -276,19 +279,21 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     }
     // ---- the producer warps
     const int wgi = tid >> 7;                 // warpgroup: 8-input chunks 2j + wgi of each window
-    const int rb = (in.row0 >> 5) + warp;
-    const bool rows_ok = rb < RB;
-    const int row = rb * 32 + lane;
     const int mt = lane >> 4, hh = (lane >> 3) & 1, g = lane & 7;
-    // this lane's row in the tiled layout: per chunk c, half: codes at
-    // tile*2048 + half*1024 + (2mt+h)*256 + 32g (32 bytes), scales at
-    // tile*128 + half*64 + (2mt+h)*16 + 2g (2 fp16)
+    // this lane's row of operand m in the tiled layout: per chunk c, half:
+    // codes at tile*2048 + half*1024 + (2mt+h)*256 + 32g (32 bytes), scales
+    // at tile*128 + half*64 + (2mt+h)*16 + 2g (2 fp16)
     const uint8_t *cbase[NMAT];
     const uint16_t *sbase[NMAT];
+    bool rows_ok[NMAT];
+    int row[NMAT];
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
-        const LinearDev &w = m == 0 ? r.w0 : r.w1;
-        const long long tile0 = ((long long)in.e * RB + (rows_ok ? rb : 0)) * C;
+        const LinearDev &w = (GLU && m == 1) ? r.w1 : r.w0;
+        const int rb = (in.row0 >> 5) + warp + (GLU ? 0 : 4 * m);
+        rows_ok[m] = rb < RB;
+        row[m] = rb * 32 + lane;
+        const long long tile0 = ((long long)in.e * RB + (rows_ok[m] ? rb : 0)) * C;
         cbase[m] = w.codes + tile0 * 2048 + (2 * mt + hh) * 256 + 32 * g + 16 * wgi;
         sbase[m] = w.scales + tile0 * 128 + (2 * mt + hh) * 16 + 2 * g;
     }
@@ -330,7 +335,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     uint4 cc[NMAT], nc1[NMAT], nc2[NMAT];
     uint32_t cs[NMAT], ns1[NMAT], ns2[NMAT];
     auto load_half = [&](int hn, int m, uint4 &c, uint32_t &sc) {
-        if (rows_ok && hn < 2 * C) {
+        if (rows_ok[m] && hn < 2 * C) {
             c = ldg_stream_v4(cbase[m] + (long long)(hn >> 1) * 2048 + (hn & 1) * 1024);
             sc = ldg_stream_u32(sbase[m] + (long long)(hn >> 1) * 128 + (hn & 1) * 64);
         } else {
@@ -376,7 +381,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
                 for (int l = 0; l < 8; ++l) {
                     const int j = l >> 1, sb = l & 1;
                     const uint32_t ad = __byte_perm(words[2 * sb + ww], lanebyte, 0x5504u | (j << 4));
-                    const uint2 e = lds64(cb_s + m * 128 + ad);
+                    const uint2 e = lds64(cb_s + (GLU ? m * 128 : 0) + ad);
                     a[m][2 * l] = hmul2_u32(e.x, s2v);
                     a[m][2 * l + 1] = hmul2_u32(e.y, s2v);
                 }
@@ -421,16 +426,19 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) tmem_ld32(t_warp + kDCol + 128 * m + 32 * q, dv[m]);
         tmem_wait_ld();
-        if (rows_ok && row < OUT) {
-            uint16_t ov[32];
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj)
-                ov[jj] = pf_value<DUAL>(__uint_as_float(dv[0][jj]), __uint_as_float(dv[NMAT - 1][jj]),
-                                        r.pair_scale != nullptr, sh.pscale[32 * q + jj], r.out_f16);
+        for (int m = 0; m < (GLU ? 1 : NMAT); ++m) {
+            if (rows_ok[m] && row[m] < OUT) {
+                uint16_t ov[32];
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-                const int p = sh.pairs[32 * q + jj];
-                if (p >= 0) r.out[(size_t)p * OUT + row] = ov[jj];
+                for (int jj = 0; jj < 32; ++jj)
+                    ov[jj] = pf_value<GLU>(__uint_as_float(dv[m][jj]), __uint_as_float(dv[1][jj]),
+                                           r.pair_scale != nullptr, sh.pscale[32 * q + jj], r.out_f16);
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int p = sh.pairs[32 * q + jj];
+                    if (p >= 0) r.out[(size_t)p * OUT + row[m]] = ov[jj];
+                }
             }
         }
     }
@@ -500,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
     uint32_t *err = a.ctl + 1;
     const int nact = min(a.s2.active[a.s2.E], kMaxE);
     const int rt1 = a.has1 ? (a.s1.OUT + 127) / 128 : 0;
-    const int rt2 = (a.s2.OUT + 127) / 128;
+    const int rt2 = (a.s2.OUT + 255) / 256;     // phase 2 tiles: 256 rows
     tile_prefix(a, sh, nact, rt1, rt2);
     const int n1 = a.has1 ? sh.pre1[nact] : 0, n2 = sh.pre2[nact];
     Pipe ps{};
@@ -522,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
             in.e = a.s2.active[in.ai];
             const int v = u - pre[in.ai];
             const int blk = v / rt;
-            in.row0 = (v - blk * rt) * 128;
+            in.row0 = (v - blk * rt) * (p1 ? 128 : 256);
             const int cnt = a.s2.cnt[in.e];
             in.base = a.s2.off[in.e] + blk * kN;
             in.n = min(kN, cnt - blk * kN);
@@ -560,13 +568,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
             __syncthreads();
         }
         if (in.phase == 1) {
-            pf_tile<2>(a.s1, in, smem_u32(cb), xs, sh, tmem, ps, err);
+            pf_tile<true>(a.s1, in, smem_u32(cb), xs, sh, tmem, ps, err);
             if (tid == 0) {
                 __threadfence();
                 atomicAdd(a.ctl + 2 + in.ai, 1u);
             }
         } else {
-            pf_tile<1>(a.s2, in, smem_u32(cb), xs, sh, tmem, ps, err);
+            pf_tile<false>(a.s2, in, smem_u32(cb), xs, sh, tmem, ps, err);
         }
     }
     tc_fence_before();

@@ -189,19 +189,20 @@ def test_block_beyond_one_launch_of_tokens():
     assert_bf16_close(y_tail, ref, "alone")
 
 
-@pytest.mark.parametrize("zipf", [0.0, 1.1])
-def test_prefill_block_matches_oracle(zipf):
+@pytest.mark.parametrize("zipf,hidden,inter", [(0.0, 512, 256), (1.1, 512, 256), (1.1, 384, 320)])
+def test_prefill_block_matches_oracle(zipf, hidden, inter):
     """Many pairs per expert (about 256 here): the routed experts take the
     tcgen05 grouped-GEMM path (128-pair tiles, partial last tiles, a Zipf
     load imbalance), and the shared expert (192 rows: a partial row tile) the
-    tcgen05 dense GEMMs."""
-    cfg = synth.MoEConfig("pf", 16, 4, 512, 256, 192, 1024, router="uniform", zipf=zipf)
+    tcgen05 dense GEMMs. hidden = 384: the last 256-row down tile is half
+    out of range; inter = 320: down's inputs end inside a 256-input chunk."""
+    cfg = synth.MoEConfig("pf", 16, 4, hidden, inter, 192, 1024, router="uniform", zipf=zipf)
     w = synth.make_weights(cfg, seed=17, scales="random")
     x = synth.make_input(cfg, seed=17)
     blk = SparseMoeBlock.from_weights(_cuda(w), cfg.top_k)
     y = to_np(blk(x.to(DEV)))
     ref = R.sparse_moe_block(to_np(x), oracle_params(w), cfg.top_k, vq=True)
-    assert_bf16_close(y, ref, f"prefill zipf={zipf}")
+    assert_bf16_close(y, ref, f"prefill zipf={zipf} H={hidden} I={inter}")
 
 
 def test_small_codebook_and_idle_experts():
