@@ -29,8 +29,6 @@
 // (tcgen05.ld) and applies the SwiGLU / routing weight.
 #include <algorithm>
 
-#include <cuda_bf16.h>
-
 #include "experts.cuh"
 #include "layout.cuh"
 #include "stages.cuh"
@@ -46,7 +44,7 @@ constexpr int kN = 128;                       // pairs per tile (MMA N)
 constexpr int kSlots = 4;                     // A slots per matrix (a 64-input window each)
 constexpr int kWin = 64;                      // inputs per x window
 constexpr int kStages = 8;                    // x windows in shared memory
-constexpr int kAhead = kStages - 2;           // x windows gathered ahead of the one multiplied
+constexpr int kAhead = 4;                     // x windows gathered ahead of the one multiplied
 constexpr int kStageBytes = kN * kWin * 2;    // 16 KB
 constexpr int kLbo = (kN / 8) * 128;          // bytes from one 8-input chunk to the next
 constexpr int kCbRegion = 65536;              // the phase's codebooks: gate / up, then down
@@ -100,9 +98,6 @@ __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, uint32
 __device__ __forceinline__ void warp_wait(uint64_t *bar, uint32_t parity, uint32_t *err, bool &failed) {
     if ((threadIdx.x & 31) == 0) mbar_wait(bar, parity, err, failed);
     __syncwarp();
-}
-__device__ __forceinline__ float bf16r_hw(float f) {
-    return __bfloat162float(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ void tc_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
@@ -207,23 +202,43 @@ struct Pipe {
 };
 
 // ----------------------------------------------------------------- tile
-// The epilogue of one accumulator pair: _SwiGLU (qwen3_5.py:108-112),
-// bf16(bf16(silu(g)) * u) with g and u the bf16 outputs of the gate and up
-// matmuls, or bf16(bf16(y) * routing weight); the conversions are the
-// hardware's round-to-nearest-even (the same bits as the software rounding
-// of the other kernels for every finite value).
-template <bool DUAL>
-__device__ __forceinline__ uint16_t pf_value(float g, float u, bool scaled, float s, int out_f16) {
-    float v;
-    if (DUAL) {
-        const float gb = bf16r_hw(g);
-        v = bf16r_hw(bf16r_hw(gb / (1.0f + expf(-gb))) * bf16r_hw(u));
+// Two accumulators -> two packed outputs (the first in the low half).
+// _SwiGLU (qwen3_5.py:108-112): bf16(bf16(silu(g)) * u) with g and u the
+// bf16 outputs of the gate and up matmuls; otherwise bf16(bf16(y) * routing
+// weight). Every rounding is the hardware's round-to-nearest-even
+// (cvt.rn.bf16x2), the same bits as the software rounding of the other
+// kernels for finite values; a bf16 x bf16 product is exact in float32. The
+// one approximation: silu's exp and division are the fast forms (ex2 /
+// rcp, a few float32 ulp before the bf16 rounding).
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+template <bool GLU>
+__device__ __forceinline__ uint32_t pf_value2(uint32_t g0, uint32_t g1, uint32_t u0, uint32_t u1, bool scaled,
+                                              float s0, float s1, int out_f16) {
+    const uint32_t gb = cvt_bf16x2(__uint_as_float(g0), __uint_as_float(g1));
+    uint32_t v;
+    if (GLU) {
+        const uint32_t ub = cvt_bf16x2(__uint_as_float(u0), __uint_as_float(u1));
+        const uint32_t sb = cvt_bf16x2(silu_fast(bf_lo(gb)), silu_fast(bf_hi(gb)));
+        v = cvt_bf16x2(bf_lo(sb) * bf_lo(ub), bf_hi(sb) * bf_hi(ub));
     } else {
-        v = bf16r_hw(g);
-        if (scaled) v = bf16r_hw(v * s);
+        v = scaled ? cvt_bf16x2(bf_lo(gb) * s0, bf_hi(gb) * s1) : gb;
     }
-    if (out_f16) return __half_as_ushort(__float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f)));
-    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    if (out_f16)
+        return cvt_f16x2(fminf(fmaxf(bf_lo(v), -65504.0f), 65504.0f), fminf(fmaxf(bf_hi(v), -65504.0f), 65504.0f));
+    return v;
 }
 
 // One tile. The producer warps (0..7): thread tid stages, in every window,
@@ -353,10 +368,11 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
 #pragma unroll
         for (int ww = 0; ww < 2; ++ww) {
             const int win = hw + ww;
-            // refill: window win + kAhead into the stage window win - 2 used
+            // refill: window win + kAhead into the stage that window
+            // win + kAhead - kStages used (its MMAs must be done)
             if (win + kAhead < NW) {
                 const int s2 = (win + kAhead) % kStages;
-                if (win >= 2) {
+                if (win >= kStages - kAhead) {
                     warp_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
                     ++ps.sw[s2];
                 }
@@ -429,15 +445,16 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
 #pragma unroll
         for (int m = 0; m < (GLU ? 1 : NMAT); ++m) {
             if (rows_ok[m] && row[m] < OUT) {
-                uint16_t ov[32];
+                uint32_t ov[16];
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj)
-                    ov[jj] = pf_value<GLU>(__uint_as_float(dv[m][jj]), __uint_as_float(dv[1][jj]),
-                                           r.pair_scale != nullptr, sh.pscale[32 * q + jj], r.out_f16);
+                for (int jp = 0; jp < 16; ++jp)
+                    ov[jp] = pf_value2<GLU>(dv[m][2 * jp], dv[m][2 * jp + 1], dv[1][2 * jp], dv[1][2 * jp + 1],
+                                            r.pair_scale != nullptr, sh.pscale[32 * q + 2 * jp],
+                                            sh.pscale[32 * q + 2 * jp + 1], r.out_f16);
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) {
                     const int p = sh.pairs[32 * q + jj];
-                    if (p >= 0) r.out[(size_t)p * OUT + row[m]] = ov[jj];
+                    if (p >= 0) r.out[(size_t)p * OUT + row[m]] = (uint16_t)(ov[jj >> 1] >> (16 * (jj & 1)));
                 }
             }
         }
