@@ -32,14 +32,14 @@
 #include "experts.cuh"
 #include "layout.cuh"
 #include "stages.cuh"
+#include "tcgen05.cuh"
 
 namespace vqmoe {
 namespace pf {
+using namespace tc;
 
 constexpr int kProducers = 256;               // two warpgroups, each over TMEM lanes 0..127
 constexpr int kThreads = kProducers + 32;     // + one warp that issues the MMAs
-constexpr int kDenseThreads = 128;            // the dense kernel: one warpgroup
-constexpr int kDenseStages = 4;               // its operand windows in shared memory (2 ahead)
 constexpr int kN = 128;                       // pairs per tile (MMA N)
 constexpr int kSlots = 4;                     // A slots per matrix (a 64-input window each)
 constexpr int kWin = 64;                      // inputs per x window
@@ -53,57 +53,10 @@ constexpr int kDCol = 2 * kSlots * 32;        // D of matrix m at kDCol + 128m (
 constexpr int kAllocCols = 512;
 constexpr int kMaxE = 512;
 constexpr long kSpin = 1L << 22;
-constexpr int kPoll = 10000;
-constexpr uint32_t kSuspendNs = 20000;
 // kind::f16, D f32, A f16, B f16, both K-major, N = 128, M = 128
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kN >> 3) << 17) | ((128u >> 4) << 24);
 
 // ---------------------------------------------------------------- PTX
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
-}
-// Bounded wait for the phase of parity `parity`: at most kPoll try_waits of
-// at most kSuspendNs each; on running out raise the error flag and skip
-// every later wait (results then wrong, and flagged, but nothing hangs).
-__device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err, bool &failed) {
-    if (failed) return;
-    const uint32_t a = smem_u32(bar);
-    for (int i = 0; i < kPoll; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}\n"
-            : "=r"(done)
-            : "r"(a), "r"(parity), "r"(kSuspendNs)
-            : "memory");
-        if (done) return;
-    }
-    failed = true;
-    atomicExch(err, 2u);
-}
-// mbar_wait by lane 0 of the warp, the other lanes held at __syncwarp
-__device__ __forceinline__ void warp_wait(uint64_t *bar, uint32_t parity, uint32_t *err, bool &failed) {
-    if ((threadIdx.x & 31) == 0) mbar_wait(bar, parity, err, failed);
-    __syncwarp();
-}
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
 __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -111,44 +64,6 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint32_t tmem_a, uint64_
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
         "r"(tmem_a), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
         : "memory");
-}
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-        "%12, %13, %14, %15, %16};\n" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, "
-        "%31, %32};\n" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
-        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
-        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() {
-    asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
-        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
-        "[%32];\n"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-          "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
-          "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
-          "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(taddr)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 // B operand descriptor, K-major, no swizzle: core matrices of 8 pairs x 8
 // inputs (16 bytes a pair); SBO = 128 (the next 8 pairs), LBO = kLbo (the
@@ -210,20 +125,6 @@ struct Pipe {
 // kernels for finite values; a bf16 x bf16 product is exact in float32. The
 // one approximation: silu's exp and division are the fast forms (ex2 /
 // rcp, a few float32 ulp before the bf16 rounding).
-__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
-    uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-}
-__device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
-    uint32_t r;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-}
-__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
-
 template <bool GLU>
 __device__ __forceinline__ uint32_t pf_value2(uint32_t g0, uint32_t g1, uint32_t u0, uint32_t u1, bool scaled,
                                               float s0, float s1, int out_f16) {
@@ -604,158 +505,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
     }
 }
 
-// ------------------------------------------------------- dense (bf16)
-// The shared expert's matmuls for many tokens (qwen3_5.py:184-185): out[T,
-// OUT] = epilogue(x[T, IN] . W^T) with bf16 W (and a second matrix for the
-// fused gate/up + SwiGLU). Tiles of 128 weight rows x 128 tokens, spread over
-// the CTAs round robin; per 64-input window both operands -- weight rows (A)
-// and token rows (B) -- are staged with cp.async into a 4-stage ring in the
-// K-major no-swizzle layout and multiplied from shared memory
-// (tcgen05.mma.kind::f16, bf16 inputs) into TMEM.
-constexpr uint32_t kIdescBf16 =
-    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) | ((128u >> 4) << 24);
-
-struct DenseArgs {
-    const uint16_t *x;           // [T][IN] bf16
-    const uint16_t *w0, *w1;     // [OUT][IN] bf16
-    uint16_t *out;               // [T][OUT] bf16
-    int T, IN, OUT;
-    uint32_t *err;
-};
-
-__device__ __forceinline__ void tc_mma_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdescBf16), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-        : "memory");
-}
-
-template <int NMAT>
-__global__ void __launch_bounds__(kDenseThreads, 1) dense_prefill_kernel(const DenseArgs a) {
-    constexpr bool DUAL = NMAT == 2;
-    constexpr int kStage = (NMAT + 1) * kStageBytes;       // A of each matrix, then B
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ uint64_t s_stage[kDenseStages];
-    __shared__ uint32_t s_tmem;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid == 0) {
-        for (int i = 0; i < kDenseStages; ++i) mbar_init(&s_stage[i], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    }
-    constexpr int kCols = DUAL ? 256 : 128;
-    if (tid < 32) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
-                         smem_u32(&s_tmem)),
-                     "r"(kCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = s_tmem;
-    const uint32_t t_warp = tmem + ((uint32_t)(warp * 32) << 16);
-    const uint32_t sm_s = smem_u32(smem);
-    const int rt = (a.OUT + 127) / 128, nbk = (a.T + kN - 1) / kN;
-    const int NW = a.IN / kWin;
-    uint32_t sw[kDenseStages] = {};
-    bool failed = false;
-    const int ch = tid & 7, n0 = tid >> 3;
-    for (int tile = blockIdx.x; tile < rt * nbk; tile += gridDim.x) {
-        const int row0 = (tile % rt) * 128, t0 = (tile / rt) * kN;
-        // this thread's 8 weight rows / tokens (row n0 + 16q), chunk ch
-        const uint16_t *wsrc[NMAT][8];
-        const uint16_t *xsrc[8];
-        uint32_t wlive = 0, xlive = 0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int n = n0 + 16 * q;
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) wsrc[m][q] = (m == 0 ? a.w0 : a.w1) + (size_t)min(row0 + n, a.OUT - 1) * a.IN + 8 * ch;
-            xsrc[q] = a.x + (size_t)min(t0 + n, a.T - 1) * a.IN + 8 * ch;
-            wlive |= (row0 + n < a.OUT ? 1u : 0u) << q;
-            xlive |= (t0 + n < a.T ? 1u : 0u) << q;
-        }
-        const uint32_t dofs = ch * kLbo;
-        auto stage = [&](int win) {
-            const uint32_t base = sm_s + (win % kDenseStages) * kStage;
-            const int f = win * kWin;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const int n = n0 + 16 * q;
-                const uint32_t d = dofs + (n >> 3) * 128 + (n & 7) * 16;
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m)
-                    cp_async16(base + m * kStageBytes + d, wsrc[m][q] + f, (wlive >> q & 1) ? 16 : 0);
-                cp_async16(base + NMAT * kStageBytes + d, xsrc[q] + f, (xlive >> q & 1) ? 16 : 0);
-            }
-        };
-        stage(0);
-        cp_async_commit();
-        if (NW > 1) stage(1);
-        cp_async_commit();
-        for (int win = 0; win < NW; ++win) {
-            if (win + 2 < NW) {
-                const int s2 = (win + 2) % kDenseStages;
-                if (win >= 2) {
-                    mbar_wait(&s_stage[s2], sw[s2] & 1, a.err, failed);
-                    ++sw[s2];
-                }
-                stage(win + 2);
-            }
-            cp_async_commit();
-            cp_async_wait<2>();
-            fence_proxy_async();
-            __syncthreads();
-            if (tid == 0) {
-                tc_fence_after();
-                const uint32_t base = sm_s + (win % kDenseStages) * kStage;
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-                    for (int k16 = 0; k16 < 4; ++k16)
-                        tc_mma_ss(tmem + 128 * m, b_desc(base + m * kStageBytes + 2 * k16 * kLbo),
-                                  b_desc(base + NMAT * kStageBytes + 2 * k16 * kLbo), win > 0 || k16 > 0);
-                tc_commit(&s_stage[win % kDenseStages]);
-            }
-        }
-        for (int win = (NW > 4 ? NW - 4 : 0); win < NW; ++win) {
-            const int s2 = win % kDenseStages;
-            mbar_wait(&s_stage[s2], sw[s2] & 1, a.err, failed);
-            ++sw[s2];
-        }
-        tc_fence_after();
-        const int row = row0 + 32 * warp + lane;
-#pragma unroll 1
-        for (int q = 0; q < kN / 32; ++q) {
-            uint32_t dv[NMAT][32];
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) tmem_ld32(t_warp + 128 * m + 32 * q, dv[m]);
-            tmem_wait_ld();
-            if (row < a.OUT) {
-#pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int t = t0 + 32 * q + jj;
-                    if (t >= a.T) continue;
-                    a.out[(size_t)t * a.OUT + row] = epilogue_value<DUAL>(
-                        __uint_as_float(dv[0][jj]), __uint_as_float(dv[NMAT - 1][jj]), nullptr, 0, 0);
-                }
-            }
-        }
-        tc_fence_before();
-        __syncthreads();
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (tid < 32) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(s_tmem), "r"(kCols)
-                     : "memory");
-    }
-}
-
 }  // namespace pf
 
 vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream) {
@@ -771,39 +520,6 @@ vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream) {
     }
     pf::expert_prefill_kernel<<<sm_count(), pf::kThreads, pf::kSmem, stream>>>(a);
     return check_launch("expert_prefill_kernel");
-}
-
-}  // namespace vqmoe
-
-namespace vqmoe {
-
-// The shared expert's dense matmul (+ SwiGLU when w1 is set) for many tokens
-// on tcgen05; IN a multiple of 64.
-vqmoe_status launch_dense_prefill(const void *x, const void *w0, const void *w1, int T, int IN, int OUT,
-                                  void *out, uint32_t *err, cudaStream_t stream) {
-    static bool configured[2][64] = {{false}};
-    const int nmat = w1 ? 2 : 1;
-    const size_t smem = (size_t)pf::kDenseStages * (nmat + 1) * pf::kStageBytes;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    auto fn = nmat == 2 ? pf::dense_prefill_kernel<2> : pf::dense_prefill_kernel<1>;
-    if (dev < 0 || dev >= 64 || !configured[nmat - 1][dev]) {
-        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return set_error(VQMOE_LAUNCH_FAILED, "dense prefill kernel: %zu bytes of shared memory", smem);
-        if (dev >= 0 && dev < 64) configured[nmat - 1][dev] = true;
-    }
-    pf::DenseArgs a{};
-    a.x = static_cast<const uint16_t *>(x);
-    a.w0 = static_cast<const uint16_t *>(w0);
-    a.w1 = static_cast<const uint16_t *>(w1 ? w1 : w0);
-    a.out = static_cast<uint16_t *>(out);
-    a.T = T;
-    a.IN = IN;
-    a.OUT = OUT;
-    a.err = err;
-    const int tiles = ((OUT + 127) / 128) * ((T + pf::kN - 1) / pf::kN);
-    fn<<<std::min(tiles, sm_count()), pf::kDenseThreads, smem, stream>>>(a);
-    return check_launch("dense_prefill_kernel");
 }
 
 }  // namespace vqmoe
