@@ -202,6 +202,7 @@ struct BlockWs {
     uint16_t *act_s;
     uint16_t *ybuf;
     uint16_t *sh;
+    uint16_t *xs;        // the prefill path's expert-ordered inputs, or null
     size_t bytes;
 };
 
@@ -221,6 +222,8 @@ static BlockWs carve_block(void *ws, const vqmoe_block *b, int T) {
     w.act_s = c.take<uint16_t>((size_t)T * Is);
     w.ybuf = c.take<uint16_t>((size_t)P * H);
     w.sh = c.take<uint16_t>((size_t)T * H);
+    const bool vq = b->gate.format == VQMOE_FMT_VQ_U8 && b->down.format == VQMOE_FMT_VQ_U8;
+    w.xs = prefill_regime(vq, E, P) ? c.take<uint16_t>((size_t)P * H) : nullptr;
     w.bytes = align_up(c.off, 256);
     return w;
 }
@@ -369,6 +372,7 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
     // the routed experts: gate/up + SwiGLU, then down (x routing weight)
     RoutedIO r1 = routed_io(rt, E, k, P, vq_in ? (const void *)w.x16 : (const void *)x, 0, w.act,
                             vq_dn, nullptr);
+    r1.xs = w.xs;
     RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores);
     s = launch_experts(&b->gate, &b->up, &r1, &b->down, r2, rt.zero, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK) return s;
@@ -387,6 +391,7 @@ struct GluWs {
     uint16_t *x16;
     RouteWs rt;
     uint16_t *act;
+    uint16_t *xs;        // the prefill path's expert-ordered inputs, or null
     size_t bytes;
 };
 
@@ -401,6 +406,8 @@ static GluWs carve_glu(void *ws, const vqmoe_linear *first, const vqmoe_linear *
     const int H = first->in_features, I = first->out_features;
     carve_route(c, w.rt, E, P, H, T, 0);
     w.act = dual ? c.take<uint16_t>((size_t)P * I) : nullptr;
+    const bool vq = first->format == VQMOE_FMT_VQ_U8 && (!dual || down->format == VQMOE_FMT_VQ_U8);
+    w.xs = prefill_regime(vq, E, P) ? c.take<uint16_t>((size_t)P * H) : nullptr;
     w.bytes = align_up(c.off, 256);
     return w;
 }
@@ -539,6 +546,7 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
             return s;
         RoutedIO r1 = routed_io(rt, E, top_k, P, vq_in ? (const void *)w.x16 : (const void *)xt, 0,
                                 w.act, vq_dn, nullptr);
+        r1.xs = w.xs;
         RoutedIO r2 = routed_io(rt, E, top_k, P, w.act, 1,
                                 static_cast<uint16_t *>(y) + (size_t)t0 * top_k * H, 0, nullptr);
         if ((s = launch_experts(gate, up, &r1, down, r2, rt.zero, st)) != VQMOE_OK) return s;
@@ -576,6 +584,7 @@ vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x
         RoutedIO r = routed_io(rt, E, top_k, P, vq ? (const void *)ws.x16 : (const void *)xt,
                                x_per_pair, static_cast<uint16_t *>(y) + (size_t)t0 * top_k * w->out_features,
                                0, nullptr);
+        r.xs = ws.xs;
         if ((s = launch_experts(nullptr, nullptr, nullptr, w, r, rt.zero, st)) != VQMOE_OK) return s;
     }
     return VQMOE_OK;

@@ -25,6 +25,7 @@
 
 #include "stages.cuh"
 #include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace vqmoe {
 namespace dn {
@@ -55,13 +56,6 @@ struct Args {
     uint32_t *err;
 };
 
-// Shared-memory descriptor of a K-major operand tile with the 128-byte
-// swizzle: 8-row groups of 128-byte rows, 1024 bytes apart (SBO); the K16
-// step k starts 32k bytes into the row.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           (1ull << 46) | (2ull << 61);
-}
 __device__ __forceinline__ void mma_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -70,20 +64,6 @@ __device__ __forceinline__ void mma_ss(uint32_t tmem_d, uint64_t adesc, uint64_t
         "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-// 2-D tensor copy global -> shared, completing on `bar` (no multicast)
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
-                                            uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
-        "%4}], [%2];\n" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
-        : "memory");
-}
-
 template <int NMAT>
 __global__ void __launch_bounds__(kThreads, 1)
     dense_tma_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
@@ -218,32 +198,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- host
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            p = nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }();
-    return fn;
-}
-
-// [rows][cols] bf16, row-major; boxes of 128 rows x 64 columns, 128-byte swizzle
-bool make_map(CUtensorMap *m, const void *base, int rows, int cols) {
-    auto fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kWin, 128};
-    const cuuint32_t es[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <int NMAT>
 vqmoe_status launch(const void *x, const void *w0, const void *w1, int T, int IN, int OUT, void *out,
                     uint32_t *err, cudaStream_t stream) {
@@ -259,7 +213,8 @@ vqmoe_status launch(const void *x, const void *w0, const void *w1, int T, int IN
     });
     if (!ok[dev]) return set_error(VQMOE_LAUNCH_FAILED, "dense prefill kernel: %zu bytes of shared memory", C::kSmem);
     CUtensorMap tx, tw0, tw1;
-    if (!make_map(&tx, x, T, IN) || !make_map(&tw0, w0, OUT, IN) || !make_map(&tw1, NMAT == 2 ? w1 : w0, OUT, IN))
+    if (!make_tma_map(&tx, x, T, IN, kTok) || !make_tma_map(&tw0, w0, OUT, IN, kRows) ||
+        !make_tma_map(&tw1, NMAT == 2 ? w1 : w0, OUT, IN, kRows))
         return set_error(VQMOE_LAUNCH_FAILED, "dense prefill: tensor map encoding failed (T %d, IN %d, OUT %d)", T,
                          IN, OUT);
     Args a{static_cast<uint16_t *>(out), T, IN, OUT, err};
@@ -269,6 +224,31 @@ vqmoe_status launch(const void *x, const void *w0, const void *w1, int T, int IN
 }
 
 }  // namespace dn
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+bool make_tma_map(CUtensorMap *m, const void *base, int rows, int cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn || rows <= 0 || cols <= 0 || (cols * 2) % 16 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 // The shared expert's dense matmul (+ SwiGLU when w1 is set) for many tokens
 // on tcgen05 with TMA; IN a multiple of 64, every pointer 16-byte aligned.

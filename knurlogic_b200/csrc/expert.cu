@@ -64,7 +64,6 @@ namespace vqmoe {
 constexpr int kThreads = 256;               // 8 warps per CTA, 2 CTAs per SM
 // average pairs per expert from which the routed experts take the tcgen05
 // prefill path (expert_prefill.cu) instead of the mma.sync decode path
-constexpr int kPrefillPairsPerExpert = 32;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRepBytes = 256 * 256;        // replicated codebooks (two matrices), 64 KB
 constexpr int kWin = 2048;                  // inputs per staged activation window
@@ -631,8 +630,8 @@ vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, co
     const bool vq2 = w2->format == VQMOE_FMT_VQ_U8;
     const bool vq1 = r1 ? gate->format == VQMOE_FMT_VQ_U8 : vq2;
     // many pairs per expert (prefill): the tcgen05 grouped GEMM
-    if (vq1 && vq2 && r2.E <= 512 && (long long)r2.P >= kPrefillPairsPerExpert * (long long)r2.E)
-        return launch_experts_prefill(a, stream);
+    void *xs = r1 ? r1->xs : r2.xs;
+    if (prefill_regime(vq1 && vq2, r2.E, r2.P) && xs) return launch_experts_prefill(a, xs, stream);
     const size_t smem = (vq1 || vq2 ? (size_t)kRepBytes : 0) + (size_t)kXBytes;
     if (vq1) return vq2 ? launch_pipe<true, true>(a, smem, stream) : launch_pipe<true, false>(a, smem, stream);
     return vq2 ? launch_pipe<false, true>(a, smem, stream) : launch_pipe<false, false>(a, smem, stream);

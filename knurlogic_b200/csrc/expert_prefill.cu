@@ -1,6 +1,6 @@
 // Routed VQ experts in the prefill regime on the 5th-generation tensor cores
-// (tcgen05 + TMEM): a token-permuted grouped GEMM with the VQ dequantisation
-// fused into the operand path.
+// (tcgen05 + TMEM + TMA): a token-permuted grouped GEMM with the VQ
+// dequantisation fused into the operand path.
 //
 // Reference: SwitchGLU.__call__ (glm5_next/_mlx_vlm/models/switch_layers.py:
 // 172-193; with many pairs the reference sorts them by expert,
@@ -8,48 +8,53 @@
 // (engine/families/deepseek/heads/deepseek_v4.py:35-42, 111-130) and the
 // _SwiGLU activation (qwen3_5.py:108-112).
 //
-// One persistent CTA of two warpgroups per SM. It takes tiles of (expert, 128
-// weight rows, 128 of the expert's pairs) from a global counter -- phase 1
-// (gate/up + SwiGLU) tiles first, then phase 2 (down x routing weight, or a
-// single switch linear); a phase 2 tile of expert e waits until every phase
-// 1 tile of e is done (bounded wait, error flag on expiry).
+// Before the kernel, permute_rows_kernel copies the pairs' fp16 input rows
+// into expert order (the routing sort's order), so that the 128 pairs of a
+// tile are 128 consecutive rows; the gate/up phase writes its SwiGLU
+// activations in that order too, so the down phase reads them the same way.
 //
-// Per tile, for each 64-input window: the warps gather the pairs' input rows
-// (fp16) with cp.async into a 4-stage shared-memory ring, in the canonical
-// K-major no-swizzle layout of the MMA's B operand (loaded two windows
-// ahead). Each lane owns one weight row and half of each window (the two
-// warpgroups take alternate 8-input chunks): it reads the row's codes from
-// the tiled VQ layout (layout.cuh), looks each code up in the shared-memory
-// codebook, multiplies the 4 fp16 weights by the group scale (one rounding:
-// fp16(codebook x scale), the dense dequantisation bit for bit) and stores
-// each 64-input window into a TMEM slot, the MMA's A operand. Lane 0 of the
-// CTA issues tcgen05.mma M=128 x N=128 x K=16 into TMEM accumulators (gate
-// and up: 128 columns each) and commits to the slot's mbarrier (and, after a
-// window, to the window's). The epilogue reads the accumulators back
-// (tcgen05.ld) and applies the SwiGLU / routing weight.
+// One persistent CTA of ten warps per SM takes tiles of (expert, weight
+// rows, 128 of the expert's pairs) from a global counter: phase 1 (gate and
+// up, 128 rows each, + SwiGLU) tiles first, then phase 2 (256 rows of down
+// x routing weight, or of a single switch linear); a phase 2 tile of expert
+// e waits until every phase 1 tile of e is done (bounded wait, error flag on
+// expiry). Every tile has two A operands in TMEM (gate and up, or two
+// 128-row halves) and one B operand (the pairs' inputs) in shared memory:
+//   warps 0-7  producers, warpgroup g dequantising operand g: each lane owns
+//              one weight row, reads its codes from the tiled VQ layout
+//              (layout.cuh), looks each code up in the shared-memory
+//              codebook, multiplies by the group scale (one rounding:
+//              fp16(codebook x scale), the dense dequantisation bit for bit)
+//              and stores each 64-input window into a TMEM slot; then the
+//              epilogue (tcgen05.ld, SwiGLU / routing weight, stores);
+//   warp 8     MMA: tcgen05.mma M=128 x N=128 x K=16, A from TMEM, B from
+//              the SW128 stage, into two 128-column accumulators;
+//   warp 9     TMA: one 2-D tensor copy (128 pairs x 64 inputs) per window
+//              into an 8-stage ring.
 #include <algorithm>
 
 #include "experts.cuh"
 #include "layout.cuh"
 #include "stages.cuh"
 #include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace vqmoe {
 namespace pf {
 using namespace tc;
 
 constexpr int kProducers = 256;               // two warpgroups, each over TMEM lanes 0..127
-constexpr int kThreads = kProducers + 32;     // + one warp that issues the MMAs
+constexpr int kMmaWarp = kProducers / 32;     // 8
+constexpr int kTmaWarp = kMmaWarp + 1;        // 9
+constexpr int kThreads = kProducers + 64;
 constexpr int kN = 128;                       // pairs per tile (MMA N)
-constexpr int kSlots = 4;                     // A slots per matrix (a 64-input window each)
-constexpr int kWin = 64;                      // inputs per x window
+constexpr int kSlots = 4;                     // A slots per operand (a 64-input window each)
+constexpr int kWin = 64;                      // inputs per window
 constexpr int kStages = 8;                    // x windows in shared memory
-constexpr int kAhead = 4;                     // x windows gathered ahead of the one multiplied
-constexpr int kStageBytes = kN * kWin * 2;    // 16 KB
-constexpr int kLbo = (kN / 8) * 128;          // bytes from one 8-input chunk to the next
+constexpr int kStageBytes = kN * kWin * 2;    // 16 KB: 128 pairs x 128 bytes, 128-byte swizzle
 constexpr int kCbRegion = 65536;              // the phase's codebooks: gate / up, then down
-constexpr size_t kSmem = kCbRegion + (size_t)kStages * kStageBytes;
-constexpr int kDCol = 2 * kSlots * 32;        // D of matrix m at kDCol + 128m (all 512 columns)
+constexpr size_t kSmem = (size_t)kStages * kStageBytes + kCbRegion + 1024;   // + 1024-byte alignment
+constexpr int kDCol = 2 * kSlots * 32;        // D of operand m at kDCol + 128m (all 512 columns)
 constexpr int kAllocCols = 512;
 constexpr int kMaxE = 512;
 constexpr long kSpin = 1L << 22;
@@ -65,24 +70,10 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint32_t tmem_a, uint64_
         "r"(tmem_a), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
         : "memory");
 }
-// B operand descriptor, K-major, no swizzle: core matrices of 8 pairs x 8
-// inputs (16 bytes a pair); SBO = 128 (the next 8 pairs), LBO = kLbo (the
-// next 8 inputs).
-__device__ __forceinline__ uint64_t b_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((kLbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)(128u >> 4) << 32) | (1ull << 46);
-}
 __device__ __forceinline__ uint2 lds64(uint32_t saddr) {
     uint2 r;
     asm("ld.shared.v2.u32 {%0, %1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(saddr));
     return r;
-}
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 // 16 interleaved copies: entry c of copy b of matrix m at region + 256c + 128m + 8b
@@ -96,9 +87,10 @@ __device__ __forceinline__ void stage_codebook(uint8_t *region, const LinearDev 
 }
 
 struct Shared {
-    uint64_t full[kSlots];                    // an A slot and its window's x stage written
+    uint64_t full[kSlots];                    // an A slot written by all producer warps
     uint64_t slot[kSlots];                    // MMAs done reading an A slot
-    uint64_t stage[kStages];                  // MMAs done reading an x stage
+    uint64_t xfull[kStages];                  // an x stage landed (TMA transaction count)
+    uint64_t xempty[kStages];                 // MMAs done reading an x stage
     uint64_t acc;                             // a tile's MMAs done: accumulators final
     TileInfo info;
     int next;
@@ -107,11 +99,10 @@ struct Shared {
     int pre1[kMaxE + 1], pre2[kMaxE + 1];     // tiles before active expert i, per phase
 };
 
-// The pipeline state (identical in all threads): batches issued, window
-// commits per stage, tile completions.
+// The pipeline state: windows issued (the same count in every warp) and
+// tiles finished (producers).
 struct Pipe {
     uint32_t gb;
-    uint32_t sw[kStages];
     uint32_t dn;
     bool failed;
 };
@@ -142,48 +133,66 @@ __device__ __forceinline__ uint32_t pf_value2(uint32_t g0, uint32_t g1, uint32_t
     return v;
 }
 
-// One tile. The producer warps (0..7): thread tid stages, in every window,
-// the 16-byte chunk tid % 8 of the 4 pair slots tid / 8 + 32q (q = 0..3),
-// with row pointers computed once per tile; each lane dequantises its weight
-// row's half of the window into the A slot; one lane per warp then arrives
-// on the slot's `full` barrier. The MMA warp (8) waits on `full`, multiplies
-// and commits the slot, the x stage and, after the last window, the
-// accumulators. One A batch is one 64-input window. Every tile has two A
-// operands: gate and up of 128 rows (GLU), or rows row0 .. row0 + 127 and
-// row0 + 128 .. row0 + 255 of the one matrix (a switch linear / down).
+// One tile. Every A batch is one 64-input window: the TMA warp copies the
+// window's 128 x-rows (sorted positions base .. base + 127) into stage gb %
+// kStages; each producer warp stores its 32 rows of its operand into slot gb
+// % kSlots and arrives on `full`; the MMA warp waits for both, multiplies
+// and commits the slot, the stage and, after the last window, the
+// accumulators. Two A operands: gate and up of 128 rows (GLU), or rows
+// row0 .. row0 + 127 and row0 + 128 .. row0 + 255 of the one matrix.
 template <bool GLU>
-__device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, uint32_t cb_s, uint8_t *xs,
-                                        Shared &sh, uint32_t tmem, Pipe &ps, uint32_t *err) {
+__device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, uint32_t cb_s, uint32_t xs_s,
+                                        const void *xmap, Shared &sh, uint32_t tmem, Pipe &ps, uint32_t *err) {
     constexpr int NMAT = 2;
-    constexpr bool DUAL = GLU;
-    const int tid = threadIdx.x, warp = (tid >> 5) & 3, lane = tid & 31;
+    const int tid = threadIdx.x, wid = tid >> 5, lane = tid & 31;
     const int IN = r.IN, OUT = r.OUT;
     const int C = (IN + 255) >> 8, RB = (OUT + 31) >> 5;
-    const int NW = C * 4;                     // 64-input windows
-    const uint32_t xs_s = smem_u32(xs);
+    const int NW = C * 4;                     // 64-input windows (beyond IN: zero-filled, zero weights)
     if (tid < kN) {
         const int p = tid < in.n ? r.list[in.base + tid] : -1;
         sh.pairs[tid] = p;
-        sh.pscale[tid] = (!DUAL && r.pair_scale && p >= 0) ? r.pair_scale[p] : 1.0f;
+        sh.pscale[tid] = (!GLU && r.pair_scale && p >= 0) ? r.pair_scale[p] : 1.0f;
     }
     __syncthreads();
-    if (tid >= kProducers) {
+    if (wid == kTmaWarp) {
+        // ---- the TMA warp
+        if (lane == 0) {
+            // phase 2 reads rows that other CTAs' phase 1 wrote (made
+            // visible by the acquire before this tile's barrier)
+            if (!GLU) fence_proxy_async_global();
+            uint32_t gb = ps.gb;
+            for (int win = 0; win < NW; ++win, ++gb) {
+                const int s = gb % kStages;
+                if (gb >= (uint32_t)kStages) mbar_wait(&sh.xempty[s], ((gb / kStages) + 1) & 1, err, ps.failed);
+                arrive_expect_tx(&sh.xfull[s], kStageBytes);
+                tma_load_2d(xs_s + s * kStageBytes, xmap, win * kWin, in.base, &sh.xfull[s]);
+            }
+        }
+        __syncwarp();
+        ps.gb += NW;
+        tc_fence_before();
+        __syncthreads();
+        return;
+    }
+    if (wid == kMmaWarp) {
         // ---- the MMA warp
         if (lane == 0) {
             uint32_t gb = ps.gb;
             for (int win = 0; win < NW; ++win, ++gb) {
                 const uint32_t slot = gb % kSlots;
+                const int s = gb % kStages;
                 mbar_wait(&sh.full[slot], (gb / kSlots) & 1, err, ps.failed);
+                mbar_wait(&sh.xfull[s], (gb / kStages) & 1, err, ps.failed);
                 tc_fence_after();
-                const int s = win % kStages;
+                const uint32_t xb = xs_s + s * kStageBytes;
 #pragma unroll
-                for (int m = 0; m < NMAT; ++m)
+                for (int k16 = 0; k16 < 4; ++k16)
 #pragma unroll
-                    for (int k16 = 0; k16 < 4; ++k16)
+                    for (int m = 0; m < NMAT; ++m)
                         tc_mma(tmem + kDCol + 128 * m, tmem + 32 * (kSlots * m + slot) + 8 * k16,
-                               b_desc(xs_s + s * kStageBytes + (2 * k16) * kLbo), win > 0 || k16 > 0);
+                               sw128_desc(xb + 32 * k16), win > 0 || k16 > 0);
                 tc_commit(&sh.slot[slot]);
-                tc_commit(&sh.stage[s]);
+                tc_commit(&sh.xempty[s]);
             }
             tc_commit(&sh.acc);
         }
@@ -193,159 +202,91 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
         __syncthreads();
         return;
     }
-    // ---- the producer warps
-    const int wgi = tid >> 7;                 // warpgroup: 8-input chunks 2j + wgi of each window
+    // ---- the producer warps: warpgroup wg dequantises operand wg
+    const int wg = tid >> 7, warp = wid & 3;
     const int mt = lane >> 4, hh = (lane >> 3) & 1, g = lane & 7;
-    // this lane's row of operand m in the tiled layout: per chunk c, half:
-    // codes at tile*2048 + half*1024 + (2mt+h)*256 + 32g (32 bytes), scales
-    // at tile*128 + half*64 + (2mt+h)*16 + 2g (2 fp16)
-    const uint8_t *cbase[NMAT];
-    const uint16_t *sbase[NMAT];
-    bool rows_ok[NMAT];
-    int row[NMAT];
-#pragma unroll
-    for (int m = 0; m < NMAT; ++m) {
-        const LinearDev &w = (GLU && m == 1) ? r.w1 : r.w0;
-        const int rb = (in.row0 >> 5) + warp + (GLU ? 0 : 4 * m);
-        rows_ok[m] = rb < RB;
-        row[m] = rb * 32 + lane;
-        const long long tile0 = ((long long)in.e * RB + (rows_ok[m] ? rb : 0)) * C;
-        cbase[m] = w.codes + tile0 * 2048 + (2 * mt + hh) * 256 + 32 * g + 16 * wgi;
-        sbase[m] = w.scales + tile0 * 128 + (2 * mt + hh) * 16 + 2 * g;
-    }
+    const LinearDev &w = (GLU && wg == 1) ? r.w1 : r.w0;
+    const int rb = (in.row0 >> 5) + warp + (GLU ? 0 : 4 * wg);
+    const bool rows_ok = rb < RB;
+    // this lane's row in the tiled layout: per chunk c, half: codes at
+    // tile*2048 + half*1024 + (2mt+h)*256 + 32g (32 bytes), scales at
+    // tile*128 + half*64 + (2mt+h)*16 + 2g (2 fp16)
+    const long long tile0 = ((long long)in.e * RB + (rows_ok ? rb : 0)) * C;
+    const uint8_t *cbase = w.codes + tile0 * 2048 + (2 * mt + hh) * 256 + 32 * g;
+    const uint16_t *sbase = w.scales + tile0 * 128 + (2 * mt + hh) * 16 + 2 * g;
     const uint32_t lanebyte = (lane & 15) * 8;
+    const uint32_t cbm = cb_s + (GLU ? wg * 128 : 0);
     const uint32_t t_warp = tmem + ((uint32_t)(warp * 32) << 16);
-    // ---- this thread's staging: input chunk ch of slots n0 + 32q. The MMA's K
-    // order within a window is permuted -- input chunk ch sits at K chunk
-    // kch(ch) = 4 (ch & 1) + ch / 2 in both operands -- so that warpgroup wgi
-    // dequantises the contiguous A columns 16 wgi .. 16 wgi + 15.
-    constexpr int kQ = kN * 8 / kProducers;   // slots a thread stages per window
-    const int ch = tid & 7, n0 = tid >> 3;
-    const int kch = 4 * (ch & 1) + (ch >> 1);
-    const uint16_t *src[kQ];
-    uint32_t dst0[kQ];
-    uint32_t live = 0;
-#pragma unroll
-    for (int q = 0; q < kQ; ++q) {
-        const int n = n0 + (kProducers / 8) * q;
-        const int p = sh.pairs[n];
-        const int xr = p < 0 ? 0 : (r.x_per_pair ? p : p / r.k);
-        src[q] = r.x + (size_t)xr * IN + 8 * ch;
-        dst0[q] = xs_s + kch * kLbo + (n >> 3) * 128 + (n & 7) * 16;
-        live |= (p >= 0 ? 1u : 0u) << q;
-    }
-#pragma unroll
-    for (int w0 = 0; w0 < kAhead; ++w0) {
-        if (w0 < NW) {
-#pragma unroll
-            for (int q = 0; q < kQ; ++q)
-                if (live >> q & 1) {
-                    const int f = w0 * kWin + 8 * ch;
-                    cp_async16(dst0[q] + w0 * kStageBytes, src[q] + w0 * kWin, f < IN ? 16 : 0);
-                }
-        }
-        cp_async_commit();
-    }
-    // ---- this warpgroup's codes of half chunks (t = 2wgi, 2wgi+1: 16 bytes):
-    // cur (windows 2h, 2h+1) and the next two
-    uint4 cc[NMAT], nc1[NMAT], nc2[NMAT];
-    uint32_t cs[NMAT], ns1[NMAT], ns2[NMAT];
-    auto load_half = [&](int hn, int m, uint4 &c, uint32_t &sc) {
-        if (rows_ok[m] && hn < 2 * C) {
-            c = ldg_stream_v4(cbase[m] + (long long)(hn >> 1) * 2048 + (hn & 1) * 1024);
-            sc = ldg_stream_u32(sbase[m] + (long long)(hn >> 1) * 128 + (hn & 1) * 64);
+    // ---- this row's codes of half chunks: cur (windows 2h, 2h+1) and the next two
+    uint4 c0[3], c1[3];
+    uint32_t sc[3];
+    auto load_half = [&](int hn, int j) {
+        if (rows_ok && hn < 2 * C) {
+            const uint8_t *p = cbase + (long long)(hn >> 1) * 2048 + (hn & 1) * 1024;
+            c0[j] = ldg_stream_v4(p);
+            c1[j] = ldg_stream_v4(p + 16);
+            sc[j] = ldg_stream_u32(sbase + (long long)(hn >> 1) * 128 + (hn & 1) * 64);
         } else {
-            c = make_uint4(0, 0, 0, 0);
-            sc = 0u;
+            c0[j] = c1[j] = make_uint4(0, 0, 0, 0);
+            sc[j] = 0u;
         }
     };
-#pragma unroll
-    for (int m = 0; m < NMAT; ++m) {
-        load_half(0, m, cc[m], cs[m]);
-        load_half(1, m, nc1[m], ns1[m]);
-        load_half(2, m, nc2[m], ns2[m]);
-    }
+    load_half(0, 0);
+    load_half(1, 1);
+    load_half(2, 2);
     for (int hw = 0; hw < NW; hw += 2) {     // two windows = one half chunk
 #pragma unroll
         for (int ww = 0; ww < 2; ++ww) {
-            const int win = hw + ww;
-            // refill: window win + kAhead into the stage that window
-            // win + kAhead - kStages used (its MMAs must be done)
-            if (win + kAhead < NW) {
-                const int s2 = (win + kAhead) % kStages;
-                if (win >= kStages - kAhead) {
-                    warp_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
-                    ++ps.sw[s2];
-                }
-                const int fw = (win + kAhead) * kWin;
-#pragma unroll
-                for (int q = 0; q < kQ; ++q)
-                    if (live >> q & 1)
-                        cp_async16(dst0[q] + s2 * kStageBytes, src[q] + fw, fw + 8 * ch < IN ? 16 : 0);
-            }
-            cp_async_commit();
-            // dequantise this lane's 32 inputs of the window (while the copies
-            // fly): local quad l = 2j + s is code t = 2wgi + s, b = 4ww + j --
-            // byte j of word 2s + ww of this warpgroup's 16 bytes -- and goes to
-            // A columns 16wgi + 2l, 2l + 1 (K chunk 4wgi + j = input chunk 2j + wgi)
+            // quad i of the window (inputs 4i .. 4i+3): code t = i & 3 of byte
+            // b = 4ww + (i >> 2) -- byte i >> 2 of word 2t + ww -- to A
+            // columns 2i, 2i + 1
             const uint32_t slot = ps.gb % kSlots;
-            uint32_t a[NMAT][16];
+            const uint32_t s2v = __byte_perm(sc[0], 0, ww ? 0x3232 : 0x1010);
+            const uint32_t words[8] = {c0[0].x, c0[0].y, c0[0].z, c0[0].w, c1[0].x, c1[0].y, c1[0].z, c1[0].w};
+            uint32_t a[32];
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                const uint32_t s2v = __byte_perm(cs[m], 0, ww ? 0x3232 : 0x1010);
-                const uint32_t words[4] = {cc[m].x, cc[m].y, cc[m].z, cc[m].w};
-#pragma unroll
-                for (int l = 0; l < 8; ++l) {
-                    const int j = l >> 1, sb = l & 1;
-                    const uint32_t ad = __byte_perm(words[2 * sb + ww], lanebyte, 0x5504u | (j << 4));
-                    const uint2 e = lds64(cb_s + (GLU ? m * 128 : 0) + ad);
-                    a[m][2 * l] = hmul2_u32(e.x, s2v);
-                    a[m][2 * l + 1] = hmul2_u32(e.y, s2v);
-                }
+            for (int i = 0; i < 16; ++i) {
+                const int t = i & 3, bq = i >> 2;
+                const uint32_t ad = __byte_perm(words[2 * t + ww], lanebyte, 0x5504u | (bq << 4));
+                const uint2 e = lds64(cbm + ad);
+                a[2 * i] = hmul2_u32(e.x, s2v);
+                a[2 * i + 1] = hmul2_u32(e.y, s2v);
             }
             if (ps.gb >= kSlots) warp_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
             tc_fence_after();
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) tmem_st16(t_warp + 32 * (kSlots * m + slot) + 16 * wgi, a[m]);
-            cp_async_wait<kAhead>();          // this thread's copies of window win
-            fence_proxy_async();
+            tmem_st32(t_warp + 32 * (kSlots * wg + slot), a);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.full[slot]);
             ++ps.gb;
         }
-        // next half chunk
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-            cc[m] = nc1[m];
-            cs[m] = ns1[m];
-            nc1[m] = nc2[m];
-            ns1[m] = ns2[m];
-            load_half((hw >> 1) + 3, m, nc2[m], ns2[m]);
-        }
+        c0[0] = c0[1];
+        c1[0] = c1[1];
+        sc[0] = sc[1];
+        c0[1] = c0[2];
+        c1[1] = c1[2];
+        sc[1] = sc[2];
+        load_half((hw >> 1) + 3, 2);
     }
-    // ---- the tile's MMAs done; then the stage commits the loop did not wait
-    // for (windows NW - kStages .. NW - 1), already complete
+    // ---- the tile's MMAs done
     warp_wait(&sh.acc, ps.dn & 1, err, ps.failed);
     ++ps.dn;
-    for (int win = (NW > kStages ? NW - kStages : 0); win < NW; ++win) {
-        const int s2 = win % kStages;
-        warp_wait(&sh.stage[s2], ps.sw[s2] & 1, err, ps.failed);
-        ++ps.sw[s2];
-    }
     tc_fence_after();
-    // ---- accumulators -> outputs, 32 pairs at a time; warpgroup wgi takes
-    // pairs 64 wgi .. 64 wgi + 63
+    // ---- accumulators -> outputs, 32 pairs at a time; warpgroup wg takes
+    // pairs 64 wg .. 64 wg + 63; output row of pair n: its pair id, or (an
+    // activation for the next phase) its sorted position base + n
 #pragma unroll 1
-    for (int q = 2 * wgi; q < 2 * wgi + 2; ++q) {
+    for (int q = 2 * wg; q < 2 * wg + 2; ++q) {
         uint32_t dv[NMAT][32];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) tmem_ld32(t_warp + kDCol + 128 * m + 32 * q, dv[m]);
         tmem_wait_ld();
 #pragma unroll
         for (int m = 0; m < (GLU ? 1 : NMAT); ++m) {
-            if (rows_ok[m] && row[m] < OUT) {
+            const int rbm = (in.row0 >> 5) + warp + (GLU ? 0 : 4 * m);
+            const int row = rbm * 32 + lane;
+            if (rbm < RB && row < OUT) {
                 uint32_t ov[16];
 #pragma unroll
                 for (int jp = 0; jp < 16; ++jp)
@@ -354,8 +295,11 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
                                             sh.pscale[32 * q + 2 * jp + 1], r.out_f16);
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) {
-                    const int p = sh.pairs[32 * q + jj];
-                    if (p >= 0) r.out[(size_t)p * OUT + row[m]] = (uint16_t)(ov[jj >> 1] >> (16 * (jj & 1)));
+                    const int n = 32 * q + jj, p = sh.pairs[n];
+                    if (p >= 0) {
+                        const long long orow = r.out_sorted ? (long long)in.base + n : (long long)p;
+                        r.out[orow * OUT + row] = (uint16_t)(ov[jj >> 1] >> (16 * (jj & 1)));
+                    }
                 }
             }
         }
@@ -397,18 +341,26 @@ __device__ __forceinline__ int find_expert(const int *pre, int nact, int u) {
 }
 
 // --------------------------------------------------------------- kernel
-__global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeArgs a) {
-    extern __shared__ __align__(1024) uint8_t smem[];
+// map1: the phase 1 B rows (the sorted copy of the inputs); map2: phase 2's
+// (the sorted SwiGLU activations, or the sorted inputs of a single linear).
+__global__ void __launch_bounds__(kThreads, 1)
+    expert_prefill_kernel(const __grid_constant__ CUtensorMap map1, const __grid_constant__ CUtensorMap map2,
+                          const PipeArgs a) {
+    extern __shared__ uint8_t smem_raw[];
     __shared__ Shared sh;
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x;
-    uint8_t *cb = smem, *xs = smem + kCbRegion;
+    const uint32_t xs_s = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *cb = smem_raw + (xs_s - smem_u32(smem_raw)) + kStages * kStageBytes;
     if (tid == 0) {
         for (int i = 0; i < kSlots; ++i) {
             mbar_init(&sh.full[i], kProducers / 32);
             mbar_init(&sh.slot[i], 1);
         }
-        for (int i = 0; i < kStages; ++i) mbar_init(&sh.stage[i], 1);
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&sh.xfull[i], 1);
+            mbar_init(&sh.xempty[i], 1);
+        }
         mbar_init(&sh.acc, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -486,13 +438,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
             __syncthreads();
         }
         if (in.phase == 1) {
-            pf_tile<true>(a.s1, in, smem_u32(cb), xs, sh, tmem, ps, err);
+            pf_tile<true>(a.s1, in, smem_u32(cb), xs_s, &map1, sh, tmem, ps, err);
             if (tid == 0) {
                 __threadfence();
                 atomicAdd(a.ctl + 2 + in.ai, 1u);
             }
         } else {
-            pf_tile<false>(a.s2, in, smem_u32(cb), xs, sh, tmem, ps, err);
+            pf_tile<false>(a.s2, in, smem_u32(cb), xs_s, &map2, sh, tmem, ps, err);
         }
     }
     tc_fence_before();
@@ -505,9 +457,22 @@ __global__ void __launch_bounds__(kThreads, 1) expert_prefill_kernel(const PipeA
     }
 }
 
+// xs[pos][0:IN] = x[row of pair list[pos]][0:IN], 16 bytes per thread
+__global__ void permute_rows_kernel(const uint16_t *__restrict__ x, int x_per_pair, int k,
+                                    const int32_t *__restrict__ list, int P, int IN, uint16_t *__restrict__ xs) {
+    const int v8 = IN / 8;
+    const size_t n = (size_t)P * v8;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int pos = (int)(i / v8), v = (int)(i - (size_t)pos * v8);
+        const int p = list[pos];
+        const size_t row = x_per_pair ? (size_t)p : (size_t)(p / k);
+        reinterpret_cast<uint4 *>(xs + (size_t)pos * IN)[v] = reinterpret_cast<const uint4 *>(x + row * IN)[v];
+    }
+}
+
 }  // namespace pf
 
-vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream) {
+vqmoe_status launch_experts_prefill(const PipeArgs &args, void *xs, cudaStream_t stream) {
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -518,7 +483,31 @@ vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream) {
                              pf::kSmem);
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    pf::expert_prefill_kernel<<<sm_count(), pf::kThreads, pf::kSmem, stream>>>(a);
+    PipeArgs a = args;
+    const RoutedSet &first = a.has1 ? a.s1 : a.s2;
+    const int P = first.P, IN = first.IN;
+    uint16_t *xs16 = static_cast<uint16_t *>(xs);
+    {
+        const size_t n = (size_t)P * (IN / 8);
+        const int grid = (int)std::min<size_t>((n + 255) / 256, (size_t)sm_count() * 8);
+        pf::permute_rows_kernel<<<grid, 256, 0, stream>>>(first.x, first.x_per_pair, first.k, first.list, P, IN,
+                                                          xs16);
+        vqmoe_status s = check_launch("permute_rows_kernel");
+        if (s != VQMOE_OK) return s;
+    }
+    CUtensorMap map1, map2;
+    if (!make_tma_map(&map1, xs16, P, IN, pf::kN))
+        return set_error(VQMOE_LAUNCH_FAILED, "prefill experts: tensor map of the inputs (P %d, IN %d)", P, IN);
+    if (a.has1) {
+        // phase 1 writes its activations in sorted order; phase 2 reads them so
+        a.s1.out_sorted = 1;
+        if (!make_tma_map(&map2, a.s1.out, P, a.s1.OUT, pf::kN))
+            return set_error(VQMOE_LAUNCH_FAILED, "prefill experts: tensor map of the activations (P %d, I %d)", P,
+                             a.s1.OUT);
+    } else {
+        map2 = map1;
+    }
+    pf::expert_prefill_kernel<<<sm_count(), pf::kThreads, pf::kSmem, stream>>>(map1, map2, a);
     return check_launch("expert_prefill_kernel");
 }
 

@@ -23,6 +23,7 @@ struct RoutedSet {
     uint16_t *out;               // [P][OUT]
     int out_f16;                 // 1: fp16 (saturated) output, 0: bf16
     const float *pair_scale;     // optional [P]: y = bf16(bf16(acc) * s)
+    int out_sorted;              // prefill path: output row = the pair's sorted position
 };
 
 struct PipeArgs {
@@ -74,6 +75,7 @@ struct TileInfo {
 
 // The prefill path (tcgen05): both stages of the routed VQ experts in one
 // launch, for layers whose experts see many tokens each.
-vqmoe_status launch_experts_prefill(const PipeArgs &a, cudaStream_t stream);
+// xs: [P][IN of the first stage] fp16 scratch for the expert-ordered inputs.
+vqmoe_status launch_experts_prefill(const PipeArgs &a, void *xs, cudaStream_t stream);
 
 }  // namespace vqmoe

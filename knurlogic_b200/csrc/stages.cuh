@@ -28,7 +28,12 @@ struct RoutedIO {
     void *out;              // [P][OUT]
     int out_f16;            // fp16 (saturated) output instead of bf16
     const float *pair_scale;
+    void *xs;               // [P][IN] fp16 scratch (the prefill path's sorted inputs), or null
 };
+
+// The prefill path (tcgen05 grouped GEMM) serves a call with VQ experts and
+// at least 32 pairs per expert on average; it needs the xs scratch.
+inline bool prefill_regime(bool vq, int E, int P) { return vq && E <= 512 && (long long)P >= 32LL * E; }
 
 // Words of the expert kernel's control block: tile counter, error flag, and
 // one finished-tile count per expert. Zeroed by the routing kernel.

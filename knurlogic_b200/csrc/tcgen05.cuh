@@ -114,5 +114,31 @@ __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 
+// Shared-memory descriptor of a K-major operand tile with the 128-byte
+// swizzle (1024-byte aligned atoms of 8 rows x 128 bytes, SBO = 1024); the
+// K16 step k of a 64-element row starts 32k bytes further.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+__device__ __forceinline__ void arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// 2-D tensor copy global -> shared, completing on `bar` (no multicast); the
+// map is a kernel parameter (__grid_constant__)
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4}], [%2];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+// orders this thread's earlier generic-proxy view of global memory (what an
+// acquire made visible) before its later async-proxy (TMA) reads
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;\n" ::: "memory");
+}
+
 }  // namespace tc
 }  // namespace vqmoe
