@@ -28,9 +28,10 @@
 //              and stores each 64-input window into a TMEM slot; then the
 //              epilogue (tcgen05.ld, SwiGLU / routing weight, stores);
 //   warp 8     MMA: tcgen05.mma M=128 x N=128 x K=16, A from TMEM, B from
-//              the SW128 stage, into two 128-column accumulators;
-//   warp 9     TMA: one 2-D tensor copy (128 pairs x 64 inputs) per window
-//              into an 8-stage ring.
+//              the SW128 stage, into two 128-column accumulators; one
+//              barrier wait per 16 MMAs (a wait stalls MMA issue);
+//   warp 9     TMA: two 2-D tensor copies (128 pairs x 64 inputs) per
+//              128-input window into a 4-stage ring.
 #include <algorithm>
 
 #include "experts.cuh"
@@ -48,13 +49,14 @@ constexpr int kMmaWarp = kProducers / 32;     // 8
 constexpr int kTmaWarp = kMmaWarp + 1;        // 9
 constexpr int kThreads = kProducers + 64;
 constexpr int kN = 128;                       // pairs per tile (MMA N)
-constexpr int kSlots = 4;                     // A slots per operand (a 64-input window each)
-constexpr int kWin = 64;                      // inputs per window
-constexpr int kStages = 8;                    // x windows in shared memory
-constexpr int kStageBytes = kN * kWin * 2;    // 16 KB: 128 pairs x 128 bytes, 128-byte swizzle
+constexpr int kSlots = 2;                     // A slots per operand (a 128-input window each: 64 columns)
+constexpr int kWin = 128;                     // inputs per window (16 MMAs per barrier wait)
+constexpr int kStages = 4;                    // x windows in shared memory
+constexpr int kSubBytes = kN * 128;           // one 64-input SW128 sub-tile: 128 pairs x 128 bytes
+constexpr int kStageBytes = 2 * kSubBytes;    // 32 KB
 constexpr int kCbRegion = 65536;              // the phase's codebooks: gate / up, then down
 constexpr size_t kSmem = (size_t)kStages * kStageBytes + kCbRegion + 1024;   // + 1024-byte alignment
-constexpr int kDCol = 2 * kSlots * 32;        // D of operand m at kDCol + 128m (all 512 columns)
+constexpr int kDCol = 2 * kSlots * 64;        // D of operand m at kDCol + 128m (all 512 columns)
 constexpr int kAllocCols = 512;
 constexpr int kMaxE = 512;
 constexpr long kSpin = 1L << 22;
@@ -87,9 +89,11 @@ __device__ __forceinline__ void stage_codebook(uint8_t *region, const LinearDev 
 }
 
 struct Shared {
-    uint64_t full[kSlots];                    // an A slot written by all producer warps
+    // window gb ready: its A slot written by all producer warps and its x
+    // stage landed (TMA transaction count); one wait per window for the MMA
+    // thread, whose every wait costs MMA issue time
+    uint64_t full[kStages];
     uint64_t slot[kSlots];                    // MMAs done reading an A slot
-    uint64_t xfull[kStages];                  // an x stage landed (TMA transaction count)
     uint64_t xempty[kStages];                 // MMAs done reading an x stage
     uint64_t acc;                             // a tile's MMAs done: accumulators final
     TileInfo info;
@@ -133,12 +137,12 @@ __device__ __forceinline__ uint32_t pf_value2(uint32_t g0, uint32_t g1, uint32_t
     return v;
 }
 
-// One tile. Every A batch is one 64-input window: the TMA warp copies the
-// window's 128 x-rows (sorted positions base .. base + 127) into stage gb %
-// kStages; each producer warp stores its 32 rows of its operand into slot gb
-// % kSlots and arrives on `full`; the MMA warp waits for both, multiplies
-// and commits the slot, the stage and, after the last window, the
-// accumulators. Two A operands: gate and up of 128 rows (GLU), or rows
+// One tile. Every A batch is one 128-input window: the TMA warp copies the
+// window's 128 x-rows (sorted positions base .. base + 127; two 64-input
+// SW128 sub-tiles) into stage gb % kStages; each producer warp stores its 32
+// rows of its operand into slot gb % kSlots; both arrive on full[gb %
+// kStages]; the MMA warp waits once, multiplies and commits the slot, the
+// stage and, after the last window, the accumulators. Two A operands: gate and up of 128 rows (GLU), or rows
 // row0 .. row0 + 127 and row0 + 128 .. row0 + 255 of the one matrix.
 template <bool GLU>
 __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, uint32_t cb_s, uint32_t xs_s,
@@ -147,7 +151,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     const int tid = threadIdx.x, wid = tid >> 5, lane = tid & 31;
     const int IN = r.IN, OUT = r.OUT;
     const int C = (IN + 255) >> 8, RB = (OUT + 31) >> 5;
-    const int NW = C * 4;                     // 64-input windows (beyond IN: zero-filled, zero weights)
+    const int NW = C * 2;                     // 128-input windows (beyond IN: zero-filled, zero weights)
     if (tid < kN) {
         const int p = tid < in.n ? r.list[in.base + tid] : -1;
         sh.pairs[tid] = p;
@@ -164,8 +168,9 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
             for (int win = 0; win < NW; ++win, ++gb) {
                 const int s = gb % kStages;
                 if (gb >= (uint32_t)kStages) mbar_wait(&sh.xempty[s], ((gb / kStages) + 1) & 1, err, ps.failed);
-                arrive_expect_tx(&sh.xfull[s], kStageBytes);
-                tma_load_2d(xs_s + s * kStageBytes, xmap, win * kWin, in.base, &sh.xfull[s]);
+                arrive_expect_tx(&sh.full[s], kStageBytes);
+                tma_load_2d(xs_s + s * kStageBytes, xmap, win * kWin, in.base, &sh.full[s]);
+                tma_load_2d(xs_s + s * kStageBytes + kSubBytes, xmap, win * kWin + 64, in.base, &sh.full[s]);
             }
         }
         __syncwarp();
@@ -181,16 +186,15 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
             for (int win = 0; win < NW; ++win, ++gb) {
                 const uint32_t slot = gb % kSlots;
                 const int s = gb % kStages;
-                mbar_wait(&sh.full[slot], (gb / kSlots) & 1, err, ps.failed);
-                mbar_wait(&sh.xfull[s], (gb / kStages) & 1, err, ps.failed);
+                mbar_wait(&sh.full[s], (gb / kStages) & 1, err, ps.failed);
                 tc_fence_after();
                 const uint32_t xb = xs_s + s * kStageBytes;
 #pragma unroll
-                for (int k16 = 0; k16 < 4; ++k16)
+                for (int k16 = 0; k16 < kWin / 16; ++k16)
 #pragma unroll
                     for (int m = 0; m < NMAT; ++m)
-                        tc_mma(tmem + kDCol + 128 * m, tmem + 32 * (kSlots * m + slot) + 8 * k16,
-                               sw128_desc(xb + 32 * k16), win > 0 || k16 > 0);
+                        tc_mma(tmem + kDCol + 128 * m, tmem + 64 * (kSlots * m + slot) + 8 * k16,
+                               sw128_desc(xb + (k16 >> 2) * kSubBytes + 32 * (k16 & 3)), win > 0 || k16 > 0);
                 tc_commit(&sh.slot[slot]);
                 tc_commit(&sh.xempty[s]);
             }
@@ -217,7 +221,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     const uint32_t lanebyte = (lane & 15) * 8;
     const uint32_t cbm = cb_s + (GLU ? wg * 128 : 0);
     const uint32_t t_warp = tmem + ((uint32_t)(warp * 32) << 16);
-    // ---- this row's codes of half chunks: cur (windows 2h, 2h+1) and the next two
+    // ---- this row's codes of half chunks (one per window): cur and the next two
     uint4 c0[3], c1[3];
     uint32_t sc[3];
     auto load_half = [&](int hn, int j) {
@@ -234,15 +238,15 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
     load_half(0, 0);
     load_half(1, 1);
     load_half(2, 2);
-    for (int hw = 0; hw < NW; hw += 2) {     // two windows = one half chunk
+    for (int win = 0; win < NW; ++win) {     // one window = one half chunk (128 inputs)
+        const uint32_t slot = ps.gb % kSlots;
+        const uint32_t words[8] = {c0[0].x, c0[0].y, c0[0].z, c0[0].w, c1[0].x, c1[0].y, c1[0].z, c1[0].w};
 #pragma unroll
         for (int ww = 0; ww < 2; ++ww) {
-            // quad i of the window (inputs 4i .. 4i+3): code t = i & 3 of byte
-            // b = 4ww + (i >> 2) -- byte i >> 2 of word 2t + ww -- to A
-            // columns 2i, 2i + 1
-            const uint32_t slot = ps.gb % kSlots;
+            // quad i of 64-input group ww (inputs 64ww + 4i .. + 3): code t =
+            // i & 3 of byte b = 4ww + (i >> 2) -- byte i >> 2 of word 2t + ww
+            // -- to A columns 32ww + 2i, 32ww + 2i + 1
             const uint32_t s2v = __byte_perm(sc[0], 0, ww ? 0x3232 : 0x1010);
-            const uint32_t words[8] = {c0[0].x, c0[0].y, c0[0].z, c0[0].w, c1[0].x, c1[0].y, c1[0].z, c1[0].w};
             uint32_t a[32];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -252,22 +256,25 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
                 a[2 * i] = hmul2_u32(e.x, s2v);
                 a[2 * i + 1] = hmul2_u32(e.y, s2v);
             }
-            if (ps.gb >= kSlots) warp_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
-            tc_fence_after();
-            tmem_st32(t_warp + 32 * (kSlots * wg + slot), a);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sh.full[slot]);
-            ++ps.gb;
+            if (ww == 0) {
+                // the slot's previous window multiplied (its first half computed meanwhile)
+                if (ps.gb >= kSlots) warp_wait(&sh.slot[slot], ((ps.gb / kSlots) + 1) & 1, err, ps.failed);
+                tc_fence_after();
+            }
+            tmem_st32(t_warp + 64 * (kSlots * wg + slot) + 32 * ww, a);
         }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.full[ps.gb % kStages]);
+        ++ps.gb;
         c0[0] = c0[1];
         c1[0] = c1[1];
         sc[0] = sc[1];
         c0[1] = c0[2];
         c1[1] = c1[2];
         sc[1] = sc[2];
-        load_half((hw >> 1) + 3, 2);
+        load_half(win + 3, 2);
     }
     // ---- the tile's MMAs done
     warp_wait(&sh.acc, ps.dn & 1, err, ps.failed);
@@ -353,12 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t xs_s = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *cb = smem_raw + (xs_s - smem_u32(smem_raw)) + kStages * kStageBytes;
     if (tid == 0) {
-        for (int i = 0; i < kSlots; ++i) {
-            mbar_init(&sh.full[i], kProducers / 32);
-            mbar_init(&sh.slot[i], 1);
-        }
+        for (int i = 0; i < kSlots; ++i) mbar_init(&sh.slot[i], 1);
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(&sh.xfull[i], 1);
+            mbar_init(&sh.full[i], kProducers / 32 + 1);   // producer warps + the TMA thread
             mbar_init(&sh.xempty[i], 1);
         }
         mbar_init(&sh.acc, 1);
