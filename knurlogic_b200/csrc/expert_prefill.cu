@@ -137,6 +137,30 @@ __device__ __forceinline__ uint32_t pf_value2(uint32_t g0, uint32_t g1, uint32_t
     return v;
 }
 
+// A warp's 32 rows (lanes) x 32 pairs of 16-bit outputs, v[j] = pairs 2j,
+// 2j + 1 of the lane's row, transposed by three shuffle butterflies (lane
+// bits 2, 1, 0 swapped with pair bits 2, 3, 4) so that lane L holds rows 8
+// (L >> 3) .. + 7 of pairs 16 (L & 1) + 8 ((L >> 1) & 1) + 4 ((L >> 2) & 1)
+// + c, c = 0..3 -- one 16-byte store per pair instead of eight 2-byte ones.
+// Afterwards the value of row 8 (L >> 3) + i, pair offset c is half c & 1
+// of v[(i & 1) << 3 | ((i >> 1) & 1) << 2 | (i >> 2) << 1 | c >> 1].
+__device__ __forceinline__ void transpose_rows8(uint32_t (&v)[16], int lane) {
+#pragma unroll
+    for (int rd = 0; rd < 3; ++rd) {
+        const int lbit = 2 - rd, jbit = 1 + rd;           // lane bit 2 <-> index bit 1, ...
+        const bool hi = (lane >> lbit) & 1;
+#pragma unroll
+        for (int i0 = 0; i0 < 16; ++i0) {
+            if (i0 & (1 << jbit)) continue;
+            const int i1 = i0 | (1 << jbit);
+            const uint32_t send = hi ? v[i0] : v[i1];
+            const uint32_t recv = __shfl_xor_sync(0xFFFFFFFFu, send, 1 << lbit);
+            if (hi) v[i0] = recv;
+            else v[i1] = recv;
+        }
+    }
+}
+
 // One tile. Every A batch is one 128-input window: the TMA warp copies the
 // window's 128 x-rows (sorted positions base .. base + 127; two 64-input
 // SW128 sub-tiles) into stage gb % kStages; each producer warp stores its 32
@@ -292,20 +316,30 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
 #pragma unroll
         for (int m = 0; m < (GLU ? 1 : NMAT); ++m) {
             const int rbm = (in.row0 >> 5) + warp + (GLU ? 0 : 4 * m);
-            const int row = rbm * 32 + lane;
-            if (rbm < RB && row < OUT) {
+            if (rbm < RB) {                   // warp-uniform: OUT is a multiple of 16
                 uint32_t ov[16];
 #pragma unroll
                 for (int jp = 0; jp < 16; ++jp)
                     ov[jp] = pf_value2<GLU>(dv[m][2 * jp], dv[m][2 * jp + 1], dv[1][2 * jp], dv[1][2 * jp + 1],
                                             r.pair_scale != nullptr, sh.pscale[32 * q + 2 * jp],
                                             sh.pscale[32 * q + 2 * jp + 1], r.out_f16);
+                transpose_rows8(ov, lane);
+                const int row8 = rbm * 32 + 8 * (lane >> 3);
+                const int pb = 16 * (lane & 1) + 8 * ((lane >> 1) & 1) + 4 * ((lane >> 2) & 1);
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) {
-                    const int n = 32 * q + jj, p = sh.pairs[n];
-                    if (p >= 0) {
+                for (int c = 0; c < 4; ++c) {
+                    const int n = 32 * q + pb + c, p = sh.pairs[n];
+                    uint32_t w4[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int i0 = 2 * k, i1 = 2 * k + 1;
+                        const uint32_t va = ov[(i0 & 1) << 3 | ((i0 >> 1) & 1) << 2 | (i0 >> 2) << 1 | (c >> 1)];
+                        const uint32_t vb = ov[(i1 & 1) << 3 | ((i1 >> 1) & 1) << 2 | (i1 >> 2) << 1 | (c >> 1)];
+                        w4[k] = __byte_perm(va, vb, (c & 1) ? 0x7632 : 0x5410);
+                    }
+                    if (p >= 0 && row8 < OUT) {
                         const long long orow = r.out_sorted ? (long long)in.base + n : (long long)p;
-                        r.out[orow * OUT + row] = (uint16_t)(ov[jj >> 1] >> (16 * (jj & 1)));
+                        *reinterpret_cast<uint4 *>(r.out + orow * OUT + row8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     }
                 }
             }
