@@ -355,6 +355,10 @@ __global__ void __launch_bounds__(kThreads, 2) expert_kernel(const PipeArgs a) {
     const int tid = threadIdx.x;
     uint8_t *cb = smem;
     uint8_t *xs = smem + ((VQ1 || VQ2) ? kRepBytes : 0);
+    // the phase 1 codebooks (weights) before the routing is ready, then the
+    // routing kernel's results (launched with programmatic dependence)
+    if (VQ1 && a.has1) stage_codebooks(cb, a.s1.w0, a.s1.w1, 2);
+    pdl_wait();
     const int nact = a.s2.active[a.s2.E];
     const int rt1 = a.has1 ? (a.s1.OUT + kTR1 - 1) / kTR1 : 0;
     const int rt2 = (a.s2.OUT + kTR2 - 1) / kTR2;
@@ -363,7 +367,6 @@ __global__ void __launch_bounds__(kThreads, 2) expert_kernel(const PipeArgs a) {
     __syncthreads();
     // ---- phase 1: gate/up + SwiGLU
     if (s_next < n1) {
-        if (VQ1) stage_codebooks(cb, a.s1.w0, a.s1.w1, 2);
         for (;;) {
             const int tile = s_next;
             if (tile >= n1) break;
@@ -584,7 +587,8 @@ static vqmoe_status launch_pipe(const PipeArgs &a, size_t smem, cudaStream_t str
             return set_error(VQMOE_LAUNCH_FAILED, "expert kernel: %zu bytes of shared memory", smem);
         if (dev >= 0 && dev < 64) configured[dev] = smem;
     }
-    fn<<<2 * sm_count(), kThreads, smem, stream>>>(a);
+    if (launch_pdl(fn, dim3(2 * sm_count()), dim3(kThreads), smem, stream, a) != cudaSuccess)
+        return check_launch("expert_kernel");
     return check_launch("expert_kernel");
 }
 

@@ -134,6 +134,7 @@ router_logits_dmma_kernel(const uint16_t *__restrict__ x, const uint16_t *__rest
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int t0 = blockIdx.y * 8, e0 = blockIdx.x * 8;
+    pdl_trigger();                   // the routing kernel may launch and wait for these logits
     if (x16 && blockIdx.x == 0) {   // fp16 copy of this CTA's tokens for the VQ experts
         const int vpr = H / 8;
         for (int v = tid; v < 8 * vpr; v += blockDim.x) {
@@ -355,8 +356,12 @@ router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int
     int32_t *s_rank = s_pe + T * k;      // [T*k]
     __shared__ int32_t s_wsum[32], s_asum[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // (the previous block call's expert kernel, the reader of `zero`, finished
+    // before this call's logits kernel began)
     for (int i = tid; i < zero_words; i += blockDim.x) zero[i] = 0u;
     for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
+    pdl_trigger();                   // the expert kernel may launch and stage its codebooks
+    pdl_wait();                      // the logits kernel's results
     __syncthreads();
     for (int t = warp; t < T; t += 32) {
         const float *lr = logits + (size_t)t * E1;
@@ -528,8 +533,9 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
             return set_error(VQMOE_LAUNCH_FAILED, "router_select: shared memory");
         if (dev >= 0 && dev < 64) configured[dev] = 100 * 1024;
     }
-    fn<<<1, 1024, smem_sel, stream>>>(logits, T, E, E1, k, wsg != nullptr, inds, scores, sgate, cnt, off,
-                                      list, active, zero, zero_words);
+    if (launch_pdl(fn, dim3(1), dim3(1024), smem_sel, stream, logits, T, E, E1, k, (int)(wsg != nullptr), inds,
+                   scores, sgate, cnt, off, list, active, zero, zero_words) != cudaSuccess)
+        return check_launch("router_select_kernel");
     return check_launch("router_select_kernel");
 }
 
