@@ -45,7 +45,9 @@
 extern "C" {
 #endif
 
-#define VQMOE_ABI_VERSION 1
+/* 2: vqmoe_linear.activation (was reserved), vqmoe_block.router_mode and
+ * its trailing reserved word, vqmoe_router_ex. */
+#define VQMOE_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define VQMOE_API __attribute__((visibility("default")))
@@ -90,8 +92,33 @@ typedef struct {
     int32_t codebook_size;       /* K */
     int32_t dim;                 /* code vector length */
     int32_t group_size;          /* inputs per vq_scales entry */
-    int32_t reserved;
+    int32_t activation;          /* on the gate linear of a SwitchGLU: VQMOE_ACT_*;
+                                    0 elsewhere */
 } vqmoe_linear;
+
+/* Activation between the gate and up projections of a SwitchGLU, set on its
+ * gate linear. Both round the activation of the bf16 gate output to bf16
+ * once and the product with the bf16 up output to bf16 once. */
+enum {
+    VQMOE_ACT_SWIGLU = 0,        /* _SwiGLU, qwen3_5.py:108-112: silu in fp32 */
+    VQMOE_ACT_GEGLU = 1          /* geglu, gemma4_text.py:131-135 (GeGLU
+                                    186-189): gelu's tanh form in fp32 */
+};
+
+/* Router variants: how the k weights come from the logits (the top-k
+ * itself is always by descending logit, ties to the lower expert). */
+enum {
+    VQMOE_ROUTER_SOFTMAX_TOPK_RENORM = 0, /* Qwen3.5, qwen3_5.py:174-179: fp32
+                                             softmax over all experts, the top
+                                             k renormalised in fp32 */
+    VQMOE_ROUTER_TOPK_SOFTMAX = 1,        /* Qwen4-exp with norm_topk_prob,
+                                             qwen4_exp.py:806-810: fp32 softmax
+                                             over the k selected logits */
+    VQMOE_ROUTER_SOFTMAX_TOPK = 2         /* Qwen4-exp without norm_topk_prob,
+                                             qwen4_exp.py:811-814: the top-k of
+                                             the fp32 softmax over all experts,
+                                             not renormalised */
+};
 
 /* One Qwen3.5-MoE sparse block (qwen3_5.py:170-192). The shared expert is
  * optional (shared_inter == 0 disables it and its gate). */
@@ -108,6 +135,8 @@ typedef struct {
     const void *shared_up_w;     /* mlp.shared_expert.up_proj   [I_s, H] bf16 */
     const void *shared_down_w;   /* mlp.shared_expert.down_proj [H, I_s] bf16 */
     const void *shared_expert_gate_w; /* mlp.shared_expert_gate [1, H] bf16 */
+    int32_t router_mode;         /* VQMOE_ROUTER_* (0: Qwen3.5) */
+    int32_t reserved;            /* 0 */
 } vqmoe_block;
 
 /* Output dtype of vqmoe_sparse_moe_block. F32 holds the bf16 block output
@@ -149,8 +178,9 @@ VQMOE_API vqmoe_status vqmoe_sparse_moe_block_timed(
     int32_t out_dtype, void *workspace, size_t workspace_bytes, void *stream,
     void *const *events, int32_t n_events);
 
-/* SwitchGLU.__call__: y[T, k, H] bf16 = down(bf16(silu(gate(x))) * up(x))
- * for each (token, slot) of indices [T, k] int32. */
+/* SwitchGLU.__call__: y[T, k, H] bf16 = down(bf16(act(gate(x))) * up(x))
+ * for each (token, slot) of indices [T, k] int32; act = gate->activation
+ * (SwiGLU or GeGLU). */
 VQMOE_API vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate,
                               const vqmoe_linear *up,
                               const vqmoe_linear *down, const void *x,
@@ -196,6 +226,15 @@ VQMOE_API vqmoe_status vqmoe_router(const void *x, const void *router_w,
                           int32_t hidden, int32_t num_experts, int32_t top_k,
                           int32_t *inds, float *scores, float *sgate,
                           void *workspace, size_t workspace_bytes,
+                          void *stream);
+
+/* vqmoe_router with the weights of a router variant (VQMOE_ROUTER_*):
+ * Qwen4-exp's SparseMoeBlock router, qwen4_exp.py:800-815. */
+VQMOE_API vqmoe_status vqmoe_router_ex(const void *x, const void *router_w,
+                          const void *shared_expert_gate_w, int32_t tokens,
+                          int32_t hidden, int32_t num_experts, int32_t top_k,
+                          int32_t router_mode, int32_t *inds, float *scores,
+                          float *sgate, void *workspace, size_t workspace_bytes,
                           void *stream);
 
 /* Dense fp16 weights of experts [first, first + count): out [count, OUT, IN]

@@ -18,6 +18,11 @@ FMT_DENSE_BF16 = 0
 FMT_VQ_U8 = 1
 OUT_BF16 = 0
 OUT_F32 = 1
+ACT_SWIGLU = 0          # vqmoe_linear.activation of a SwitchGLU's gate linear
+ACT_GEGLU = 1
+ROUTER_SOFTMAX_TOPK_RENORM = 0   # Qwen3.5 (qwen3_5.py:174-179)
+ROUTER_TOPK_SOFTMAX = 1          # Qwen4-exp, norm_topk_prob (qwen4_exp.py:806-810)
+ROUTER_SOFTMAX_TOPK = 2          # Qwen4-exp, not renormalised (qwen4_exp.py:811-814)
 
 STATUS = {0: "OK", 1: "BAD_SHAPE", 2: "BAD_FORMAT", 3: "BAD_POINTER",
           4: "WORKSPACE_TOO_SMALL", 5: "BAD_CODE", 6: "LAUNCH_FAILED",
@@ -31,7 +36,7 @@ class Linear(Structure):
                 ("weight", c_void_p), ("codes", c_void_p),
                 ("codebook", c_void_p), ("scales", c_void_p),
                 ("codebook_size", c_int32), ("dim", c_int32),
-                ("group_size", c_int32), ("reserved", c_int32)]
+                ("group_size", c_int32), ("activation", c_int32)]
 
 
 class Block(Structure):
@@ -41,7 +46,8 @@ class Block(Structure):
                 ("router_w", c_void_p), ("gate", Linear), ("up", Linear),
                 ("down", Linear), ("shared_gate_w", c_void_p),
                 ("shared_up_w", c_void_p), ("shared_down_w", c_void_p),
-                ("shared_expert_gate_w", c_void_p)]
+                ("shared_expert_gate_w", c_void_p),
+                ("router_mode", c_int32), ("reserved", c_int32)]
 
 
 #: every symbol include/vqmoe.h declares: (name, restype, argtypes)
@@ -71,6 +77,9 @@ SIGNATURES = [
       c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_router", c_int32,
      [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
+      c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("vqmoe_router_ex", c_int32,
+     [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
       c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_dequant", c_int32,
      [POINTER(Linear), c_int32, c_int32, c_void_p, c_void_p]),

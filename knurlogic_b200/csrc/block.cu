@@ -232,6 +232,13 @@ static BlockWs carve_block(void *ws, const vqmoe_block *b, int T) {
 // (bounds the workspace).
 constexpr int kMaxTokensPerLaunch = 2048;
 
+// the gate linear of a SwitchGLU names its activation
+static vqmoe_status check_glu_activation(const vqmoe_linear *gate) {
+    if (gate->activation != VQMOE_ACT_SWIGLU && gate->activation != VQMOE_ACT_GEGLU)
+        return set_error(VQMOE_BAD_FORMAT, "gate_proj activation %d (0 SwiGLU, 1 GeGLU)", gate->activation);
+    return VQMOE_OK;
+}
+
 static vqmoe_status check_block(const vqmoe_block *b, int T) {
     if (!b) return set_error(VQMOE_BAD_POINTER, "null block");
     if (T <= 0) return set_error(VQMOE_BAD_SHAPE, "tokens %d", T);
@@ -252,6 +259,9 @@ static vqmoe_status check_block(const vqmoe_block *b, int T) {
                              "switch_mlp shapes: gate/up must be [E=%d, I, H=%d], down [E, H, I]", E, H);
     if (b->gate.format != b->up.format)
         return set_error(VQMOE_BAD_FORMAT, "gate_proj and up_proj formats differ");
+    if ((s = check_glu_activation(&b->gate)) != VQMOE_OK) return s;
+    if (b->router_mode < VQMOE_ROUTER_SOFTMAX_TOPK_RENORM || b->router_mode > VQMOE_ROUTER_SOFTMAX_TOPK)
+        return set_error(VQMOE_BAD_FORMAT, "router_mode %d (0..2)", b->router_mode);
     if (!aligned_ptr(b->router_w)) return set_error(VQMOE_BAD_POINTER, "router_w");
     if (b->shared_inter < 0 || b->shared_inter % 16)
         return set_error(VQMOE_BAD_SHAPE, "shared_inter %d is not a multiple of 16", b->shared_inter);
@@ -367,12 +377,13 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
     s = launch_router_route(x, static_cast<const uint16_t *>(b->router_w),
                             shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr,
                             T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, rt.cnt, rt.off,
-                            rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, st);
+                            rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, b->router_mode, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 1, st)) != VQMOE_OK) return s;
     // the routed experts: gate/up + SwiGLU, then down (x routing weight)
     RoutedIO r1 = routed_io(rt, E, k, P, vq_in ? (const void *)w.x16 : (const void *)x, 0, w.act,
                             vq_dn, nullptr);
     r1.xs = w.xs;
+    r1.act = b->gate.activation;
     RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores);
     s = launch_experts(&b->gate, &b->up, &r1, &b->down, r2, rt.zero, st);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK) return s;
@@ -520,6 +531,7 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
     if ((s = check_linear(gate, "gate_proj")) != VQMOE_OK) return s;
     if ((s = check_linear(up, "up_proj")) != VQMOE_OK) return s;
     if ((s = check_linear(down, "down_proj")) != VQMOE_OK) return s;
+    if ((s = check_glu_activation(gate)) != VQMOE_OK) return s;
     if (tokens <= 0 || top_k <= 0) return set_error(VQMOE_BAD_SHAPE, "tokens %d top_k %d", tokens, top_k);
     const int I = gate->out_features, H = gate->in_features, E = gate->num_experts;
     if (up->out_features != I || up->in_features != H || down->out_features != H ||
@@ -547,6 +559,7 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
         RoutedIO r1 = routed_io(rt, E, top_k, P, vq_in ? (const void *)w.x16 : (const void *)xt, 0,
                                 w.act, vq_dn, nullptr);
         r1.xs = w.xs;
+        r1.act = gate->activation;
         RoutedIO r2 = routed_io(rt, E, top_k, P, w.act, 1,
                                 static_cast<uint16_t *>(y) + (size_t)t0 * top_k * H, 0, nullptr);
         if ((s = launch_experts(gate, up, &r1, down, r2, rt.zero, st)) != VQMOE_OK) return s;
@@ -590,9 +603,9 @@ vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x
     return VQMOE_OK;
 }
 
-vqmoe_status vqmoe_router(const void *x, const void *router_w, const void *sgw,
-                          int32_t tokens, int32_t hidden, int32_t num_experts,
-                          int32_t top_k, int32_t *inds, float *scores, float *sgate,
+vqmoe_status vqmoe_router_ex(const void *x, const void *router_w, const void *sgw,
+                             int32_t tokens, int32_t hidden, int32_t num_experts,
+                             int32_t top_k, int32_t router_mode, int32_t *inds, float *scores, float *sgate,
                           void *workspace, size_t workspace_bytes, void *stream) {
     if (tokens <= 0 || hidden <= 0 || hidden % 8 || num_experts <= 0 || num_experts > 512 ||
         top_k <= 0 || top_k > 32 || top_k > num_experts)
@@ -601,12 +614,21 @@ vqmoe_status vqmoe_router(const void *x, const void *router_w, const void *sgw,
     if (!aligned_ptr(x) || !aligned_ptr(router_w) || (sgw && !aligned16(sgw)) || !inds ||
         !scores || (sgw && !sgate) || !workspace)
         return set_error(VQMOE_BAD_POINTER, "router pointers");
+    if (router_mode < VQMOE_ROUTER_SOFTMAX_TOPK_RENORM || router_mode > VQMOE_ROUTER_SOFTMAX_TOPK)
+        return set_error(VQMOE_BAD_FORMAT, "router_mode %d (0..2)", router_mode);
     if (workspace_bytes < vqmoe_router_workspace_size(tokens, num_experts))
         return set_error(VQMOE_WORKSPACE_TOO_SMALL, "router workspace");
     return launch_router(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(router_w),
                          static_cast<const uint16_t *>(sgw), tokens, hidden, num_experts, top_k,
-                         static_cast<float *>(workspace), inds, scores, sgate, nullptr,
+                         static_cast<float *>(workspace), inds, scores, sgate, nullptr, router_mode,
                          static_cast<cudaStream_t>(stream));
+}
+
+vqmoe_status vqmoe_router(const void *x, const void *router_w, const void *sgw, int32_t tokens, int32_t hidden,
+                          int32_t num_experts, int32_t top_k, int32_t *inds, float *scores, float *sgate,
+                          void *workspace, size_t workspace_bytes, void *stream) {
+    return vqmoe_router_ex(x, router_w, sgw, tokens, hidden, num_experts, top_k, VQMOE_ROUTER_SOFTMAX_TOPK_RENORM,
+                           inds, scores, sgate, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

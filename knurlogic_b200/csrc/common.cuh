@@ -80,6 +80,12 @@ __device__ __forceinline__ float silu_f32(float g) {
     return g / (1.0f + expf(-g));
 }
 
+// gelu's tanh form (mlx's gelu_approx, torch's gelu_pytorch_tanh):
+// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), in fp32
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+
 __device__ __forceinline__ float sigmoid_f32(float g) {
     return 1.0f / (1.0f + expf(-g));
 }

@@ -322,7 +322,7 @@ __device__ __forceinline__ void run_tile(const RoutedSet &r, const TileInfo &in,
                     const int p = s_pairs[tk];
                     if (p < 0 || row >= OUT) continue;
                     r.out[(size_t)p * OUT + row] = epilogue_value<DUAL>(
-                        acc[0][mt][i], acc[NMAT - 1][mt][i], r.pair_scale, p, r.out_f16);
+                        acc[0][mt][i], acc[NMAT - 1][mt][i], r.pair_scale, p, r.out_f16, r.act);
                 }
         }
     }
@@ -620,6 +620,7 @@ static RoutedSet set_of(const RoutedIO &r, const vqmoe_linear *w0, const vqmoe_l
     s.out = static_cast<uint16_t *>(r.out);
     s.out_f16 = r.out_f16;
     s.pair_scale = r.pair_scale;
+    s.act = r.act;
     return s;
 }
 

@@ -115,19 +115,22 @@ struct Pipe {
 // Two accumulators -> two packed outputs (the first in the low half).
 // _SwiGLU (qwen3_5.py:108-112): bf16(bf16(silu(g)) * u) with g and u the
 // bf16 outputs of the gate and up matmuls; otherwise bf16(bf16(y) * routing
-// weight). Every rounding is the hardware's round-to-nearest-even
+// weight); with GeGLU (gemma4_text.py:131-135) gelu's tanh form in fp32
+// takes silu's place. Every rounding is the hardware's round-to-nearest-even
 // (cvt.rn.bf16x2), the same bits as the software rounding of the other
 // kernels for finite values; a bf16 x bf16 product is exact in float32. The
 // one approximation: silu's exp and division are the fast forms (ex2 /
 // rcp, a few float32 ulp before the bf16 rounding).
 template <bool GLU>
 __device__ __forceinline__ uint32_t pf_value2(uint32_t g0, uint32_t g1, uint32_t u0, uint32_t u1, bool scaled,
-                                              float s0, float s1, int out_f16) {
+                                              float s0, float s1, int out_f16, int act) {
     const uint32_t gb = cvt_bf16x2(__uint_as_float(g0), __uint_as_float(g1));
     uint32_t v;
     if (GLU) {
         const uint32_t ub = cvt_bf16x2(__uint_as_float(u0), __uint_as_float(u1));
-        const uint32_t sb = cvt_bf16x2(silu_fast(bf_lo(gb)), silu_fast(bf_hi(gb)));
+        const uint32_t sb = act == VQMOE_ACT_GEGLU
+                                ? cvt_bf16x2(gelu_tanh_f32(bf_lo(gb)), gelu_tanh_f32(bf_hi(gb)))
+                                : cvt_bf16x2(silu_fast(bf_lo(gb)), silu_fast(bf_hi(gb)));
         v = cvt_bf16x2(bf_lo(sb) * bf_lo(ub), bf_hi(sb) * bf_hi(ub));
     } else {
         v = scaled ? cvt_bf16x2(bf_lo(gb) * s0, bf_hi(gb) * s1) : gb;
@@ -322,7 +325,7 @@ __device__ __forceinline__ void pf_tile(const RoutedSet &r, const TileInfo &in, 
                 for (int jp = 0; jp < 16; ++jp)
                     ov[jp] = pf_value2<GLU>(dv[m][2 * jp], dv[m][2 * jp + 1], dv[1][2 * jp], dv[1][2 * jp + 1],
                                             r.pair_scale != nullptr, sh.pscale[32 * q + 2 * jp],
-                                            sh.pscale[32 * q + 2 * jp + 1], r.out_f16);
+                                            sh.pscale[32 * q + 2 * jp + 1], r.out_f16, r.act);
                 transpose_rows8(ov, lane);
                 const int row8 = rbm * 32 + 8 * (lane >> 3);
                 const int pb = 16 * (lane & 1) + 8 * ((lane >> 1) & 1) + 4 * ((lane >> 2) & 1);

@@ -23,6 +23,7 @@ struct RoutedSet {
     uint16_t *out;               // [P][OUT]
     int out_f16;                 // 1: fp16 (saturated) output, 0: bf16
     const float *pair_scale;     // optional [P]: y = bf16(bf16(acc) * s)
+    int act;                     // gate/up stage: VQMOE_ACT_SWIGLU or VQMOE_ACT_GEGLU
     int out_sorted;              // prefill path: output row = the pair's sorted position
 };
 
@@ -37,12 +38,14 @@ struct PipeArgs {
 
 template <bool DUAL>
 __device__ __forceinline__ uint16_t epilogue_value(float g, float u, const float *pair_scale,
-                                                   int pair, int out_f16) {
+                                                   int pair, int out_f16, int act = VQMOE_ACT_SWIGLU) {
     float v;
     if (DUAL) {
-        // _SwiGLU (qwen3_5.py:108-112): bf16(bf16(silu(g)) * u), g and u the
-        // bf16 outputs of the gate and up matmuls
-        v = bf16r(bf16r(silu_f32(bf16r(g))) * bf16r(u));
+        // _SwiGLU (qwen3_5.py:108-112) / geglu (gemma4_text.py:131-135):
+        // bf16(bf16(act(g)) * u), g and u the bf16 outputs of the gate and
+        // up matmuls, act in fp32
+        const float gb = bf16r(g);
+        v = bf16r(bf16r(act == VQMOE_ACT_GEGLU ? gelu_tanh_f32(gb) : silu_f32(gb)) * bf16r(u));
     } else {
         v = bf16r(g);
         if (pair_scale) v = bf16r(v * pair_scale[pair]);

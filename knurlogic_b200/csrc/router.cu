@@ -280,7 +280,7 @@ __device__ __forceinline__ uint32_t logit_key(float l, int j) {
 }
 
 template <int EPL>
-__device__ __forceinline__ void topk_warp(const float *__restrict__ lr, int E, int k, int lane,
+__device__ __forceinline__ void topk_warp(const float *__restrict__ lr, int E, int k, int lane, int mode,
                                           int &my_j, float &my_score) {
     float l[EPL], ex[EPL];
     uint32_t key[EPL];
@@ -312,7 +312,7 @@ __device__ __forceinline__ void topk_warp(const float *__restrict__ lr, int E, i
                 const uint32_t tk = key[b]; key[b] = key[b - 1]; key[b - 1] = tk;
                 const float te = ex[b]; ex[b] = ex[b - 1]; ex[b - 1] = te;
             }
-    float den = 0.0f, my_p = 0.0f;
+    float den = 0.0f, my_p = 0.0f, my_e = 0.0f;
     my_j = 0;
     for (int s = 0; s < k; ++s) {
         uint32_t best = key[0];
@@ -330,13 +330,19 @@ __device__ __forceinline__ void topk_warp(const float *__restrict__ lr, int E, i
             key[EPL - 1] = 0u;
         }
         const float p = e / z;
-        den += p;                      // sequential float32 sum, selection order
+        // sequential float32 sum, selection order: of the probabilities, or
+        // (softmax over the top k: its max is the top-1 logit, the global
+        // max) of the exponentials
+        den += mode == VQMOE_ROUTER_TOPK_SOFTMAX ? e : p;
         if (lane == s) {
             my_p = p;
+            my_e = e;
             my_j = j;
         }
     }
-    my_score = bf16r(my_p / den);
+    my_score = mode == VQMOE_ROUTER_SOFTMAX_TOPK   ? bf16r(my_p)
+               : mode == VQMOE_ROUTER_TOPK_SOFTMAX ? bf16r(my_e / den)
+                                                   : bf16r(my_p / den);
 }
 
 // Routing for one launch of up to kSelectMaxTok tokens in ONE CTA: top-k of
@@ -348,7 +354,7 @@ __global__ void __launch_bounds__(1024)
 router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int k, int has_shared,
                      int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate,
                      int32_t *__restrict__ cnt, int32_t *__restrict__ off, int32_t *__restrict__ list,
-                     int32_t *__restrict__ active, uint32_t *__restrict__ zero, int zero_words) {
+                     int32_t *__restrict__ active, uint32_t *__restrict__ zero, int zero_words, int mode) {
     extern __shared__ int32_t s_dyn[];
     int32_t *s_cnt = s_dyn;              // [E]
     int32_t *s_off = s_dyn + E;          // [E]
@@ -367,7 +373,7 @@ router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int
         const float *lr = logits + (size_t)t * E1;
         int j;
         float sc;
-        topk_warp<EPL>(lr, E, k, lane, j, sc);
+        topk_warp<EPL>(lr, E, k, lane, mode, j, sc);
         if (lane < k) {
             inds[(size_t)t * k + lane] = j;
             scores[(size_t)t * k + lane] = sc;
@@ -431,14 +437,14 @@ router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int
 template <int EPL>
 __global__ void __launch_bounds__(256)
 router_topk_kernel_t(const float *__restrict__ logits, int T, int E, int E1, int k, int has_shared,
-                     int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate) {
+                     int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate, int mode) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
     if (t >= T) return;
     const float *lr = logits + (size_t)t * E1;
     int j;
     float sc;
-    topk_warp<EPL>(lr, E, k, lane, j, sc);
+    topk_warp<EPL>(lr, E, k, lane, mode, j, sc);
     if (lane < k) {
         inds[(size_t)t * k + lane] = j;
         scores[(size_t)t * k + lane] = sc;
@@ -448,18 +454,19 @@ router_topk_kernel_t(const float *__restrict__ logits, int T, int E, int E1, int
 
 template <int EPL>
 static void launch_topk_t(const float *logits, int T, int E, int E1, int k, int has_shared, int32_t *inds,
-                          float *scores, float *sgate, cudaStream_t st) {
-    router_topk_kernel_t<EPL><<<(T + 7) / 8, 256, 0, st>>>(logits, T, E, E1, k, has_shared, inds, scores, sgate);
+                          float *scores, float *sgate, int mode, cudaStream_t st) {
+    router_topk_kernel_t<EPL><<<(T + 7) / 8, 256, 0, st>>>(logits, T, E, E1, k, has_shared, inds, scores, sgate,
+                                                           mode);
 }
 
 static vqmoe_status launch_topk(const float *logits, int T, int E, int E1, int k, int has_shared,
-                                int32_t *inds, float *scores, float *sgate, cudaStream_t st) {
+                                int32_t *inds, float *scores, float *sgate, int mode, cudaStream_t st) {
     const int epl = (E + 31) / 32;
-    if (epl <= 1) launch_topk_t<1>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
-    else if (epl <= 2) launch_topk_t<2>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
-    else if (epl <= 4) launch_topk_t<4>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
-    else if (epl <= 8) launch_topk_t<8>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
-    else launch_topk_t<16>(logits, T, E, E1, k, has_shared, inds, scores, sgate, st);
+    if (epl <= 1) launch_topk_t<1>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
+    else if (epl <= 2) launch_topk_t<2>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
+    else if (epl <= 4) launch_topk_t<4>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
+    else if (epl <= 8) launch_topk_t<8>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
+    else launch_topk_t<16>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
     return check_launch("router_topk_kernel");
 }
 
@@ -492,11 +499,11 @@ vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t 
 vqmoe_status launch_router(const uint16_t *x, const uint16_t *w,
                            const uint16_t *wsg, int T, int H, int E, int k,
                            float *logits, int32_t *inds, float *scores,
-                           float *sgate, uint16_t *x16, cudaStream_t stream) {
+                           float *sgate, uint16_t *x16, int mode, cudaStream_t stream) {
     const int E1 = E + (wsg ? 1 : 0);
     vqmoe_status s = launch_logits(x, w, wsg, T, H, E, E1, logits, x16, stream);
     if (s != VQMOE_OK) return s;
-    return launch_topk(logits, T, E, E1, k, wsg != nullptr, inds, scores, sgate, stream);
+    return launch_topk(logits, T, E, E1, k, wsg != nullptr, inds, scores, sgate, mode, stream);
 }
 
 // Logits, then top-k + counting sort in one CTA when the launch is small
@@ -505,11 +512,11 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
                                  int H, int E, int k, float *logits, int32_t *inds, float *scores,
                                  float *sgate, uint16_t *x16, int32_t *cnt, int32_t *off,
                                  int32_t *list, int32_t *active, int32_t *rank_scratch,
-                                 uint32_t *zero, int zero_words, cudaStream_t stream) {
+                                 uint32_t *zero, int zero_words, int mode, cudaStream_t stream) {
     const int E1 = E + (wsg ? 1 : 0);
     const size_t smem_sel = (size_t)(2 * E + 2 * T * k) * sizeof(int32_t);
     if (T > kSelectMaxTok || E > 1024 || smem_sel > 100 * 1024) {
-        vqmoe_status s = launch_router(x, w, wsg, T, H, E, k, logits, inds, scores, sgate, x16, stream);
+        vqmoe_status s = launch_router(x, w, wsg, T, H, E, k, logits, inds, scores, sgate, x16, mode, stream);
         if (s != VQMOE_OK) return s;
         return launch_route(inds, T * k, E, cnt, off, list, active, rank_scratch, zero, zero_words, stream);
     }
@@ -534,7 +541,7 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
         if (dev >= 0 && dev < 64) configured[dev] = 100 * 1024;
     }
     if (launch_pdl(fn, dim3(1), dim3(1024), smem_sel, stream, logits, T, E, E1, k, (int)(wsg != nullptr), inds,
-                   scores, sgate, cnt, off, list, active, zero, zero_words) != cudaSuccess)
+                   scores, sgate, cnt, off, list, active, zero, zero_words, mode) != cudaSuccess)
         return check_launch("router_select_kernel");
     return check_launch("router_select_kernel");
 }

@@ -8,7 +8,7 @@ namespace vqmoe {
 
 vqmoe_status launch_router(const uint16_t *x, const uint16_t *w, const uint16_t *wsg, int T,
                            int H, int E, int k, float *logits, int32_t *inds, float *scores,
-                           float *sgate, uint16_t *x16, cudaStream_t stream);
+                           float *sgate, uint16_t *x16, int mode, cudaStream_t stream);
 vqmoe_status launch_route(const int32_t *inds, int P, int E, int32_t *cnt, int32_t *off,
                           int32_t *list, int32_t *active, int32_t *rank_scratch, uint32_t *zero,
                           int zero_words, cudaStream_t stream);
@@ -16,7 +16,7 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
                                  int H, int E, int k, float *logits, int32_t *inds, float *scores,
                                  float *sgate, uint16_t *x16, int32_t *cnt, int32_t *off,
                                  int32_t *list, int32_t *active, int32_t *rank_scratch,
-                                 uint32_t *zero, int zero_words, cudaStream_t stream);
+                                 uint32_t *zero, int zero_words, int mode, cudaStream_t stream);
 vqmoe_status launch_to_f16(const uint16_t *x, uint16_t *x16, size_t n, cudaStream_t stream);
 
 // The routed experts of one stage: pairs grouped by expert (route_kernel).
@@ -28,6 +28,7 @@ struct RoutedIO {
     void *out;              // [P][OUT]
     int out_f16;            // fp16 (saturated) output instead of bf16
     const float *pair_scale;
+    int act;                // a gate/up stage's VQMOE_ACT_*
     void *xs;               // [P][IN] fp16 scratch (the prefill path's sorted inputs), or null
 };
 

@@ -57,18 +57,27 @@ class SharedExpert(nn.Module):
 
 
 class SparseMoeBlock(nn.Module):
-    """Qwen3.5-MoE `SparseMoeBlock` on B200. `forward(x [..., H] bf16)`."""
+    """Qwen3.5-MoE `SparseMoeBlock` on B200. `forward(x [..., H] bf16)`.
 
-    norm_topk_prob = True
+    `router_mode` picks how the k weights come from the router logits:
+    `_lib.ROUTER_SOFTMAX_TOPK_RENORM` (Qwen3.5, `qwen3_5.py:174-179`, the
+    default), `_lib.ROUTER_TOPK_SOFTMAX` (Qwen4-exp's block with
+    `norm_topk_prob`, `qwen4_exp.py:806-810`) or `_lib.ROUTER_SOFTMAX_TOPK`
+    (Qwen4-exp without it, `qwen4_exp.py:811-814`)."""
 
     def __init__(self, gate_weight: torch.Tensor, switch_mlp: SwitchGLU,
                  top_k: int, shared_expert: SharedExpert | None = None,
                  shared_expert_gate_weight: torch.Tensor | None = None,
-                 sharding_group=None):
+                 sharding_group=None, router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM):
         super().__init__()
         E, H = gate_weight.shape
         self.num_experts, self.hidden = int(E), int(H)
         self.top_k = int(top_k)
+        if router_mode not in (_lib.ROUTER_SOFTMAX_TOPK_RENORM, _lib.ROUTER_TOPK_SOFTMAX,
+                               _lib.ROUTER_SOFTMAX_TOPK):
+            raise ValueError(f"router_mode {router_mode} (0, 1 or 2)")
+        self.router_mode = int(router_mode)
+        self.norm_topk_prob = router_mode != _lib.ROUTER_SOFTMAX_TOPK
         self.gate = _bf16_linear(gate_weight)
         self.switch_mlp = switch_mlp
         if (shared_expert is None) != (shared_expert_gate_weight is None):
@@ -95,8 +104,9 @@ class SparseMoeBlock(nn.Module):
         b = _lib.Block()
         b.hidden, b.num_experts, b.top_k = self.hidden, self.num_experts, self.top_k
         b.router_w = self.gate.weight.data_ptr()
-        b.gate, b.up, b.down = (sm.gate_proj.descriptor(), sm.up_proj.descriptor(),
+        b.gate, b.up, b.down = (sm.gate_descriptor(), sm.up_proj.descriptor(),
                                 sm.down_proj.descriptor())
+        b.router_mode = self.router_mode
         if self.shared_expert is not None:
             se = self.shared_expert
             b.shared_inter = se.gate_proj.weight.shape[0]
@@ -146,14 +156,17 @@ class SparseMoeBlock(nn.Module):
     # ------------------------------------------------------------------
     @classmethod
     def from_weights(cls, w: dict, top_k: int, prefix: str = "mlp.",
-                     group_size: int | None = None, sharding_group=None):
+                     group_size: int | None = None, sharding_group=None,
+                     router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM, activation=None):
         """Build from a state dict with the reference's names:
         `{prefix}gate.weight`; `{prefix}switch_mlp.{gate,up,down}_proj.`
         `{codes, codebook, vq_scales}` (VQ) or `.weight` (bf16), or the HF
         fused `{prefix}experts.gate_up_proj [E, 2I, H]` /
         `{prefix}experts.down_proj [E, H, I]` (split as
         `qwen3_5_moe.py:36-50`); `{prefix}shared_expert.{gate,up,down}_proj.`
-        `weight`, `{prefix}shared_expert_gate.weight`."""
+        `weight`, `{prefix}shared_expert_gate.weight`. `router_mode` and
+        `activation` (a `SwiGLU` or `GeGLU`) select the router and the
+        experts' activation variants."""
         p = prefix
         sw = f"{p}switch_mlp."
         if f"{p}experts.gate_up_proj" in w:
@@ -182,8 +195,8 @@ class SparseMoeBlock(nn.Module):
                               w[f"{p}shared_expert.up_proj.weight"],
                               w[f"{p}shared_expert.down_proj.weight"])
             seg = w[f"{p}shared_expert_gate.weight"]
-        return cls(w[f"{p}gate.weight"], SwitchGLU(**projs), top_k, se, seg,
-                   sharding_group=sharding_group)
+        return cls(w[f"{p}gate.weight"], SwitchGLU(**projs, activation=activation), top_k, se, seg,
+                   sharding_group=sharding_group, router_mode=router_mode)
 
 
 class CapturedBlock:

@@ -256,15 +256,40 @@ class VQSwitchLinear(_SwitchBase):
         return out
 
 
+class SwiGLU(nn.Module):
+    """`_SwiGLU` (`qwen3_5.py:108-112`): bf16(bf16(silu(gate)) * x), silu in
+    float32. A marker for `SwitchGLU(activation=...)`: the kernels apply it
+    in the gate/up epilogue."""
+    code = _lib.ACT_SWIGLU
+
+
+class GeGLU(nn.Module):
+    """`GeGLU` (`gemma4_text.py:186-189`, `geglu` 131-135): bf16(bf16(
+    gelu_tanh(gate)) * x), gelu's tanh form in float32. A marker for
+    `SwitchGLU(activation=...)`."""
+    code = _lib.ACT_GEGLU
+
+
 class SwitchGLU(nn.Module):
-    """`SwitchGLU` (`switch_layers.py:151-193`) with the Qwen3.5 activation
-    (`_SwiGLU`, `qwen3_5.py:108-112`): y = down(bf16(silu(gate(x))) * up(x))
-    per (token, slot). One fused gate/up launch and one down launch."""
+    """`SwitchGLU` (`switch_layers.py:151-193`): y = down(act(gate(x), up(x)))
+    per (token, slot), act the Qwen3.5 `_SwiGLU` (default, `qwen3_5.py:
+    108-112`) or Gemma-4's `GeGLU`. One fused gate/up launch and one down
+    launch."""
 
     def __init__(self, gate_proj: _SwitchBase, up_proj: _SwitchBase,
-                 down_proj: _SwitchBase):
+                 down_proj: _SwitchBase, activation: nn.Module | None = None):
         super().__init__()
         self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
+        self.activation = activation if activation is not None else SwiGLU()
+        if not isinstance(self.activation, (SwiGLU, GeGLU)):
+            raise ValueError(f"activation {type(self.activation).__name__}: "
+                             "SwiGLU or GeGLU (the kernels apply it in the gate/up epilogue)")
+
+    def gate_descriptor(self) -> _lib.Linear:
+        """The gate linear's descriptor, naming the activation."""
+        g = self.gate_proj.descriptor()
+        g.activation = self.activation.code
+        return g
 
     def forward(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
         require_cuda(x, indices)
@@ -278,7 +303,7 @@ class SwitchGLU(nn.Module):
         ii = _contig(indices.reshape(T, k).to(torch.int32))
         y = torch.empty((T, k, self.down_proj.output_dims), dtype=torch.bfloat16,
                         device=x.device)
-        g, u, d = (m.descriptor() for m in (self.gate_proj, self.up_proj, self.down_proj))
+        g, u, d = self.gate_descriptor(), self.up_proj.descriptor(), self.down_proj.descriptor()
         ws_bytes = _lib.lib().vqmoe_switch_glu_workspace_size(ctypes_ref(g), ctypes_ref(d), T, k)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         _lib.call("vqmoe_switch_glu", ctypes_ref(g), ctypes_ref(u), ctypes_ref(d),

@@ -166,17 +166,33 @@ def _silu_f32(g: np.ndarray) -> np.ndarray:
         return (g / (np.float32(1) + np.exp(-g))).astype(np.float32)
 
 
+def _gelu_tanh_f32(g: np.ndarray) -> np.ndarray:
+    """gelu's tanh form in float32 (mlx `nn.gelu_approx`, torch's
+    gelu_pytorch_tanh): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))."""
+    g = g.astype(np.float32)
+    c = np.float32(0.7978845608028654)
+    inner = c * (g + np.float32(0.044715) * g * g * g)
+    return (np.float32(0.5) * g * (np.float32(1) + np.tanh(inner.astype(np.float32)))).astype(np.float32)
+
+
 def _sigmoid_f32(g: np.ndarray) -> np.ndarray:
     g = g.astype(np.float32)
     with np.errstate(over="ignore"):
         return (np.float32(1) / (np.float32(1) + np.exp(-g))).astype(np.float32)
 
 
-def router(x: np.ndarray, gate_w: np.ndarray, k: int):
+ROUTER_SOFTMAX_TOPK_RENORM, ROUTER_TOPK_SOFTMAX, ROUTER_SOFTMAX_TOPK = 0, 1, 2
+
+
+def router(x: np.ndarray, gate_w: np.ndarray, k: int, mode: int = ROUTER_SOFTMAX_TOPK_RENORM):
     """`SparseMoeBlock.__call__` router, `qwen3_5.py:174-179`.
 
     logits = bf16(x @ Wg^T); probs = softmax_f32(logits); the k largest;
     scores = bf16(p_sel / sum(p_sel)) with the renormalisation in float32.
+    The Qwen4-exp variants (`qwen4_exp.py:800-815`): mode 1
+    (`norm_topk_prob`) scores = bf16(softmax_f32 over the k selected
+    logits) -- e_sel / sum(e_sel), e = exp(l - max), the max being the top-1
+    logit; mode 2 scores = bf16(p_sel), not renormalised.
 
     Selection order: descending logit, ties to the lower expert index.
     softmax is monotone in the logit, so this is a top-k of `probs` (the
@@ -195,10 +211,13 @@ def router(x: np.ndarray, gate_w: np.ndarray, k: int):
         z[:, 0] += e[:, j]
     p = (e / z).astype(np.float32)
     psel = np.take_along_axis(p, order, axis=-1)
+    if mode == ROUTER_SOFTMAX_TOPK:
+        return order.astype(np.int32), bf16(psel), logits
+    vsel = np.take_along_axis(e, order, axis=-1) if mode == ROUTER_TOPK_SOFTMAX else psel
     den = np.zeros((T, 1), np.float32)
     for j in range(k):
-        den[:, 0] += psel[:, j]
-    scores = bf16((psel / den).astype(np.float32))
+        den[:, 0] += vsel[:, j]
+    scores = bf16((vsel / den).astype(np.float32))
     return order.astype(np.int32), scores, logits
 
 
@@ -221,8 +240,16 @@ def swiglu(up: np.ndarray, gate: np.ndarray) -> np.ndarray:
     return bf16(bf16(_silu_f32(gate)).astype(np.float64) * up)
 
 
+def geglu(up: np.ndarray, gate: np.ndarray) -> np.ndarray:
+    """`geglu` (`gemma4_text.py:131-135`): bf16(bf16(gelu_tanh_f32(gate)) * up)."""
+    return bf16(bf16(_gelu_tanh_f32(gate)).astype(np.float64) * up)
+
+
+ACT_SWIGLU, ACT_GEGLU = 0, 1
+
+
 def switch_glu(x: np.ndarray, inds: np.ndarray, gate_w, up_w, down_w,
-               vq: bool) -> np.ndarray:
+               vq: bool, act: int = ACT_SWIGLU) -> np.ndarray:
     """`SwitchGLU.__call__` (`switch_layers.py:172-193`): [T, k, H] bf16.
     The sort by expert it does for >= 64 pairs does not change any value."""
     T, k = inds.shape
@@ -230,7 +257,7 @@ def switch_glu(x: np.ndarray, inds: np.ndarray, gate_w, up_w, down_w,
     ex = inds.reshape(-1)
     u = switch_linear(rows, ex, up_w, vq)
     g = switch_linear(rows, ex, gate_w, vq)
-    a = swiglu(u, g)
+    a = geglu(u, g) if act == ACT_GEGLU else swiglu(u, g)
     y = switch_linear(a, ex, down_w, vq)
     return y.reshape(T, k, -1)
 
@@ -257,14 +284,15 @@ def shared_expert(x, sg_w, sup_w, sgate_w, sdown_w):
 
 
 def sparse_moe_block(x: np.ndarray, p: dict, k: int, vq: bool,
-                     return_parts: bool = False):
+                     return_parts: bool = False, router_mode: int = ROUTER_SOFTMAX_TOPK_RENORM,
+                     act: int = ACT_SWIGLU):
     """`SparseMoeBlock.__call__` (`qwen3_5.py:170-192`) on [T, H] bf16 input.
 
     `p` holds float32 arrays of bf16 (router, shared expert) and, for the
     experts, either dense bf16 `gate`, `up`, `down` [E, OUT, IN] or, with
     vq=True, already dequantised fp16 weights under the same names."""
-    inds, scores, logits = router(x, p["router"], k)
-    y = switch_glu(x, inds, p["gate"], p["up"], p["down"], vq)
+    inds, scores, logits = router(x, p["router"], k, router_mode)
+    y = switch_glu(x, inds, p["gate"], p["up"], p["down"], vq, act)
     routed = combine(y, scores)
     out = routed
     if "shared_gate" in p:

@@ -32,10 +32,11 @@ def test_every_declared_symbol_is_exported(so):
 
 
 def test_abi_version_and_struct_layout(so):
-    assert so.vqmoe_abi_version() == 1
-    # vqmoe_linear: 4 int32, 4 pointers, 4 int32
+    assert so.vqmoe_abi_version() == 2
+    # vqmoe_linear: 4 int32, 4 pointers, 4 int32 (the last: the activation)
     assert ctypes.sizeof(_lib.Linear) == 16 + 4 * 8 + 16
-    assert ctypes.sizeof(_lib.Block) == 16 + 8 + 3 * ctypes.sizeof(_lib.Linear) + 4 * 8
+    # vqmoe_block: ..., 4 shared pointers, router_mode, reserved
+    assert ctypes.sizeof(_lib.Block) == 16 + 8 + 3 * ctypes.sizeof(_lib.Linear) + 4 * 8 + 8
 
 
 def _block(H=2048, E=128, k=8, I=768, Is=768):
