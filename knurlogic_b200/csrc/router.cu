@@ -190,6 +190,100 @@ router_logits_dmma_kernel(const uint16_t *__restrict__ x, const uint16_t *__rest
     }
 }
 
+// Register-blocked variant for many tokens (T >= kBlkMinTok, E1 <= 144,
+// H % 256 == 0): a CTA owns 8 tokens x every logit column. Its 8 warps are
+// 2 column groups x 4 quarters of H; a warp keeps the fp64 accumulators of
+// up to 9 column tiles of 8 and reuses each token fragment for all of them,
+// so an operand byte loaded from L2 feeds 8-9 MMAs instead of 1. Lane (g, t)
+// of quarter q feeds inputs q*H/4 + t*H/16 + j of MMA j (one permutation of
+// the k axis for A and B alike), read as 16-byte vectors one batch of 8
+// MMAs ahead. The quarter partials are added in a fixed order (quarter 0
+// first), then rounded once to bf16.
+constexpr int kBlkMinTok = 1024;
+constexpr int kBlkMaxNt = 18;                    // E1 <= 144
+constexpr int kBlkNpg = kBlkMaxNt / 2;           // column tiles per warp
+
+__device__ __forceinline__ double bf16_f64(uint32_t h) { return (double)__uint_as_float(h << 16); }
+
+__global__ void __launch_bounds__(256)
+router_logits_dmma_blk_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
+                              const uint16_t *__restrict__ wsg, int T, int H, int E, int E1,
+                              float *__restrict__ logits, uint16_t *__restrict__ x16) {
+    __shared__ double part[4][8][kBlkMaxNt * 8];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int kq = warp & 3, ng = warp >> 2;
+    const int NT = (E1 + 7) >> 3, NT0 = (NT + 1) >> 1;
+    const int nt0 = ng ? NT0 : 0, nnt = ng ? NT - NT0 : NT0;   // this warp's column tiles
+    const int t0 = blockIdx.x * 8;
+    pdl_trigger();                   // the routing kernel may launch and wait for these logits
+    const int S = H >> 4;            // inputs per lane per quarter (multiple of 16)
+    const int k0 = kq * (H >> 2) + t * S;
+    const int tok = t0 + g;
+    const bool tok_ok = tok < T;
+    const uint16_t *xp = x + (size_t)(tok_ok ? tok : 0) * H + k0;
+    const uint16_t *wp[kBlkNpg];
+    bool row_ok[kBlkNpg];
+#pragma unroll
+    for (int n = 0; n < kBlkNpg; ++n) {
+        const int row = (nt0 + n) * 8 + g;
+        row_ok[n] = n < nnt && row < E1;
+        wp[n] = (row < E ? w + (size_t)row * H : (wsg ? wsg : w)) + k0;
+    }
+    double acc[kBlkNpg][2];
+#pragma unroll
+    for (int n = 0; n < kBlkNpg; ++n) acc[n][0] = acc[n][1] = 0.0;
+    uint4 xv, wv[kBlkNpg];
+    auto load = [&](int j0) {
+        xv = tok_ok ? __ldg(reinterpret_cast<const uint4 *>(xp + j0)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int n = 0; n < kBlkNpg; ++n)
+            wv[n] = row_ok[n] ? __ldg(reinterpret_cast<const uint4 *>(wp[n] + j0)) : make_uint4(0, 0, 0, 0);
+    };
+    load(0);
+    for (int j0 = 0; j0 < S; j0 += 8) {
+        const uint4 xc = xv;
+        uint4 wc[kBlkNpg];
+#pragma unroll
+        for (int n = 0; n < kBlkNpg; ++n) wc[n] = wv[n];
+        if (j0 + 8 < S) load(j0 + 8);
+        if (x16 && ng == 0 && tok_ok) {      // fp16 copy of the tokens for the VQ experts
+            const uint32_t u[4] = {xc.x, xc.y, xc.z, xc.w};
+            uint32_t h[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                h[q] = (uint32_t)bf16_to_f16_sat(u[q] & 0xFFFFu) | ((uint32_t)bf16_to_f16_sat(u[q] >> 16) << 16);
+            *reinterpret_cast<uint4 *>(x16 + (size_t)tok * H + k0 + j0) = make_uint4(h[0], h[1], h[2], h[3]);
+        }
+        const uint32_t xu[4] = {xc.x, xc.y, xc.z, xc.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const double a = bf16_f64((xu[q >> 1] >> (16 * (q & 1))) & 0xFFFFu);
+#pragma unroll
+            for (int n = 0; n < kBlkNpg; ++n) {
+                if (n < nnt) {
+                    const uint32_t wq = (q >> 1) == 0 ? wc[n].x : (q >> 1) == 1 ? wc[n].y : (q >> 1) == 2 ? wc[n].z : wc[n].w;
+                    dmma_f64(acc[n], a, bf16_f64((wq >> (16 * (q & 1))) & 0xFFFFu));
+                }
+            }
+        }
+    }
+    // D fragment: (token g, columns 8 (nt0 + n) + 2t, + 1)
+#pragma unroll
+    for (int n = 0; n < kBlkNpg; ++n)
+        if (n < nnt) {
+            part[kq][g][(nt0 + n) * 8 + 2 * t] = acc[n][0];
+            part[kq][g][(nt0 + n) * 8 + 2 * t + 1] = acc[n][1];
+        }
+    __syncthreads();
+    const int cols = NT * 8;
+    for (int o = tid; o < 8 * cols; o += 256) {
+        const int tg = o / cols, c = o - tg * cols;
+        const double v = ((part[0][tg][c] + part[1][tg][c]) + part[2][tg][c]) + part[3][tg][c];
+        if (t0 + tg < T && c < E1) logits[(size_t)(t0 + tg) * E1 + c] = bf16_to_f32(f64_to_bf16(v));
+    }
+}
+
 // Counting sort of pairs by expert (one CTA). Out-of-range expert ids are
 // dropped (their pairs get no output). Also zeroes `zero_words` words at
 // `zero` (the expert kernels' work counters and split-K semaphores).
@@ -484,7 +578,10 @@ vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t 
         if (dev >= 0 && dev < 64) configured_smem[dev] = (int)smem;
     }
     vqmoe_status s;
-    if (H % 256 == 0) {
+    if (H % 256 == 0 && T >= kBlkMinTok && E1 <= kBlkMaxNt * 8) {
+        router_logits_dmma_blk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
+        s = check_launch("router_logits_dmma_blk_kernel");
+    } else if (H % 256 == 0) {
         dim3 gt((E1 + 7) / 8, (T + 7) / 8);
         router_logits_dmma_kernel<<<gt, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
         s = check_launch("router_logits_dmma_kernel");
