@@ -191,95 +191,235 @@ router_logits_dmma_kernel(const uint16_t *__restrict__ x, const uint16_t *__rest
 }
 
 // Register-blocked variant for many tokens (T >= kBlkMinTok, E1 <= 144,
-// H % 256 == 0): a CTA owns 8 tokens x every logit column. Its 8 warps are
-// 2 column groups x 4 quarters of H; a warp keeps the fp64 accumulators of
-// up to 9 column tiles of 8 and reuses each token fragment for all of them,
-// so an operand byte loaded from L2 feeds 8-9 MMAs instead of 1. Lane (g, t)
-// of quarter q feeds inputs q*H/4 + t*H/16 + j of MMA j (one permutation of
-// the k axis for A and B alike), read as 16-byte vectors one batch of 8
-// MMAs ahead. The quarter partials are added in a fixed order (quarter 0
-// first), then rounded once to bf16.
+// H % 256 == 0): a CTA owns 8 MT tokens x every logit column. Its 8 warps
+// are NG column groups x 8 / NG slices of H; a warp keeps the fp64
+// accumulators of its MT x (up to NPG) tiles of 8 x 8, reusing each token
+// fragment for all its column tiles and each (converted) weight fragment
+// for all MT token tiles. Lane (g, t) of slice q feeds inputs
+// q*H/KS + t*H/(4 KS) + j of MMA j (one permutation of the k axis for A and
+// B alike), read as 16-byte vectors one batch of 8 MMAs ahead. The slice
+// partials are added in a fixed order (slice 0 first), then rounded once to
+// bf16.
 constexpr int kBlkMinTok = 1024;
 constexpr int kBlkMaxNt = 18;                    // E1 <= 144
-constexpr int kBlkNpg = kBlkMaxNt / 2;           // column tiles per warp
 
 __device__ __forceinline__ double bf16_f64(uint32_t h) { return (double)__uint_as_float(h << 16); }
 
+template <int MT, int NG>
 __global__ void __launch_bounds__(256)
 router_logits_dmma_blk_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
                               const uint16_t *__restrict__ wsg, int T, int H, int E, int E1,
                               float *__restrict__ logits, uint16_t *__restrict__ x16) {
-    __shared__ double part[4][8][kBlkMaxNt * 8];
+    constexpr int KS = 8 / NG;
+    constexpr int NPG = (kBlkMaxNt + NG - 1) / NG;
+    __shared__ double part[KS][8 * MT][kBlkMaxNt * 8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int kq = warp & 3, ng = warp >> 2;
-    const int NT = (E1 + 7) >> 3, NT0 = (NT + 1) >> 1;
-    const int nt0 = ng ? NT0 : 0, nnt = ng ? NT - NT0 : NT0;   // this warp's column tiles
-    const int t0 = blockIdx.x * 8;
+    const int kq = warp % KS, ng = warp / KS;
+    const int NT = (E1 + 7) >> 3, per = (NT + NG - 1) / NG;
+    const int nt0 = min(ng * per, NT), nnt = min(per, NT - nt0);   // this warp's column tiles
+    const int t0 = blockIdx.x * 8 * MT;
     pdl_trigger();                   // the routing kernel may launch and wait for these logits
-    const int S = H >> 4;            // inputs per lane per quarter (multiple of 16)
-    const int k0 = kq * (H >> 2) + t * S;
-    const int tok = t0 + g;
-    const bool tok_ok = tok < T;
-    const uint16_t *xp = x + (size_t)(tok_ok ? tok : 0) * H + k0;
-    const uint16_t *wp[kBlkNpg];
-    bool row_ok[kBlkNpg];
+    const int S = H / (4 * KS);      // inputs per lane per slice (multiple of 8)
+    const int k0 = kq * (H / KS) + t * S;
+    const uint16_t *xp[MT];
+    bool tok_ok[MT];
 #pragma unroll
-    for (int n = 0; n < kBlkNpg; ++n) {
+    for (int mt = 0; mt < MT; ++mt) {
+        const int tok = t0 + 8 * mt + g;
+        tok_ok[mt] = tok < T;
+        xp[mt] = x + (size_t)(tok_ok[mt] ? tok : 0) * H + k0;
+    }
+    const uint16_t *wp[NPG];
+    bool row_ok[NPG];
+#pragma unroll
+    for (int n = 0; n < NPG; ++n) {
         const int row = (nt0 + n) * 8 + g;
         row_ok[n] = n < nnt && row < E1;
         wp[n] = (row < E ? w + (size_t)row * H : (wsg ? wsg : w)) + k0;
     }
-    double acc[kBlkNpg][2];
+    double acc[MT][NPG][2];
 #pragma unroll
-    for (int n = 0; n < kBlkNpg; ++n) acc[n][0] = acc[n][1] = 0.0;
-    uint4 xv, wv[kBlkNpg];
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int n = 0; n < NPG; ++n) acc[mt][n][0] = acc[mt][n][1] = 0.0;
+    uint4 xv[MT], wv[NPG];
     auto load = [&](int j0) {
-        xv = tok_ok ? __ldg(reinterpret_cast<const uint4 *>(xp + j0)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int n = 0; n < kBlkNpg; ++n)
+        for (int mt = 0; mt < MT; ++mt)
+            xv[mt] = tok_ok[mt] ? __ldg(reinterpret_cast<const uint4 *>(xp[mt] + j0)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int n = 0; n < NPG; ++n)
             wv[n] = row_ok[n] ? __ldg(reinterpret_cast<const uint4 *>(wp[n] + j0)) : make_uint4(0, 0, 0, 0);
     };
     load(0);
     for (int j0 = 0; j0 < S; j0 += 8) {
-        const uint4 xc = xv;
-        uint4 wc[kBlkNpg];
+        uint4 xc[MT], wc[NPG];
 #pragma unroll
-        for (int n = 0; n < kBlkNpg; ++n) wc[n] = wv[n];
+        for (int mt = 0; mt < MT; ++mt) xc[mt] = xv[mt];
+#pragma unroll
+        for (int n = 0; n < NPG; ++n) wc[n] = wv[n];
         if (j0 + 8 < S) load(j0 + 8);
-        if (x16 && ng == 0 && tok_ok) {      // fp16 copy of the tokens for the VQ experts
-            const uint32_t u[4] = {xc.x, xc.y, xc.z, xc.w};
-            uint32_t h[4];
+        if (x16 && ng == 0) {                // fp16 copy of the tokens for the VQ experts
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                h[q] = (uint32_t)bf16_to_f16_sat(u[q] & 0xFFFFu) | ((uint32_t)bf16_to_f16_sat(u[q] >> 16) << 16);
-            *reinterpret_cast<uint4 *>(x16 + (size_t)tok * H + k0 + j0) = make_uint4(h[0], h[1], h[2], h[3]);
+            for (int mt = 0; mt < MT; ++mt) {
+                if (!tok_ok[mt]) continue;
+                const uint32_t u[4] = {xc[mt].x, xc[mt].y, xc[mt].z, xc[mt].w};
+                uint32_t h[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    h[q] = (uint32_t)bf16_to_f16_sat(u[q] & 0xFFFFu) | ((uint32_t)bf16_to_f16_sat(u[q] >> 16) << 16);
+                *reinterpret_cast<uint4 *>(x16 + (size_t)(t0 + 8 * mt + g) * H + k0 + j0) =
+                    make_uint4(h[0], h[1], h[2], h[3]);
+            }
         }
-        const uint32_t xu[4] = {xc.x, xc.y, xc.z, xc.w};
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            const double a = bf16_f64((xu[q >> 1] >> (16 * (q & 1))) & 0xFFFFu);
+            double a[MT];
 #pragma unroll
-            for (int n = 0; n < kBlkNpg; ++n) {
+            for (int mt = 0; mt < MT; ++mt) {
+                const uint32_t xq = (q >> 1) == 0 ? xc[mt].x : (q >> 1) == 1 ? xc[mt].y : (q >> 1) == 2 ? xc[mt].z : xc[mt].w;
+                a[mt] = bf16_f64((xq >> (16 * (q & 1))) & 0xFFFFu);
+            }
+#pragma unroll
+            for (int n = 0; n < NPG; ++n) {
                 if (n < nnt) {
                     const uint32_t wq = (q >> 1) == 0 ? wc[n].x : (q >> 1) == 1 ? wc[n].y : (q >> 1) == 2 ? wc[n].z : wc[n].w;
-                    dmma_f64(acc[n], a, bf16_f64((wq >> (16 * (q & 1))) & 0xFFFFu));
+                    const double b = bf16_f64((wq >> (16 * (q & 1))) & 0xFFFFu);
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) dmma_f64(acc[mt][n], a[mt], b);
                 }
             }
         }
     }
-    // D fragment: (token g, columns 8 (nt0 + n) + 2t, + 1)
+    // D fragment of tile (mt, n): (token 8mt + g, columns 8 (nt0 + n) + 2t, + 1)
 #pragma unroll
-    for (int n = 0; n < kBlkNpg; ++n)
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int n = 0; n < NPG; ++n)
+            if (n < nnt) {
+                part[kq][8 * mt + g][(nt0 + n) * 8 + 2 * t] = acc[mt][n][0];
+                part[kq][8 * mt + g][(nt0 + n) * 8 + 2 * t + 1] = acc[mt][n][1];
+            }
+    __syncthreads();
+    const int cols = NT * 8;
+    for (int o = tid; o < 8 * MT * cols; o += 256) {
+        const int tg = o / cols, c = o - tg * cols;
+        double v = part[0][tg][c];
+#pragma unroll
+        for (int q = 1; q < KS; ++q) v += part[q][tg][c];
+        if (t0 + tg < T && c < E1) logits[(size_t)(t0 + tg) * E1 + c] = bf16_to_f32(f64_to_bf16(v));
+    }
+}
+
+// The same with the m16n8k8 fp64 MMA and 16 tokens per CTA: per MMA lane
+// (g, t) feeds k-slots t and t + 4 with two consecutive inputs of its
+// segment (a0 / a1: tokens g / g + 8 at slot t, a2 / a3 at slot t + 4;
+// b0 / b1: column g at slots t / t + 4), so a 16-byte vector covers 4 MMAs.
+__device__ __forceinline__ void dmma_f64_k8(double (&d)[4], double a0, double a1, double a2, double a3, double b0,
+                                            double b1) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a0), "d"(a1), "d"(a2), "d"(a3), "d"(b0), "d"(b1));
+}
+
+template <int NG>
+__global__ void __launch_bounds__(256)
+router_logits_dmma16_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
+                            const uint16_t *__restrict__ wsg, int T, int H, int E, int E1,
+                            float *__restrict__ logits, uint16_t *__restrict__ x16) {
+    constexpr int KS = 8 / NG;
+    constexpr int NPG = (kBlkMaxNt + NG - 1) / NG;
+    __shared__ double part[KS][16][kBlkMaxNt * 8];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int kq = warp % KS, ng = warp / KS;
+    const int NT = (E1 + 7) >> 3, per = (NT + NG - 1) / NG;
+    const int nt0 = min(ng * per, NT), nnt = min(per, NT - nt0);
+    const int t0 = blockIdx.x * 16;
+    pdl_trigger();
+    const int S = H / (4 * KS);
+    const int k0 = kq * (H / KS) + t * S;
+    const uint16_t *xp[2];
+    bool tok_ok[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int tok = t0 + 8 * h + g;
+        tok_ok[h] = tok < T;
+        xp[h] = x + (size_t)(tok_ok[h] ? tok : 0) * H + k0;
+    }
+    const uint16_t *wp[NPG];
+    bool row_ok[NPG];
+#pragma unroll
+    for (int n = 0; n < NPG; ++n) {
+        const int row = (nt0 + n) * 8 + g;
+        row_ok[n] = n < nnt && row < E1;
+        wp[n] = (row < E ? w + (size_t)row * H : (wsg ? wsg : w)) + k0;
+    }
+    double acc[NPG][4];
+#pragma unroll
+    for (int n = 0; n < NPG; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0;
+    uint4 xv[2], wv[NPG];
+    auto load = [&](int j0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            xv[h] = tok_ok[h] ? __ldg(reinterpret_cast<const uint4 *>(xp[h] + j0)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int n = 0; n < NPG; ++n)
+            wv[n] = row_ok[n] ? __ldg(reinterpret_cast<const uint4 *>(wp[n] + j0)) : make_uint4(0, 0, 0, 0);
+    };
+    load(0);
+    for (int j0 = 0; j0 < S; j0 += 8) {
+        uint4 xc[2], wc[NPG];
+        xc[0] = xv[0];
+        xc[1] = xv[1];
+#pragma unroll
+        for (int n = 0; n < NPG; ++n) wc[n] = wv[n];
+        if (j0 + 8 < S) load(j0 + 8);
+        if (x16 && ng == 0) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (!tok_ok[h]) continue;
+                const uint32_t u[4] = {xc[h].x, xc[h].y, xc[h].z, xc[h].w};
+                uint32_t f[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    f[q] = (uint32_t)bf16_to_f16_sat(u[q] & 0xFFFFu) | ((uint32_t)bf16_to_f16_sat(u[q] >> 16) << 16);
+                *reinterpret_cast<uint4 *>(x16 + (size_t)(t0 + 8 * h + g) * H + k0 + j0) = make_uint4(f[0], f[1], f[2], f[3]);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {        // word q: inputs j0 + 2q (slot t), j0 + 2q + 1 (slot t + 4)
+            const uint32_t x0 = q == 0 ? xc[0].x : q == 1 ? xc[0].y : q == 2 ? xc[0].z : xc[0].w;
+            const uint32_t x1 = q == 0 ? xc[1].x : q == 1 ? xc[1].y : q == 2 ? xc[1].z : xc[1].w;
+            const double a0 = bf16_f64(x0 & 0xFFFFu), a2 = bf16_f64(x0 >> 16);
+            const double a1 = bf16_f64(x1 & 0xFFFFu), a3 = bf16_f64(x1 >> 16);
+#pragma unroll
+            for (int n = 0; n < NPG; ++n) {
+                if (n < nnt) {
+                    const uint32_t wq = q == 0 ? wc[n].x : q == 1 ? wc[n].y : q == 2 ? wc[n].z : wc[n].w;
+                    dmma_f64_k8(acc[n], a0, a1, a2, a3, bf16_f64(wq & 0xFFFFu), bf16_f64(wq >> 16));
+                }
+            }
+        }
+    }
+    // D fragment: c0 / c1 (token g, columns 2t / 2t + 1), c2 / c3 (token g + 8)
+#pragma unroll
+    for (int n = 0; n < NPG; ++n)
         if (n < nnt) {
-            part[kq][g][(nt0 + n) * 8 + 2 * t] = acc[n][0];
-            part[kq][g][(nt0 + n) * 8 + 2 * t + 1] = acc[n][1];
+            const int c = (nt0 + n) * 8 + 2 * t;
+            part[kq][g][c] = acc[n][0];
+            part[kq][g][c + 1] = acc[n][1];
+            part[kq][g + 8][c] = acc[n][2];
+            part[kq][g + 8][c + 1] = acc[n][3];
         }
     __syncthreads();
     const int cols = NT * 8;
-    for (int o = tid; o < 8 * cols; o += 256) {
+    for (int o = tid; o < 16 * cols; o += 256) {
         const int tg = o / cols, c = o - tg * cols;
-        const double v = ((part[0][tg][c] + part[1][tg][c]) + part[2][tg][c]) + part[3][tg][c];
+        double v = part[0][tg][c];
+#pragma unroll
+        for (int q = 1; q < KS; ++q) v += part[q][tg][c];
         if (t0 + tg < T && c < E1) logits[(size_t)(t0 + tg) * E1 + c] = bf16_to_f32(f64_to_bf16(v));
     }
 }
@@ -579,7 +719,11 @@ vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t 
     }
     vqmoe_status s;
     if (H % 256 == 0 && T >= kBlkMinTok && E1 <= kBlkMaxNt * 8) {
-        router_logits_dmma_blk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
+        if (T >= 2 * kBlkMinTok)
+            router_logits_dmma16_kernel<4><<<(T + 15) / 16, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
+        else
+            router_logits_dmma_blk_kernel<1, 2><<<(T + 7) / 8, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits,
+                                                                                   x16);
         s = check_launch("router_logits_dmma_blk_kernel");
     } else if (H % 256 == 0) {
         dim3 gt((E1 + 7) / 8, (T + 7) / 8);
