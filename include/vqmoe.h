@@ -46,7 +46,7 @@ extern "C" {
 #endif
 
 /* 2: vqmoe_linear.activation (was reserved), vqmoe_block.router_mode and
- * its trailing reserved word, vqmoe_router_ex. */
+ * its trailing reserved word, vqmoe_router_ex, vqmoe_moe_experts. */
 #define VQMOE_ABI_VERSION 2
 
 #if defined(__GNUC__)
@@ -229,12 +229,30 @@ VQMOE_API vqmoe_status vqmoe_router(const void *x, const void *router_w,
                           void *stream);
 
 /* vqmoe_router with the weights of a router variant (VQMOE_ROUTER_*):
- * Qwen4-exp's SparseMoeBlock router, qwen4_exp.py:800-815. */
+ * Qwen4-exp's SparseMoeBlock router, qwen4_exp.py:800-815. expert_scale
+ * (optional, [num_experts] float): each selected weight becomes
+ * bf16(weight * expert_scale[expert]) -- Gemma-4's Router.per_expert_scale
+ * (gemma4_text.py:156-182, with VQMOE_ROUTER_TOPK_SOFTMAX; its RMS norm
+ * of the input is the caller's). */
 VQMOE_API vqmoe_status vqmoe_router_ex(const void *x, const void *router_w,
                           const void *shared_expert_gate_w, int32_t tokens,
                           int32_t hidden, int32_t num_experts, int32_t top_k,
-                          int32_t router_mode, int32_t *inds, float *scores,
-                          float *sgate, void *workspace, size_t workspace_bytes,
+                          int32_t router_mode, const float *expert_scale,
+                          int32_t *inds, float *scores, float *sgate,
+                          void *workspace, size_t workspace_bytes, void *stream);
+
+/* Gemma-4's Experts.__call__ (gemma4_text.py:196-214): out[T, H] bf16 =
+ * sum over the k slots of bf16(y[t, s] * scores[t, s]), in fp32 and rounded
+ * once, with y = vqmoe_switch_glu(gate, up, down, x, indices) (GeGLU via
+ * gate->activation). */
+VQMOE_API size_t vqmoe_moe_experts_workspace_size(const vqmoe_linear *gate,
+                                                  const vqmoe_linear *down,
+                                                  int32_t tokens, int32_t top_k);
+VQMOE_API vqmoe_status vqmoe_moe_experts(const vqmoe_linear *gate,
+                          const vqmoe_linear *up, const vqmoe_linear *down,
+                          const void *x, const int32_t *indices,
+                          const float *scores, int32_t tokens, int32_t top_k,
+                          void *out, void *workspace, size_t workspace_bytes,
                           void *stream);
 
 /* Dense fp16 weights of experts [first, first + count): out [count, OUT, IN]

@@ -7,6 +7,7 @@ the reference's split rules (`tensor_split`).
 """
 from .switch_layers import GeGLU, SwiGLU, SwitchGLU, SwitchLinear, VQSwitchLinear  # noqa: F401
 from .moe import CapturedBlock, SharedExpert, SparseMoeBlock  # noqa: F401
+from . import gemma4  # noqa: F401
 
 __all__ = ["SwitchGLU", "SwitchLinear", "VQSwitchLinear", "SwiGLU", "GeGLU", "SharedExpert", "CapturedBlock",
            "SparseMoeBlock"]

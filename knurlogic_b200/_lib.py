@@ -80,7 +80,11 @@ SIGNATURES = [
       c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_router_ex", c_int32,
      [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
-      c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+      c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("vqmoe_moe_experts_workspace_size", c_size_t, [POINTER(Linear), POINTER(Linear), c_int32, c_int32]),
+    ("vqmoe_moe_experts", c_int32,
+     [POINTER(Linear), POINTER(Linear), POINTER(Linear), c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+      c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_dequant", c_int32,
      [POINTER(Linear), c_int32, c_int32, c_void_p, c_void_p]),
     ("vqmoe_vq_layout_bytes", c_int32,

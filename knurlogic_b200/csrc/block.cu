@@ -567,6 +567,70 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
     return VQMOE_OK;
 }
 
+// Experts.__call__ of gemma4_text.py:196-214: y = SwitchGLU(x, indices),
+// out[t] = sum_s w[t, s] * y[t, s] -- per pair bf16(y * w), summed over the
+// k slots in fp32 and rounded once (the block's combine without a shared
+// expert). Workspace: the SwitchGLU workspace, then the [T, k, H] bf16
+// expert outputs.
+static size_t moe_experts_ybuf_offset(const GluWs &w) { return align_up(w.bytes, 256); }
+
+size_t vqmoe_moe_experts_workspace_size(const vqmoe_linear *gate, const vqmoe_linear *down, int32_t tokens,
+                                        int32_t top_k) {
+    if (!gate || !down || tokens <= 0 || top_k <= 0) return 0;
+    const int T = std::min<int>(tokens, kMaxTokensPerLaunch);
+    const GluWs w = carve_glu(nullptr, gate, down, T, top_k, T);
+    return align_up(moe_experts_ybuf_offset(w) + (size_t)T * top_k * gate->in_features * sizeof(uint16_t), 256);
+}
+
+vqmoe_status vqmoe_moe_experts(const vqmoe_linear *gate, const vqmoe_linear *up, const vqmoe_linear *down,
+                               const void *x, const int32_t *indices, const float *scores, int32_t tokens,
+                               int32_t top_k, void *out, void *workspace, size_t workspace_bytes, void *stream) {
+    vqmoe_status s;
+    if ((s = check_linear(gate, "gate_proj")) != VQMOE_OK) return s;
+    if ((s = check_linear(up, "up_proj")) != VQMOE_OK) return s;
+    if ((s = check_linear(down, "down_proj")) != VQMOE_OK) return s;
+    if ((s = check_glu_activation(gate)) != VQMOE_OK) return s;
+    if (tokens <= 0 || top_k <= 0) return set_error(VQMOE_BAD_SHAPE, "tokens %d top_k %d", tokens, top_k);
+    const int I = gate->out_features, H = gate->in_features, E = gate->num_experts;
+    if (up->out_features != I || up->in_features != H || down->out_features != H ||
+        down->in_features != I || up->num_experts != E || down->num_experts != E ||
+        gate->format != up->format)
+        return set_error(VQMOE_BAD_SHAPE, "moe_experts: inconsistent gate/up/down shapes");
+    if (E > 1024) return set_error(VQMOE_BAD_SHAPE, "moe_experts: %d experts (<= 1024)", E);
+    if (!aligned_ptr(x) || !aligned_ptr(out) || !indices || !scores || !aligned_ptr(workspace))
+        return set_error(VQMOE_BAD_POINTER, "x / indices / scores / out / workspace");
+    const int chunk = std::min<int>(tokens, kMaxTokensPerLaunch);
+    GluWs w = carve_glu(workspace, gate, down, chunk, top_k, chunk);
+    const size_t need = vqmoe_moe_experts_workspace_size(gate, down, tokens, top_k);
+    if (workspace_bytes < need)
+        return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, need);
+    uint16_t *ybuf = reinterpret_cast<uint16_t *>(static_cast<char *>(workspace) + moe_experts_ybuf_offset(w));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool vq_in = gate->format == VQMOE_FMT_VQ_U8, vq_dn = down->format == VQMOE_FMT_VQ_U8;
+    for (int t0 = 0; t0 < tokens; t0 += chunk) {
+        const int T = std::min(chunk, tokens - t0), P = T * top_k;
+        const int32_t *ind = indices + (size_t)t0 * top_k;
+        const uint16_t *xt = static_cast<const uint16_t *>(x) + (size_t)t0 * H;
+        const RouteWs &rt = w.rt;
+        if (vq_in && (s = launch_to_f16(xt, w.x16, (size_t)T * H, st)) != VQMOE_OK) return s;
+        if ((s = launch_route(ind, P, E, rt.cnt, rt.off, rt.list, rt.active, rt.rank, rt.zero,
+                              rt.zero_words, st)) != VQMOE_OK)
+            return s;
+        RoutedIO r1 = routed_io(rt, E, top_k, P, vq_in ? (const void *)w.x16 : (const void *)xt, 0,
+                                w.act, vq_dn, nullptr);
+        r1.xs = w.xs;
+        r1.act = gate->activation;
+        RoutedIO r2 = routed_io(rt, E, top_k, P, w.act, 1, ybuf, 0, scores + (size_t)t0 * top_k);
+        if ((s = launch_experts(gate, up, &r1, down, r2, rt.zero, st)) != VQMOE_OK) return s;
+        const size_t nvec = (size_t)T * (H / 8);
+        const int grid = (int)std::min<size_t>((nvec + 255) / 256, (size_t)sm_count() * 8);
+        combine_kernel<<<grid, 256, 0, st>>>(ybuf, T, top_k, H, nullptr, nullptr,
+                                             static_cast<uint16_t *>(out) + (size_t)t0 * H, 0);
+        if ((s = check_launch("combine_kernel")) != VQMOE_OK) return s;
+    }
+    return VQMOE_OK;
+}
+
 vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x_per_pair,
                                  const int32_t *indices, int32_t tokens, int32_t top_k,
                                  void *y, void *workspace, size_t workspace_bytes, void *stream) {
@@ -605,8 +669,8 @@ vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x
 
 vqmoe_status vqmoe_router_ex(const void *x, const void *router_w, const void *sgw,
                              int32_t tokens, int32_t hidden, int32_t num_experts,
-                             int32_t top_k, int32_t router_mode, int32_t *inds, float *scores, float *sgate,
-                          void *workspace, size_t workspace_bytes, void *stream) {
+                             int32_t top_k, int32_t router_mode, const float *expert_scale, int32_t *inds,
+                             float *scores, float *sgate, void *workspace, size_t workspace_bytes, void *stream) {
     if (tokens <= 0 || hidden <= 0 || hidden % 8 || num_experts <= 0 || num_experts > 512 ||
         top_k <= 0 || top_k > 32 || top_k > num_experts)
         return set_error(VQMOE_BAD_SHAPE, "router: T %d H %d E %d k %d", tokens, hidden,
@@ -621,14 +685,14 @@ vqmoe_status vqmoe_router_ex(const void *x, const void *router_w, const void *sg
     return launch_router(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(router_w),
                          static_cast<const uint16_t *>(sgw), tokens, hidden, num_experts, top_k,
                          static_cast<float *>(workspace), inds, scores, sgate, nullptr, router_mode,
-                         static_cast<cudaStream_t>(stream));
+                         expert_scale, static_cast<cudaStream_t>(stream));
 }
 
 vqmoe_status vqmoe_router(const void *x, const void *router_w, const void *sgw, int32_t tokens, int32_t hidden,
                           int32_t num_experts, int32_t top_k, int32_t *inds, float *scores, float *sgate,
                           void *workspace, size_t workspace_bytes, void *stream) {
     return vqmoe_router_ex(x, router_w, sgw, tokens, hidden, num_experts, top_k, VQMOE_ROUTER_SOFTMAX_TOPK_RENORM,
-                           inds, scores, sgate, workspace, workspace_bytes, stream);
+                           nullptr, inds, scores, sgate, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

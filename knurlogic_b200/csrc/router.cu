@@ -588,7 +588,8 @@ __global__ void __launch_bounds__(1024)
 router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int k, int has_shared,
                      int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate,
                      int32_t *__restrict__ cnt, int32_t *__restrict__ off, int32_t *__restrict__ list,
-                     int32_t *__restrict__ active, uint32_t *__restrict__ zero, int zero_words, int mode) {
+                     int32_t *__restrict__ active, uint32_t *__restrict__ zero, int zero_words, int mode,
+                     const float *__restrict__ escale) {
     extern __shared__ int32_t s_dyn[];
     int32_t *s_cnt = s_dyn;              // [E]
     int32_t *s_off = s_dyn + E;          // [E]
@@ -609,6 +610,7 @@ router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int
         float sc;
         topk_warp<EPL>(lr, E, k, lane, mode, j, sc);
         if (lane < k) {
+            if (escale) sc = bf16r(sc * escale[j]);
             inds[(size_t)t * k + lane] = j;
             scores[(size_t)t * k + lane] = sc;
             s_pe[t * k + lane] = j;
@@ -671,7 +673,8 @@ router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int
 template <int EPL>
 __global__ void __launch_bounds__(256)
 router_topk_kernel_t(const float *__restrict__ logits, int T, int E, int E1, int k, int has_shared,
-                     int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate, int mode) {
+                     int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate, int mode,
+                     const float *__restrict__ escale) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
     if (t >= T) return;
@@ -680,6 +683,7 @@ router_topk_kernel_t(const float *__restrict__ logits, int T, int E, int E1, int
     float sc;
     topk_warp<EPL>(lr, E, k, lane, mode, j, sc);
     if (lane < k) {
+        if (escale) sc = bf16r(sc * escale[j]);
         inds[(size_t)t * k + lane] = j;
         scores[(size_t)t * k + lane] = sc;
     }
@@ -688,19 +692,20 @@ router_topk_kernel_t(const float *__restrict__ logits, int T, int E, int E1, int
 
 template <int EPL>
 static void launch_topk_t(const float *logits, int T, int E, int E1, int k, int has_shared, int32_t *inds,
-                          float *scores, float *sgate, int mode, cudaStream_t st) {
+                          float *scores, float *sgate, int mode, const float *escale, cudaStream_t st) {
     router_topk_kernel_t<EPL><<<(T + 7) / 8, 256, 0, st>>>(logits, T, E, E1, k, has_shared, inds, scores, sgate,
-                                                           mode);
+                                                           mode, escale);
 }
 
 static vqmoe_status launch_topk(const float *logits, int T, int E, int E1, int k, int has_shared,
-                                int32_t *inds, float *scores, float *sgate, int mode, cudaStream_t st) {
+                                int32_t *inds, float *scores, float *sgate, int mode, const float *escale,
+                                cudaStream_t st) {
     const int epl = (E + 31) / 32;
-    if (epl <= 1) launch_topk_t<1>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
-    else if (epl <= 2) launch_topk_t<2>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
-    else if (epl <= 4) launch_topk_t<4>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
-    else if (epl <= 8) launch_topk_t<8>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
-    else launch_topk_t<16>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, st);
+    if (epl <= 1) launch_topk_t<1>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, escale, st);
+    else if (epl <= 2) launch_topk_t<2>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, escale, st);
+    else if (epl <= 4) launch_topk_t<4>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, escale, st);
+    else if (epl <= 8) launch_topk_t<8>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, escale, st);
+    else launch_topk_t<16>(logits, T, E, E1, k, has_shared, inds, scores, sgate, mode, escale, st);
     return check_launch("router_topk_kernel");
 }
 
@@ -740,11 +745,11 @@ vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t 
 vqmoe_status launch_router(const uint16_t *x, const uint16_t *w,
                            const uint16_t *wsg, int T, int H, int E, int k,
                            float *logits, int32_t *inds, float *scores,
-                           float *sgate, uint16_t *x16, int mode, cudaStream_t stream) {
+                           float *sgate, uint16_t *x16, int mode, const float *escale, cudaStream_t stream) {
     const int E1 = E + (wsg ? 1 : 0);
     vqmoe_status s = launch_logits(x, w, wsg, T, H, E, E1, logits, x16, stream);
     if (s != VQMOE_OK) return s;
-    return launch_topk(logits, T, E, E1, k, wsg != nullptr, inds, scores, sgate, mode, stream);
+    return launch_topk(logits, T, E, E1, k, wsg != nullptr, inds, scores, sgate, mode, escale, stream);
 }
 
 // Logits, then top-k + counting sort in one CTA when the launch is small
@@ -757,7 +762,8 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
     const int E1 = E + (wsg ? 1 : 0);
     const size_t smem_sel = (size_t)(2 * E + 2 * T * k) * sizeof(int32_t);
     if (T > kSelectMaxTok || E > 1024 || smem_sel > 100 * 1024) {
-        vqmoe_status s = launch_router(x, w, wsg, T, H, E, k, logits, inds, scores, sgate, x16, mode, stream);
+        vqmoe_status s = launch_router(x, w, wsg, T, H, E, k, logits, inds, scores, sgate, x16, mode, nullptr,
+                                       stream);
         if (s != VQMOE_OK) return s;
         return launch_route(inds, T * k, E, cnt, off, list, active, rank_scratch, zero, zero_words, stream);
     }
@@ -782,7 +788,8 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
         if (dev >= 0 && dev < 64) configured[dev] = 100 * 1024;
     }
     if (launch_pdl(fn, dim3(1), dim3(1024), smem_sel, stream, logits, T, E, E1, k, (int)(wsg != nullptr), inds,
-                   scores, sgate, cnt, off, list, active, zero, zero_words, mode) != cudaSuccess)
+                   scores, sgate, cnt, off, list, active, zero, zero_words, mode,
+                   static_cast<const float *>(nullptr)) != cudaSuccess)
         return check_launch("router_select_kernel");
     return check_launch("router_select_kernel");
 }

@@ -8,7 +8,8 @@ namespace vqmoe {
 
 vqmoe_status launch_router(const uint16_t *x, const uint16_t *w, const uint16_t *wsg, int T,
                            int H, int E, int k, float *logits, int32_t *inds, float *scores,
-                           float *sgate, uint16_t *x16, int mode, cudaStream_t stream);
+                           float *sgate, uint16_t *x16, int mode, const float *escale,
+                           cudaStream_t stream);
 vqmoe_status launch_route(const int32_t *inds, int P, int E, int32_t *cnt, int32_t *off,
                           int32_t *list, int32_t *active, int32_t *rank_scratch, uint32_t *zero,
                           int zero_words, cudaStream_t stream);

@@ -184,7 +184,8 @@ def _sigmoid_f32(g: np.ndarray) -> np.ndarray:
 ROUTER_SOFTMAX_TOPK_RENORM, ROUTER_TOPK_SOFTMAX, ROUTER_SOFTMAX_TOPK = 0, 1, 2
 
 
-def router(x: np.ndarray, gate_w: np.ndarray, k: int, mode: int = ROUTER_SOFTMAX_TOPK_RENORM):
+def router(x: np.ndarray, gate_w: np.ndarray, k: int, mode: int = ROUTER_SOFTMAX_TOPK_RENORM,
+           expert_scale: np.ndarray | None = None):
     """`SparseMoeBlock.__call__` router, `qwen3_5.py:174-179`.
 
     logits = bf16(x @ Wg^T); probs = softmax_f32(logits); the k largest;
@@ -192,7 +193,9 @@ def router(x: np.ndarray, gate_w: np.ndarray, k: int, mode: int = ROUTER_SOFTMAX
     The Qwen4-exp variants (`qwen4_exp.py:800-815`): mode 1
     (`norm_topk_prob`) scores = bf16(softmax_f32 over the k selected
     logits) -- e_sel / sum(e_sel), e = exp(l - max), the max being the top-1
-    logit; mode 2 scores = bf16(p_sel), not renormalised.
+    logit; mode 2 scores = bf16(p_sel), not renormalised. Gemma-4's
+    per-expert scale (`gemma4_text.py:179-180`, with mode 1):
+    scores = bf16(scores * expert_scale[inds]).
 
     Selection order: descending logit, ties to the lower expert index.
     softmax is monotone in the logit, so this is a top-k of `probs` (the
@@ -212,12 +215,15 @@ def router(x: np.ndarray, gate_w: np.ndarray, k: int, mode: int = ROUTER_SOFTMAX
     p = (e / z).astype(np.float32)
     psel = np.take_along_axis(p, order, axis=-1)
     if mode == ROUTER_SOFTMAX_TOPK:
-        return order.astype(np.int32), bf16(psel), logits
-    vsel = np.take_along_axis(e, order, axis=-1) if mode == ROUTER_TOPK_SOFTMAX else psel
-    den = np.zeros((T, 1), np.float32)
-    for j in range(k):
-        den[:, 0] += vsel[:, j]
-    scores = bf16((vsel / den).astype(np.float32))
+        scores = bf16(psel)
+    else:
+        vsel = np.take_along_axis(e, order, axis=-1) if mode == ROUTER_TOPK_SOFTMAX else psel
+        den = np.zeros((T, 1), np.float32)
+        for j in range(k):
+            den[:, 0] += vsel[:, j]
+        scores = bf16((vsel / den).astype(np.float32))
+    if expert_scale is not None:
+        scores = bf16(scores.astype(np.float32) * np.asarray(expert_scale, np.float32)[order])
     return order.astype(np.int32), scores, logits
 
 
@@ -270,6 +276,25 @@ def combine(y: np.ndarray, scores: np.ndarray) -> np.ndarray:
     for j in range(prod.shape[1]):
         acc += prod[:, j]
     return bf16(acc)
+
+
+def moe_experts(x: np.ndarray, inds: np.ndarray, scores: np.ndarray, gate_w, up_w, down_w,
+                vq: bool, act: int = ACT_GEGLU) -> np.ndarray:
+    """Gemma-4's `Experts.__call__` (`gemma4_text.py:196-214`):
+    `(w * switch_glu(x, inds)).sum(-2)` with `combine`'s roundings."""
+    return combine(switch_glu(x, inds, gate_w, up_w, down_w, vq, act), scores)
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """`mx.fast.rms_norm(x, w, eps)` as restated for the Gemma-4 router
+    input (`gemma4_text.py:171`): float32 mean of squares, the normalised
+    value rounded to bf16, then times the bf16 weight, rounded again. The
+    reference's MLX kernel is not available here: this order of roundings
+    is this build's reading of it (unpinned)."""
+    xf = np.asarray(x, np.float32)
+    ms = (xf * xf).mean(axis=-1, keepdims=True, dtype=np.float32)
+    inv = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+    return bf16(bf16(xf * inv).astype(np.float32) * np.asarray(w, np.float32))
 
 
 def shared_expert(x, sg_w, sup_w, sgate_w, sdown_w):

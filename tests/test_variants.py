@@ -1,7 +1,8 @@
 """Router and activation variants of the same expert path: the Qwen4-exp
 router (`qwen4_exp.py:800-815`: softmax over the top-k logits with
-`norm_topk_prob`, or the top-k of the full softmax without it) and Gemma-4's
-GeGLU activation (`gemma4_text.py:131-135, 186-189`).
+`norm_topk_prob`, or the top-k of the full softmax without it), Gemma-4's
+GeGLU activation (`gemma4_text.py:131-135, 186-189`) and Gemma-4's router
+(per-expert scale) and experts module (`gemma4_text.py:156-214`).
 
 CPU: the oracle's pieces against independent restatements, and the ABI's
 argument checks (they return before any CUDA call). GPU: the kernels
@@ -55,6 +56,45 @@ def _fake_linear(out, inp, E=8, act=0):
                        activation=act)
 
 
+def test_oracle_expert_scale():
+    cfg = synth.CONFIGS["c2"]
+    w = synth.make_weights(cfg, seed=3, scales="ones")
+    x = to_np(synth.make_input(cfg, seed=3))
+    gw = to_np(w["mlp.gate.weight"])
+    es = np.random.default_rng(3).uniform(0.5, 1.5, cfg.experts).astype(np.float32)
+    i1, s1, _ = R.router(x, gw, cfg.top_k, R.ROUTER_TOPK_SOFTMAX)
+    i2, s2, _ = R.router(x, gw, cfg.top_k, R.ROUTER_TOPK_SOFTMAX, es)
+    assert np.array_equal(i1, i2)
+    assert np.array_equal(s2, R.bf16(s1 * es[i1]))
+
+
+def test_oracle_rms_norm_matches_torch():
+    x = R.bf16(np.random.default_rng(4).normal(0, 2, (16, 512)).astype(np.float32))
+    w = R.bf16(np.random.default_rng(5).uniform(0.5, 1.5, 512).astype(np.float32))
+    ours = R.rms_norm(x, w, 1e-6)
+    xt = torch.from_numpy(x)
+    inv = torch.rsqrt(xt.pow(2).mean(-1, keepdim=True) + 1e-6)
+    ref = ((xt * inv).to(torch.bfloat16).float() * torch.from_numpy(w)).to(torch.bfloat16).float().numpy()
+    # float32 rsqrt against numpy's 1/sqrt: the rare bf16 tie may land apart
+    assert (ours != ref).mean() < 1e-3
+    assert np.all(np.abs(ours - ref) <= np.abs(ref) * 2.0 ** -7)
+
+
+def test_moe_experts_arguments_are_checked():
+    so = _lib.lib()
+    H, I, E = 256, 128, 8
+    g, u, d = _fake_linear(I, H, E, act=_lib.ACT_GEGLU), _fake_linear(I, H, E), _fake_linear(H, I, E)
+    assert so.vqmoe_moe_experts_workspace_size(ctypes.byref(g), ctypes.byref(d), 4, 2) > \
+        so.vqmoe_switch_glu_workspace_size(ctypes.byref(g), ctypes.byref(d), 4, 2)
+    p = 1 << 12
+    st = so.vqmoe_moe_experts(ctypes.byref(g), ctypes.byref(u), ctypes.byref(d), p, p, None, 4, 2, p, p,
+                              1 << 30, None)
+    assert _lib.STATUS[st] == "BAD_POINTER"
+    st = so.vqmoe_moe_experts(ctypes.byref(g), ctypes.byref(u), ctypes.byref(u), p, p, p, 4, 2, p, p,
+                              1 << 30, None)
+    assert _lib.STATUS[st] == "BAD_SHAPE"
+
+
 def test_variant_arguments_are_checked():
     so = _lib.lib()
     H, I, E = 256, 128, 8
@@ -73,16 +113,17 @@ def test_variant_arguments_are_checked():
 
 # ------------------------------------------------------------------- GPU
 
-def _router_ex(x, w, k, mode):
+def _router_ex(x, w, k, mode, expert_scale=None):
     T, H = x.shape
     E = w.shape[0]
     inds = torch.empty(T, k, dtype=torch.int32, device=DEV)
     scores = torch.empty(T, k, dtype=torch.float32, device=DEV)
     n = _lib.lib().vqmoe_router_workspace_size(T, E)
     ws = torch.empty(n, dtype=torch.uint8, device=DEV)
+    es = None if expert_scale is None else expert_scale.to(DEV, torch.float32).contiguous()
     _lib.call("vqmoe_router_ex", x.data_ptr(), w.data_ptr(), None, T, H, E, k, mode,
-              inds.data_ptr(), scores.data_ptr(), None, ws.data_ptr(), n,
-              torch.cuda.current_stream().cuda_stream)
+              None if es is None else es.data_ptr(), inds.data_ptr(), scores.data_ptr(), None,
+              ws.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     return inds.cpu().numpy(), scores.cpu().numpy()
 
@@ -129,3 +170,58 @@ def test_geglu_block_matches_oracle(name, tokens):
     y = to_np(blk(x.to(DEV)))
     ref = R.sparse_moe_block(to_np(x), oracle_params(w), cfg.top_k, vq=True, act=R.ACT_GEGLU)
     assert_bf16_close(y, ref, f"geglu {name}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,tokens", [("c2", 64), ("c3", 2048)])
+def test_router_expert_scale_matches_oracle(name, tokens):
+    """Gemma-4's per-expert scale on the softmax over the top-k logits;
+    c3's 2048 tokens take the blocked logits kernel and the multi-CTA top-k."""
+    cfg = synth.CONFIGS[name]
+    w = synth.make_weights(cfg, seed=9, scales="ones")
+    x = synth.make_input(cfg, seed=9, tokens=tokens)
+    es = torch.from_numpy(np.random.default_rng(9).uniform(0.5, 1.5, cfg.experts).astype(np.float32))
+    inds, scores = _router_ex(x.to(DEV), w["mlp.gate.weight"].to(DEV), cfg.top_k, _lib.ROUTER_TOPK_SOFTMAX, es)
+    oi, osc, _ = R.router(to_np(x), to_np(w["mlp.gate.weight"]), cfg.top_k, R.ROUTER_TOPK_SOFTMAX, es.numpy())
+    assert np.array_equal(inds, oi), f"{int((inds != oi).sum())} indices differ"
+    # one bf16 step from the softmax (CUDA's expf against numpy's exp), and
+    # up to half a step more where the scaled weight is rounded again
+    assert np.all(np.abs(scores - osc) <= np.abs(osc) * 2.0 ** -6 + 1e-30)
+
+
+def _gemma_experts(w, cfg):
+    from knurlogic_b200 import SwitchGLU, VQSwitchLinear
+    from knurlogic_b200.gemma4 import Experts
+    lin = {n: VQSwitchLinear(w[f"mlp.switch_mlp.{n}_proj.codes"].to(DEV), w[f"mlp.switch_mlp.{n}_proj.codebook"].to(DEV),
+                             w[f"mlp.switch_mlp.{n}_proj.vq_scales"].to(DEV), group_size=cfg.group)
+           for n in ("gate", "up", "down")}
+    return Experts(SwitchGLU(lin["gate"], lin["up"], lin["down"], activation=GeGLU()))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,tokens", [("c2", 64), ("pf", 1024)])
+def test_gemma4_router_and_experts_match_oracle(name, tokens):
+    """The Gemma-4 modules end to end: the router on its own normalised
+    input (the oracle takes the module's RMS-normed rows, an unpinned step
+    restated separately), then the GeGLU experts and the weighted sum on the
+    decode path (c2) and the tcgen05 prefill path ("pf")."""
+    from tests.test_gpu_parity import assert_bf16_close
+    from knurlogic_b200.gemma4 import Router
+    cfg = (synth.MoEConfig("pf", 16, 4, 512, 256, 0, tokens, router="uniform")
+           if name == "pf" else synth.CONFIGS[name])
+    w = synth.make_weights(cfg, seed=14, scales="random")
+    x = synth.make_input(cfg, seed=14, tokens=tokens)
+    g = np.random.default_rng(14)
+    scale = torch.from_numpy(g.uniform(0.5, 1.5, cfg.hidden).astype(np.float32))
+    pes = torch.from_numpy(g.uniform(0.5, 1.5, cfg.experts).astype(np.float32))
+    router = Router(w["mlp.gate.weight"].to(DEV), scale.to(DEV), pes.to(DEV), cfg.top_k)
+    inds, weights = router(x.to(DEV))
+    xn = to_np(router.normalize(x.to(DEV)))
+    oi, osc, _ = R.router(xn, to_np(w["mlp.gate.weight"]), cfg.top_k, R.ROUTER_TOPK_SOFTMAX, pes.numpy())
+    assert np.array_equal(inds.cpu().numpy(), oi)
+    assert np.all(np.abs(weights.float().cpu().numpy() - osc) <= np.abs(osc) * 2.0 ** -6 + 1e-30)
+    experts = _gemma_experts(w, cfg)
+    y = to_np(experts(x.to(DEV), inds, weights))
+    p = oracle_params(w)
+    ref = R.moe_experts(to_np(x), oi, osc, p["gate"], p["up"], p["down"], vq=True, act=R.ACT_GEGLU)
+    assert_bf16_close(y, ref, f"gemma4 experts {name}")
