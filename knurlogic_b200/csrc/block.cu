@@ -165,7 +165,7 @@ struct RouteWs {
 };
 
 static void carve_route(Carve &c, RouteWs &w, int E, int P, int H, int T, int Is) {
-    w.cnt = c.take<int32_t>(E);
+    w.cnt = c.take<int32_t>(E + 1);            // cnt[E]: the routing kernel's finished-CTA count
     w.off = c.take<int32_t>(E + 1);
     w.list = c.take<int32_t>(P);
     w.active = c.take<int32_t>(E + 1);

@@ -34,10 +34,12 @@ router_logits_kernel(const uint16_t *__restrict__ x,
                      const uint16_t *__restrict__ w,
                      const uint16_t *__restrict__ wsg, int T, int H, int E,
                      int E1, float *__restrict__ logits,
-                     uint16_t *__restrict__ x16) {
+                     uint16_t *__restrict__ x16, uint32_t *__restrict__ zero2, int nzero2) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint16_t *xs = reinterpret_cast<uint16_t *>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (zero2 && blockIdx.x == 0 && blockIdx.y == 0)   // the routing kernel's counters
+        for (int i = tid; i < nzero2; i += blockDim.x) zero2[i] = 0u;
     const int t0 = blockIdx.y * kRouterTok;
     const int vec_per_row = H / 8;
     for (int v = tid; v < kRouterTok * vec_per_row; v += blockDim.x) {
@@ -128,10 +130,13 @@ __device__ __forceinline__ void dmma_f64(double (&d)[2], double a, double b) {
 __global__ void __launch_bounds__(256)
 router_logits_dmma_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w,
                           const uint16_t *__restrict__ wsg, int T, int H, int E, int E1,
-                          float *__restrict__ logits, uint16_t *__restrict__ x16) {
+                          float *__restrict__ logits, uint16_t *__restrict__ x16, uint32_t *__restrict__ zero2,
+                          int nzero2) {
     constexpr int NW = 8;                        // warps splitting H
     __shared__ double part[NW][8][8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (zero2 && blockIdx.x == 0 && blockIdx.y == 0)   // the routing kernel's counters
+        for (int i = tid; i < nzero2; i += blockDim.x) zero2[i] = 0u;
     const int g = lane >> 2, t = lane & 3;
     const int t0 = blockIdx.y * 8, e0 = blockIdx.x * 8;
     pdl_trigger();                   // the routing kernel may launch and wait for these logits
@@ -579,32 +584,35 @@ __device__ __forceinline__ void topk_warp(const float *__restrict__ lr, int E, i
                                                    : bf16r(my_p / den);
 }
 
-// Routing for one launch of up to kSelectMaxTok tokens in ONE CTA: top-k of
-// every token (a warp per token), then the counting sort of the (token,
-// slot) pairs by expert, without leaving the CTA. Zeroes `zero`.
+// Routing for one launch of up to kSelectMaxTok tokens: top-k of every
+// token (a warp per token, 8 tokens per CTA), each (token, slot) pair's rank
+// within its expert from a global atomic on cnt[expert], then the CTA that
+// finishes last (an atomic on cnt[E]) scans the counts and scatters the
+// pairs into per-expert lists. cnt[0..E] start at zero: the logits kernel
+// zeroes them, and this kernel reads nothing before it has waited for that
+// kernel. The order of pairs inside an expert's list is the atomics'
+// (each pair's output does not depend on it). Zeroes `zero`.
 constexpr int kSelectMaxTok = 512;
+constexpr int kSelectWarps = 8;
 template <int EPL>
-__global__ void __launch_bounds__(1024)
+__global__ void __launch_bounds__(kSelectWarps * 32)
 router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int k, int has_shared,
                      int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate,
                      int32_t *__restrict__ cnt, int32_t *__restrict__ off, int32_t *__restrict__ list,
-                     int32_t *__restrict__ active, uint32_t *__restrict__ zero, int zero_words, int mode,
-                     const float *__restrict__ escale) {
-    extern __shared__ int32_t s_dyn[];
-    int32_t *s_cnt = s_dyn;              // [E]
-    int32_t *s_off = s_dyn + E;          // [E]
-    int32_t *s_pe = s_dyn + 2 * E;       // [T*k] expert of each pair
-    int32_t *s_rank = s_pe + T * k;      // [T*k]
-    __shared__ int32_t s_wsum[32], s_asum[32];
+                     int32_t *__restrict__ active, int32_t *__restrict__ rank, uint32_t *__restrict__ zero,
+                     int zero_words, int mode, const float *__restrict__ escale) {
+    __shared__ int32_t s_off[1024];
+    __shared__ int32_t s_wc[kSelectWarps], s_wa[kSelectWarps];
+    __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // (the previous block call's expert kernel, the reader of `zero`, finished
     // before this call's logits kernel began)
-    for (int i = tid; i < zero_words; i += blockDim.x) zero[i] = 0u;
-    for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
+    if (blockIdx.x == 0)
+        for (int i = tid; i < zero_words; i += blockDim.x) zero[i] = 0u;
     pdl_trigger();                   // the expert kernel may launch and stage its codebooks
-    pdl_wait();                      // the logits kernel's results
-    __syncthreads();
-    for (int t = warp; t < T; t += 32) {
+    pdl_wait();                      // the logits kernel's results (and its zeroed cnt)
+    const int t = blockIdx.x * kSelectWarps + warp;
+    if (t < T) {
         const float *lr = logits + (size_t)t * E1;
         int j;
         float sc;
@@ -613,17 +621,30 @@ router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int
             if (escale) sc = bf16r(sc * escale[j]);
             inds[(size_t)t * k + lane] = j;
             scores[(size_t)t * k + lane] = sc;
-            s_pe[t * k + lane] = j;
-            s_rank[t * k + lane] = atomicAdd(&s_cnt[j], 1);
+            rank[(size_t)t * k + lane] = atomicAdd(&cnt[j], 1);
         }
         if (lane == 0 && has_shared) sgate[t] = bf16r(sigmoid_f32(lr[E]));
     }
     __syncthreads();
-    // exclusive scans of counts and of (count > 0), E <= 1024
-    const int e = tid;
-    const int c = e < E ? s_cnt[e] : 0;
-    const int a = c > 0;
-    int ic = c, ia = a;
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(reinterpret_cast<uint32_t *>(cnt + E), 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // exclusive scans of counts and of (count > 0): 4 experts per thread
+    const int P = T * k;
+    int c[4], a[4], sc_ = 0, sa = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int e = 4 * tid + q;
+        c[q] = e < E ? __ldcg(cnt + e) : 0;
+        a[q] = c[q] > 0;
+        sc_ += c[q];
+        sa += a[q];
+    }
+    int ic = sc_, ia = sa;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int u = __shfl_up_sync(0xffffffffu, ic, o);
@@ -634,40 +655,33 @@ router_select_kernel(const float *__restrict__ logits, int T, int E, int E1, int
         }
     }
     if (lane == 31) {
-        s_wsum[warp] = ic;
-        s_asum[warp] = ia;
+        s_wc[warp] = ic;
+        s_wa[warp] = ia;
     }
     __syncthreads();
-    if (warp == 0) {
-        const int wc = s_wsum[lane], wa = s_asum[lane];
-        int xc = wc, xa = wa;
+    int bc = 0, ba = 0;
+    for (int w2 = 0; w2 < warp; ++w2) {
+        bc += s_wc[w2];
+        ba += s_wa[w2];
+    }
+    int oc = bc + ic - sc_, oa = ba + ia - sa;   // exclusive prefix of this thread's first expert
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int u = __shfl_up_sync(0xffffffffu, xc, o);
-            const int v = __shfl_up_sync(0xffffffffu, xa, o);
-            if (lane >= o) {
-                xc += u;
-                xa += v;
+    for (int q = 0; q < 4; ++q) {
+        const int e = 4 * tid + q;
+        if (e < E) {
+            s_off[e] = oc;
+            off[e] = oc;
+            if (a[q]) active[oa] = e;
+            if (e == E - 1) {
+                off[E] = oc + c[q];
+                active[E] = oa + a[q];   // number of active experts
             }
         }
-        s_wsum[lane] = xc - wc;
-        s_asum[lane] = xa - wa;
+        oc += c[q];
+        oa += a[q];
     }
     __syncthreads();
-    if (e < E) {
-        const int oc = s_wsum[warp] + ic - c;
-        const int oa = s_asum[warp] + ia - a;
-        s_off[e] = oc;
-        cnt[e] = c;
-        off[e] = oc;
-        if (a) active[oa] = e;
-        if (e == E - 1) {
-            off[E] = oc + c;
-            active[E] = oa + a;
-        }
-    }
-    __syncthreads();
-    for (int p = tid; p < T * k; p += blockDim.x) list[s_off[s_pe[p]] + s_rank[p]] = p;
+    for (int p = tid; p < P; p += blockDim.x) list[s_off[__ldcg(inds + p)] + __ldcg(rank + p)] = p;
 }
 
 template <int EPL>
@@ -709,8 +723,11 @@ static vqmoe_status launch_topk(const float *logits, int T, int E, int E1, int k
     return check_launch("router_topk_kernel");
 }
 
+// zero2 (optional, nzero2 words): zeroed by the small-launch kernels (the
+// routing kernel's counters; only launches of up to kSelectMaxTok tokens pass it)
 vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t *wsg, int T, int H,
-                           int E, int E1, float *logits, uint16_t *x16, cudaStream_t stream) {
+                           int E, int E1, float *logits, uint16_t *x16, cudaStream_t stream,
+                           uint32_t *zero2 = nullptr, int nzero2 = 0) {
     size_t smem = (size_t)kRouterTok * H * sizeof(uint16_t);
     static int configured_smem[64] = {0};   // per device
     int dev = 0;
@@ -723,7 +740,7 @@ vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t 
         if (dev >= 0 && dev < 64) configured_smem[dev] = (int)smem;
     }
     vqmoe_status s;
-    if (H % 256 == 0 && T >= kBlkMinTok && E1 <= kBlkMaxNt * 8) {
+    if (H % 256 == 0 && T >= kBlkMinTok && E1 <= kBlkMaxNt * 8 && !zero2) {
         if (T >= 2 * kBlkMinTok)
             router_logits_dmma16_kernel<4><<<(T + 15) / 16, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
         else
@@ -732,11 +749,11 @@ vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t 
         s = check_launch("router_logits_dmma_blk_kernel");
     } else if (H % 256 == 0) {
         dim3 gt((E1 + 7) / 8, (T + 7) / 8);
-        router_logits_dmma_kernel<<<gt, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
+        router_logits_dmma_kernel<<<gt, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16, zero2, nzero2);
         s = check_launch("router_logits_dmma_kernel");
     } else {
         dim3 g1((E1 + kRouterRows - 1) / kRouterRows, (T + kRouterTok - 1) / kRouterTok);
-        router_logits_kernel<<<g1, 256, smem, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);
+        router_logits_kernel<<<g1, 256, smem, stream>>>(x, w, wsg, T, H, E, E1, logits, x16, zero2, nzero2);
         s = check_launch("router_logits_kernel");
     }
     return s;
@@ -760,36 +777,25 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
                                  int32_t *list, int32_t *active, int32_t *rank_scratch,
                                  uint32_t *zero, int zero_words, int mode, cudaStream_t stream) {
     const int E1 = E + (wsg ? 1 : 0);
-    const size_t smem_sel = (size_t)(2 * E + 2 * T * k) * sizeof(int32_t);
-    if (T > kSelectMaxTok || E > 1024 || smem_sel > 100 * 1024) {
+    if (T > kSelectMaxTok || E > 1024) {
         vqmoe_status s = launch_router(x, w, wsg, T, H, E, k, logits, inds, scores, sgate, x16, mode, nullptr,
                                        stream);
         if (s != VQMOE_OK) return s;
         return launch_route(inds, T * k, E, cnt, off, list, active, rank_scratch, zero, zero_words, stream);
     }
-    vqmoe_status s = launch_logits(x, w, wsg, T, H, E, E1, logits, x16, stream);
+    // cnt[0..E]: the select kernel's counters (cnt[E] counts finished CTAs)
+    vqmoe_status s = launch_logits(x, w, wsg, T, H, E, E1, logits, x16, stream,
+                                   reinterpret_cast<uint32_t *>(cnt), E + 1);
     if (s != VQMOE_OK) return s;
-    static size_t configured[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
     const int epl = (E + 31) / 32;
     auto fn = epl <= 1 ? router_select_kernel<1>
               : epl <= 2 ? router_select_kernel<2>
               : epl <= 4 ? router_select_kernel<4>
               : epl <= 8 ? router_select_kernel<8>
                          : router_select_kernel<16>;
-    if (smem_sel > 48 * 1024 && (dev < 0 || dev >= 64 || smem_sel > configured[dev])) {
-        if (cudaFuncSetAttribute(router_select_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess ||
-            cudaFuncSetAttribute(router_select_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess ||
-            cudaFuncSetAttribute(router_select_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess ||
-            cudaFuncSetAttribute(router_select_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess ||
-            cudaFuncSetAttribute(router_select_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess)
-            return set_error(VQMOE_LAUNCH_FAILED, "router_select: shared memory");
-        if (dev >= 0 && dev < 64) configured[dev] = 100 * 1024;
-    }
-    if (launch_pdl(fn, dim3(1), dim3(1024), smem_sel, stream, logits, T, E, E1, k, (int)(wsg != nullptr), inds,
-                   scores, sgate, cnt, off, list, active, zero, zero_words, mode,
-                   static_cast<const float *>(nullptr)) != cudaSuccess)
+    if (launch_pdl(fn, dim3((T + kSelectWarps - 1) / kSelectWarps), dim3(kSelectWarps * 32), 0, stream, logits, T,
+                   E, E1, k, (int)(wsg != nullptr), inds, scores, sgate, cnt, off, list, active, rank_scratch, zero,
+                   zero_words, mode, static_cast<const float *>(nullptr)) != cudaSuccess)
         return check_launch("router_select_kernel");
     return check_launch("router_select_kernel");
 }
