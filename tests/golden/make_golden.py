@@ -1,10 +1,9 @@
 """Writes `qwen3_5_moe_bf16_mlp.npz`: the reference's bf16 MoE-block golden
 with the exact weights and input it was computed on.
 
-Run in a container where the reference is mounted (default path below, or
-`--reference DIR`):
+Run in a container where the reference is mounted, naming its checkout:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 Sources (reference paths):
 * golden output: `tests/support/goldens/qwen_reference.npz`
@@ -35,7 +34,8 @@ OUT = HERE / "qwen3_5_moe_bf16_mlp.npz"
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="the reference checkout (its tests/support/goldens is read)")
     args = ap.parse_args(argv)
     gdir = Path(args.reference) / "tests" / "support" / "goldens"
     sys.path.insert(0, str(gdir))
