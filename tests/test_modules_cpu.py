@@ -49,6 +49,49 @@ def test_modules_refuse_cpu_tensors():
         glu(torch.zeros(3, 128, dtype=torch.bfloat16), idx)
 
 
+def test_gemma4_modules_check_their_arguments():
+    """Gemma-4's Router and Experts (gemma4_text.py:156-214): shapes and the
+    GeGLU activation are checked at construction; CPU tensors are refused."""
+    from knurlogic_b200 import GeGLU
+    from knurlogic_b200.gemma4 import Experts, Router
+    E, H = 8, 128
+    proj = torch.zeros(E, H)
+    with pytest.raises(ValueError, match="per_expert_scale"):
+        Router(proj, torch.ones(H), torch.ones(E + 1), 2)
+    with pytest.raises(ValueError, match="top_k_experts"):
+        Router(proj, torch.ones(H), torch.ones(E), E + 1)
+    r = Router(proj, torch.ones(H), torch.ones(E), 2)
+    assert r.per_expert_scale.dtype == torch.float32 and r.proj.weight.dtype == torch.bfloat16
+    with pytest.raises(RuntimeError, match="CUDA"):
+        r(torch.zeros(3, H, dtype=torch.bfloat16))
+    lins = [SwitchLinear(torch.zeros(E, 16, H)), SwitchLinear(torch.zeros(E, 16, H)),
+            SwitchLinear(torch.zeros(E, H, 16))]
+    with pytest.raises(ValueError, match="GeGLU"):
+        Experts(SwitchGLU(*lins))
+    ex = Experts(SwitchGLU(*lins, activation=GeGLU()))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ex(torch.zeros(3, H, dtype=torch.bfloat16), torch.zeros(3, 2, dtype=torch.int32), torch.ones(3, 2))
+
+
+def test_gemma4_router_norm_matches_the_oracle():
+    """The router's RMS norm (torch ops, the one step outside the kernels)
+    against the oracle's restatement of it."""
+    import numpy as np
+    from knurlogic_b200.gemma4 import Router
+    from oracle import moe_ref as R
+    g = np.random.default_rng(0)
+    H = 256
+    x = torch.from_numpy(R.bf16(g.normal(0, 2, (8, H)).astype(np.float32))).to(torch.bfloat16)
+    scale = torch.from_numpy(g.uniform(0.5, 1.5, H).astype(np.float32))
+    r = Router(torch.zeros(4, H), scale, torch.ones(4), 2)
+    ours = r.normalize(x).float().numpy()
+    w = R.bf16(R.bf16(scale.numpy()) * np.float32(H ** -0.5))
+    ref = R.rms_norm(x.float().numpy(), w, r.eps)
+    # float32 rsqrt against numpy's 1/sqrt: a rare bf16 tie may land apart
+    assert (ours != ref).mean() < 1e-2
+    assert np.all(np.abs(ours - ref) <= np.abs(ref) * 2.0 ** -7)
+
+
 def test_block_reads_the_reference_state_dict_names():
     cfg = synth.CONFIGS["c1"]
     w = synth.make_weights(cfg, seed=0)
