@@ -46,8 +46,10 @@ extern "C" {
 #endif
 
 /* 2: vqmoe_linear.activation (was reserved), vqmoe_block.router_mode and
- * its trailing reserved word, vqmoe_router_ex, vqmoe_moe_experts. */
-#define VQMOE_ABI_VERSION 2
+ * its trailing reserved word, vqmoe_router_ex, vqmoe_moe_experts.
+ * 3: vqmoe_block.wait_polls (was reserved), vqmoe_workspace_status; every
+ * workspace starts with VQMOE_STATUS_BYTES of status words. */
+#define VQMOE_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define VQMOE_API __attribute__((visibility("default")))
@@ -63,7 +65,7 @@ typedef enum {
     VQMOE_WORKSPACE_TOO_SMALL = 4,
     VQMOE_BAD_CODE = 5,          /* a VQ code >= codebook size */
     VQMOE_LAUNCH_FAILED = 6,     /* a CUDA launch or call returned an error */
-    VQMOE_TIMEOUT = 7,           /* reserved: a bounded device wait ran out */
+    VQMOE_TIMEOUT = 7,           /* a bounded device wait ran out (vqmoe_workspace_status) */
     VQMOE_NOT_SUPPORTED = 8
 } vqmoe_status;
 
@@ -136,7 +138,9 @@ typedef struct {
     const void *shared_down_w;   /* mlp.shared_expert.down_proj [H, I_s] bf16 */
     const void *shared_expert_gate_w; /* mlp.shared_expert_gate [1, H] bf16 */
     int32_t router_mode;         /* VQMOE_ROUTER_* (0: Qwen3.5) */
-    int32_t reserved;            /* 0 */
+    int32_t wait_polls;          /* polls before a phase 2 tile gives up waiting
+                                    for its expert's phase 1 tiles; 0: the
+                                    default (about four seconds) */
 } vqmoe_block;
 
 /* Output dtype of vqmoe_sparse_moe_block. F32 holds the bf16 block output
@@ -172,7 +176,9 @@ VQMOE_API vqmoe_status vqmoe_sparse_moe_block(const vqmoe_block *blk, const void
  * (cudaEvent_t, passed as void*) on `stream`: before the router, then after
  * the router and routing sort, the routed experts (gate/up + SwiGLU and
  * down, one launch), the join of the shared expert's side stream, and the
- * combine. For profiling; tokens <= 2048. */
+ * combine. A sixth event, when n_events >= 6, is recorded between the
+ * prefill path's input permute and its grouped GEMM (right after the
+ * routing on the decode path). For profiling; tokens <= 2048. */
 VQMOE_API vqmoe_status vqmoe_sparse_moe_block_timed(
     const vqmoe_block *blk, const void *x, int32_t tokens, void *out,
     int32_t out_dtype, void *workspace, size_t workspace_bytes, void *stream,
@@ -297,6 +303,21 @@ VQMOE_API vqmoe_status vqmoe_count_bad_codes(const uint8_t *codes,
                                              int32_t codebook_size,
                                              uint32_t *bad_count,
                                              void *stream);
+
+/* Every workspace (of vqmoe_sparse_moe_block, vqmoe_switch_glu,
+ * vqmoe_switch_linear, vqmoe_moe_experts) starts with this many bytes of
+ * status words, cleared at the start of each call on its stream. */
+#define VQMOE_STATUS_BYTES 256
+
+/* The device-side status of the last call that used `workspace`: waits for
+ * `stream` (host synchronisation), then returns VQMOE_TIMEOUT when one of
+ * the call's bounded device waits ran out (its outputs are then wrong; the
+ * message names the stage and the wait), else VQMOE_OK. Every device wait is
+ * bounded, so a kernel never hangs on one: the Knurlogic runtime treats a
+ * stalled peer as an event (src/knurlogic/engine/split/liveness.py), and this
+ * is the event's device-side form. Read it between calls; the next call
+ * clears it. */
+VQMOE_API vqmoe_status vqmoe_workspace_status(const void *workspace, void *stream);
 
 /* Message of the last non-OK status returned on this host thread. */
 VQMOE_API const char *vqmoe_last_error(void);

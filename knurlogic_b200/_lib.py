@@ -47,12 +47,13 @@ class Block(Structure):
                 ("down", Linear), ("shared_gate_w", c_void_p),
                 ("shared_up_w", c_void_p), ("shared_down_w", c_void_p),
                 ("shared_expert_gate_w", c_void_p),
-                ("router_mode", c_int32), ("reserved", c_int32)]
+                ("router_mode", c_int32), ("wait_polls", c_int32)]
 
 
 #: every symbol include/vqmoe.h declares: (name, restype, argtypes)
 SIGNATURES = [
     ("vqmoe_abi_version", c_int32, []),
+    ("vqmoe_workspace_status", c_int32, [c_void_p, c_void_p]),
     ("vqmoe_last_error", c_char_p, []),
     ("vqmoe_block_workspace_size", c_size_t, [POINTER(Block), c_int32]),
     ("vqmoe_switch_glu_workspace_size", c_size_t,

@@ -9,9 +9,12 @@
 //   shared expert down (dense)                 -> sh   [T, H]
 //   combine: bf16(sum_k ybuf) + bf16(sg * sh)  -> out  [T, H]
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 
 #include "stages.cuh"
 
@@ -35,15 +38,35 @@ vqmoe_status check_launch(const char *what) {
 }
 
 int sm_count() {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+    if (dev >= 0 && dev < 64) {
+        const int c = cached[dev].load(std::memory_order_relaxed);
+        if (c) return c;
+    }
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (n <= 0) n = 148;
-    if (dev >= 0 && dev < 64) cached[dev] = n;
+    if (dev >= 0 && dev < 64) cached[dev].store(n, std::memory_order_relaxed);
     return n;
+}
+
+vqmoe_status ensure_dynamic_smem(const void *fn, size_t bytes, const char *what) {
+    if (bytes <= 48 * 1024) return VQMOE_OK;
+    static std::mutex mu;
+    static std::map<std::pair<const void *, int>, size_t> done;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return check_launch(what);
+    std::lock_guard<std::mutex> lock(mu);
+    size_t &have = done[{fn, dev}];
+    if (have >= bytes) return VQMOE_OK;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(VQMOE_LAUNCH_FAILED, "%s: %zu bytes of shared memory", what, bytes);
+    }
+    have = bytes;
+    return VQMOE_OK;
 }
 
 // ------------------------------------------------------------- combine
@@ -192,6 +215,7 @@ static void carve_route(Carve &c, RouteWs &w, int E, int P, int H, int T, int Is
 }
 
 struct BlockWs {
+    uint32_t *status;    // kStatusBytes at offset 0: [0] routed experts, [1] shared expert
     float *logits;
     int32_t *inds;
     float *scores;
@@ -212,6 +236,7 @@ static BlockWs carve_block(void *ws, const vqmoe_block *b, int T) {
     const int E = b->num_experts, k = b->top_k, H = b->hidden;
     const int I = b->gate.out_features, Is = std::max(b->shared_inter, 0);
     const int P = T * k;
+    w.status = c.take<uint32_t>(kStatusBytes / sizeof(uint32_t));
     w.logits = c.take<float>((size_t)T * (E + 1));
     w.inds = c.take<int32_t>(P);
     w.scores = c.take<float>(P);
@@ -226,6 +251,14 @@ static BlockWs carve_block(void *ws, const vqmoe_block *b, int T) {
     w.xs = prefill_regime(vq, E, P) ? c.take<uint16_t>((size_t)P * H) : nullptr;
     w.bytes = align_up(c.off, 256);
     return w;
+}
+
+// The status words of a call start at zero (before the shared expert's side
+// stream forks, so both streams see it); they stay set across the token
+// chunks of the call.
+static vqmoe_status clear_status(uint32_t *status, cudaStream_t st) {
+    if (cudaMemsetAsync(status, 0, 2 * sizeof(uint32_t), st) != cudaSuccess) return check_launch("status words");
+    return VQMOE_OK;
 }
 
 // Tokens per launch sequence; a larger T runs as independent token chunks
@@ -246,6 +279,7 @@ static vqmoe_status check_block(const vqmoe_block *b, int T) {
     if (H <= 0 || H % 16) return set_error(VQMOE_BAD_SHAPE, "hidden %d is not a multiple of 16", H);
     if (E <= 0 || E > 512) return set_error(VQMOE_BAD_SHAPE, "num_experts %d (1..512)", E);
     if (k <= 0 || k > 32 || k > E) return set_error(VQMOE_BAD_SHAPE, "top_k %d (1..min(32, E))", k);
+    if (b->wait_polls < 0) return set_error(VQMOE_BAD_SHAPE, "wait_polls %d (>= 0)", b->wait_polls);
     vqmoe_status s;
     if ((s = check_linear(&b->gate, "gate_proj")) != VQMOE_OK) return s;
     if ((s = check_linear(&b->up, "up_proj")) != VQMOE_OK) return s;
@@ -272,10 +306,10 @@ static vqmoe_status check_block(const vqmoe_block *b, int T) {
     return VQMOE_OK;
 }
 
-// events (optional, n_ev >= 6): recorded before the router, after the
-// routing, after the gate/up stage (routed + shared), after the down stage,
-// again after the down stage (the shared expert runs inside both stages),
-// and after the combine.
+// events (optional, n_ev >= 5): recorded before the router, after the
+// routing, after the routed experts, after the join of the shared expert's
+// side stream, and after the combine; a sixth, when given, after the
+// prefill path's input permute (with the routing's when there is none).
 static vqmoe_status mark(cudaEvent_t *ev, int n_ev, int i, cudaStream_t st) {
     if (ev && i < n_ev && cudaEventRecord(ev[i], st) != cudaSuccess)
         return set_error(VQMOE_LAUNCH_FAILED, "event %d", i);
@@ -339,10 +373,10 @@ static vqmoe_status run_shared(const vqmoe_block *b, const uint16_t *x, int T, c
     const RouteWs &rt = w.rt;
     if (T >= kDensePrefillTokens && b->hidden % 64 == 0 && b->shared_inter % 64 == 0) {
         vqmoe_status s = launch_dense_prefill(x, b->shared_gate_w, b->shared_up_w, T, b->hidden,
-                                              b->shared_inter, w.act_s, rt.zero + 1, st);
+                                              b->shared_inter, w.act_s, w.status + 1, st);
         if (s != VQMOE_OK) return s;
         return launch_dense_prefill(w.act_s, b->shared_down_w, nullptr, T, b->shared_inter, b->hidden,
-                                    w.sh, rt.zero + 1, st);
+                                    w.sh, w.status + 1, st);
     }
     if (rt.szero_words &&
         cudaMemsetAsync(rt.szero, 0, (size_t)rt.szero_words * sizeof(uint32_t), st) != cudaSuccess)
@@ -385,7 +419,8 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
     r1.xs = w.xs;
     r1.act = b->gate.activation;
     RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores);
-    s = launch_experts(&b->gate, &b->up, &r1, &b->down, r2, rt.zero, st);
+    s = launch_experts(&b->gate, &b->up, &r1, &b->down, r2, rt.zero, w.status, (uint32_t)b->wait_polls, st,
+                       ev && n_ev > 5 ? ev[5] : nullptr);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK) return s;
     if (shared && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
         return check_launch("side stream join");
@@ -399,6 +434,7 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
 
 // Workspace of vqmoe_switch_glu / vqmoe_switch_linear at T tokens.
 struct GluWs {
+    uint32_t *status;    // kStatusBytes at offset 0: [0] routed experts
     uint16_t *x16;
     RouteWs rt;
     uint16_t *act;
@@ -412,6 +448,7 @@ static GluWs carve_glu(void *ws, const vqmoe_linear *first, const vqmoe_linear *
     GluWs w{};
     const int E = first->num_experts, P = T * k;
     const bool dual = down != nullptr;
+    w.status = c.take<uint32_t>(kStatusBytes / sizeof(uint32_t));
     w.x16 = first->format == VQMOE_FMT_VQ_U8 ? c.take<uint16_t>((size_t)rows_x * first->in_features)
                                              : nullptr;
     const int H = first->in_features, I = first->out_features;
@@ -453,6 +490,23 @@ extern "C" {
 
 int32_t vqmoe_abi_version(void) { return VQMOE_ABI_VERSION; }
 
+vqmoe_status vqmoe_workspace_status(const void *workspace, void *stream) {
+    if (!aligned_ptr(workspace)) return set_error(VQMOE_BAD_POINTER, "workspace_status: workspace");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint32_t w[2] = {0, 0};
+    if (cudaMemcpyAsync(w, workspace, sizeof(w), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return check_launch("workspace_status");
+    if (!w[0] && !w[1]) return VQMOE_OK;
+    auto kind = [](uint32_t v) {
+        return v == kWaitDependency ? "a phase 2 tile's wait for its expert's phase 1 tiles"
+               : v == kWaitPipeline ? "a tcgen05 pipeline barrier"
+                                    : "none";
+    };
+    return set_error(VQMOE_TIMEOUT, "a bounded device wait ran out: routed experts: %s; shared expert: %s",
+                     kind(w[0]), kind(w[1]));
+}
+
 const char *vqmoe_last_error(void) { return g_err; }
 
 size_t vqmoe_router_workspace_size(int32_t tokens, int32_t num_experts) {
@@ -492,6 +546,7 @@ static vqmoe_status block_impl(const vqmoe_block *blk, const void *x, int32_t to
     if (workspace_bytes < w.bytes)
         return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, w.bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((s = clear_status(w.status, st)) != VQMOE_OK) return s;
     const size_t osz = out_dtype == VQMOE_OUT_F32 ? 4 : 2;
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
         const int T = std::min(chunk, tokens - t0);
@@ -546,6 +601,7 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
     if (workspace_bytes < w.bytes)
         return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, w.bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((s = clear_status(w.status, st)) != VQMOE_OK) return s;
     const bool vq_in = gate->format == VQMOE_FMT_VQ_U8, vq_dn = down->format == VQMOE_FMT_VQ_U8;
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
         const int T = std::min(chunk, tokens - t0), P = T * top_k;
@@ -562,7 +618,7 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
         r1.act = gate->activation;
         RoutedIO r2 = routed_io(rt, E, top_k, P, w.act, 1,
                                 static_cast<uint16_t *>(y) + (size_t)t0 * top_k * H, 0, nullptr);
-        if ((s = launch_experts(gate, up, &r1, down, r2, rt.zero, st)) != VQMOE_OK) return s;
+        if ((s = launch_experts(gate, up, &r1, down, r2, rt.zero, w.status, 0, st)) != VQMOE_OK) return s;
     }
     return VQMOE_OK;
 }
@@ -606,6 +662,7 @@ vqmoe_status vqmoe_moe_experts(const vqmoe_linear *gate, const vqmoe_linear *up,
         return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, need);
     uint16_t *ybuf = reinterpret_cast<uint16_t *>(static_cast<char *>(workspace) + moe_experts_ybuf_offset(w));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((s = clear_status(w.status, st)) != VQMOE_OK) return s;
     const bool vq_in = gate->format == VQMOE_FMT_VQ_U8, vq_dn = down->format == VQMOE_FMT_VQ_U8;
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
         const int T = std::min(chunk, tokens - t0), P = T * top_k;
@@ -621,7 +678,7 @@ vqmoe_status vqmoe_moe_experts(const vqmoe_linear *gate, const vqmoe_linear *up,
         r1.xs = w.xs;
         r1.act = gate->activation;
         RoutedIO r2 = routed_io(rt, E, top_k, P, w.act, 1, ybuf, 0, scores + (size_t)t0 * top_k);
-        if ((s = launch_experts(gate, up, &r1, down, r2, rt.zero, st)) != VQMOE_OK) return s;
+        if ((s = launch_experts(gate, up, &r1, down, r2, rt.zero, w.status, 0, st)) != VQMOE_OK) return s;
         const size_t nvec = (size_t)T * (H / 8);
         const int grid = (int)std::min<size_t>((nvec + 255) / 256, (size_t)sm_count() * 8);
         combine_kernel<<<grid, 256, 0, st>>>(ybuf, T, top_k, H, nullptr, nullptr,
@@ -646,6 +703,7 @@ vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x
     if (workspace_bytes < ws.bytes)
         return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, ws.bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((s = clear_status(ws.status, st)) != VQMOE_OK) return s;
     const bool vq = w->format == VQMOE_FMT_VQ_U8;
     const int IN = w->in_features, E = w->num_experts;
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
@@ -662,7 +720,7 @@ vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x
                                x_per_pair, static_cast<uint16_t *>(y) + (size_t)t0 * top_k * w->out_features,
                                0, nullptr);
         r.xs = ws.xs;
-        if ((s = launch_experts(nullptr, nullptr, nullptr, w, r, rt.zero, st)) != VQMOE_OK) return s;
+        if ((s = launch_experts(nullptr, nullptr, nullptr, w, r, rt.zero, ws.status, 0, st)) != VQMOE_OK) return s;
     }
     return VQMOE_OK;
 }

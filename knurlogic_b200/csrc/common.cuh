@@ -183,6 +183,17 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0,
 vqmoe_status set_error(vqmoe_status s, const char *fmt, ...);
 vqmoe_status check_launch(const char *what);
 int sm_count();
+// Raises kernel `fn`'s dynamic shared-memory limit on the current device to
+// at least `bytes`, once per (kernel, device); safe from several host threads.
+vqmoe_status ensure_dynamic_smem(const void *fn, size_t bytes, const char *what);
+
+// Status words at the head of every caller workspace (and of the fixed
+// scratch): [0] the routed-expert kernels' bounded waits, [1] the shared
+// expert's (side stream). Zeroed at the start of each call; a kernel whose
+// wait runs out stores its kind (kWaitDependency, kWaitPipeline) there.
+constexpr size_t kStatusBytes = 256;
+constexpr uint32_t kWaitDependency = 1;   // a phase 2 tile's wait for its expert's phase 1 tiles
+constexpr uint32_t kWaitPipeline = 2;     // an mbarrier wait inside a tcgen05 pipeline
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 inline bool aligned16(const void *p) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;

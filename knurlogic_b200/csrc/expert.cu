@@ -186,16 +186,19 @@ __device__ __forceinline__ void stage_codebooks(uint8_t *cb, const LinearDev &w0
     }
 }
 
-// Thread 0: wait until *count >= want (acquire), at most kWaitLimit polls
-// with a growing sleep; on running out, raise the error flag and go on.
-__device__ __noinline__ void wait_count(const uint32_t *count, uint32_t want, uint32_t *err) {
+// Thread 0: wait until *count >= want (acquire), at most `limit` polls
+// (kWaitLimit when 0) with a growing sleep; on running out, store
+// kWaitDependency in the call's status word and go on (the tile's results
+// are then wrong, and the call reports VQMOE_TIMEOUT, but nothing hangs).
+__device__ __noinline__ void wait_count(const uint32_t *count, uint32_t want, uint32_t *err, uint32_t limit) {
+    const long polls = limit ? (long)limit : kWaitLimit;
     unsigned ns = 64;
-    for (long i = 0;; ++i) {
+    for (long i = 1;; ++i) {
         uint32_t v;
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(count) : "memory");
         if (v >= want) return;
-        if (i >= kWaitLimit) {
-            atomicExch(err, 1u);
+        if (i >= polls) {
+            atomicExch(err, kWaitDependency);
             return;
         }
         __nanosleep(ns);
@@ -397,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 2) expert_kernel(const PipeArgs a) {
             const TileInfo in = tile_info(a.s2, tile, n1, rt1, rt2);
             // phase 2 reads what every phase 1 tile of this expert wrote;
             // those tiles were all taken before this one, by running CTAs
-            if (a.has1) wait_count(a.ctl + 2 + in.ai, (uint32_t)rt1, a.ctl + 1);
+            if (a.has1) wait_count(a.ctl + 2 + in.ai, (uint32_t)rt1, a.err, a.wait_polls);
             s_info = in;
             s_next = (int)atomicAdd(a.ctl, 1u);
         }
@@ -560,15 +563,9 @@ vqmoe_status launch_shared_dense(const void *x, const void *w0, const void *w1, 
     a.part = part;
     a.sem = sem;
     dim3 grid((OUT + kShRows - 1) / kShRows, ks);
-    static size_t configured[2][64] = {{0}};
-    int dev = 0;
-    cudaGetDevice(&dev);
     auto fn = nmat == 2 ? shared_dense_kernel<2> : shared_dense_kernel<1>;
-    if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || smem > configured[nmat - 1][dev])) {
-        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return set_error(VQMOE_LAUNCH_FAILED, "shared expert kernel: %zu bytes of shared memory", smem);
-        if (dev >= 0 && dev < 64) configured[nmat - 1][dev] = smem;
-    }
+    vqmoe_status s = ensure_dynamic_smem(reinterpret_cast<const void *>(fn), smem, "shared expert kernel");
+    if (s != VQMOE_OK) return s;
     fn<<<grid, 256, smem, stream>>>(a);
     return check_launch("shared_dense_kernel");
 }
@@ -577,16 +574,9 @@ vqmoe_status launch_shared_dense(const void *x, const void *w0, const void *w1, 
 
 template <bool VQ1, bool VQ2>
 static vqmoe_status launch_pipe(const PipeArgs &a, size_t smem, cudaStream_t stream) {
-    static size_t configured[64] = {0};   // per device
-    int dev = 0;
-    cudaGetDevice(&dev);
     auto fn = expert_kernel<VQ1, VQ2>;
-    if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || smem > configured[dev])) {
-        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-            return set_error(VQMOE_LAUNCH_FAILED, "expert kernel: %zu bytes of shared memory", smem);
-        if (dev >= 0 && dev < 64) configured[dev] = smem;
-    }
+    vqmoe_status s = ensure_dynamic_smem(reinterpret_cast<const void *>(fn), smem, "expert kernel");
+    if (s != VQMOE_OK) return s;
     if (launch_pdl(fn, dim3(2 * sm_count()), dim3(kThreads), smem, stream, a) != cudaSuccess)
         return check_launch("expert_kernel");
     return check_launch("expert_kernel");
@@ -625,10 +615,12 @@ static RoutedSet set_of(const RoutedIO &r, const vqmoe_linear *w0, const vqmoe_l
 }
 
 vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,
-                            const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl,
-                            cudaStream_t stream) {
+                            const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl, uint32_t *err,
+                            uint32_t wait_polls, cudaStream_t stream, cudaEvent_t after_permute) {
     PipeArgs a{};
     a.ctl = ctl;
+    a.err = err;
+    a.wait_polls = wait_polls;
     a.has1 = r1 != nullptr;
     a.s2 = set_of(r2, w2, nullptr);
     a.s1 = r1 ? set_of(*r1, gate, up) : a.s2;
@@ -636,7 +628,8 @@ vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, co
     const bool vq1 = r1 ? gate->format == VQMOE_FMT_VQ_U8 : vq2;
     // many pairs per expert (prefill): the tcgen05 grouped GEMM
     void *xs = r1 ? r1->xs : r2.xs;
-    if (prefill_regime(vq1 && vq2, r2.E, r2.P) && xs) return launch_experts_prefill(a, xs, stream);
+    if (prefill_regime(vq1 && vq2, r2.E, r2.P) && xs) return launch_experts_prefill(a, xs, stream, after_permute);
+    if (after_permute && cudaEventRecord(after_permute, stream) != cudaSuccess) return check_launch("event");
     const size_t smem = (vq1 || vq2 ? (size_t)kRepBytes : 0) + (size_t)kXBytes;
     if (vq1) return vq2 ? launch_pipe<true, true>(a, smem, stream) : launch_pipe<true, false>(a, smem, stream);
     return vq2 ? launch_pipe<false, true>(a, smem, stream) : launch_pipe<false, false>(a, smem, stream);

@@ -256,12 +256,12 @@ __device__ __forceinline__ void tma_role(const PipeArgs &a, Shared &sh, const vo
             // they were all taken before this one, by running CTAs
             const uint32_t want = (uint32_t)(((a.s2.cnt[cur.e] + kN - 1) / kN) * rt1);
             const uint32_t *c = a.ctl + 2 + cur.ai;
-            for (long i = 0;; ++i) {
+            for (long i = 1;; ++i) {
                 uint32_t val;
                 asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(val) : "l"(c) : "memory");
                 if (val >= want) break;
-                if (i >= kSpin) {
-                    atomicExch(err, 1u);
+                if (i >= (a.wait_polls ? (long)a.wait_polls : kSpin)) {
+                    atomicExch(err, kWaitDependency);
                     break;
                 }
                 __nanosleep(256);
@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    uint32_t *err = a.ctl + 1;
+    uint32_t *err = a.err;
     const int nact = min(a.s2.active[a.s2.E], kMaxE);
     const int rt1 = a.has1 ? (a.s1.OUT + 127) / 128 : 0;
     const int rt2 = (a.s2.OUT + 255) / 256;     // phase 2 tiles: 256 rows
@@ -640,16 +640,11 @@ __global__ void permute_rows_kernel(const uint16_t *__restrict__ x, int x_per_pa
 
 }  // namespace pf
 
-vqmoe_status launch_experts_prefill(const PipeArgs &args, void *xs, cudaStream_t stream) {
-    static bool configured[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        if (cudaFuncSetAttribute(pf::expert_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)pf::kSmem) != cudaSuccess)
-            return set_error(VQMOE_LAUNCH_FAILED, "prefill expert kernel: %zu bytes of shared memory",
-                             pf::kSmem);
-        if (dev >= 0 && dev < 64) configured[dev] = true;
+vqmoe_status launch_experts_prefill(const PipeArgs &args, void *xs, cudaStream_t stream, cudaEvent_t after_permute) {
+    {
+        vqmoe_status s = ensure_dynamic_smem(reinterpret_cast<const void *>(pf::expert_prefill_kernel), pf::kSmem,
+                                             "prefill expert kernel");
+        if (s != VQMOE_OK) return s;
     }
     PipeArgs a = args;
     const RoutedSet &first = a.has1 ? a.s1 : a.s2;
@@ -662,6 +657,7 @@ vqmoe_status launch_experts_prefill(const PipeArgs &args, void *xs, cudaStream_t
                                                           xs16);
         vqmoe_status s = check_launch("permute_rows_kernel");
         if (s != VQMOE_OK) return s;
+        if (after_permute && cudaEventRecord(after_permute, stream) != cudaSuccess) return check_launch("event");
     }
     CUtensorMap map1, map2;
     if (!make_tma_map(&map1, xs16, P, IN, pf::kN))

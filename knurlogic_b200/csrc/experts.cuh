@@ -31,9 +31,11 @@ struct PipeArgs {
     RoutedSet s1;                // phase 1: fused gate/up (when has1)
     RoutedSet s2;                // phase 2: down, or the one switch linear
     int has1;
-    // [0] tile counter, [1] error flag (a wait ran out), [2 + i] finished
-    // phase 1 tiles of active expert i; zeroed by the routing kernel
+    // [0] tile counter, [1] unused, [2 + i] finished phase 1 tiles of
+    // active expert i; zeroed by the routing kernel
     uint32_t *ctl;
+    uint32_t *err;               // the call's status word (kWait* when a wait ran out)
+    uint32_t wait_polls;         // polls of a phase 2 tile's dependency wait (0: the default)
 };
 
 template <bool DUAL>
@@ -79,6 +81,7 @@ struct TileInfo {
 // The prefill path (tcgen05): both stages of the routed VQ experts in one
 // launch, for layers whose experts see many tokens each.
 // xs: [P][IN of the first stage] fp16 scratch for the expert-ordered inputs.
-vqmoe_status launch_experts_prefill(const PipeArgs &a, void *xs, cudaStream_t stream);
+vqmoe_status launch_experts_prefill(const PipeArgs &a, void *xs, cudaStream_t stream,
+                                    cudaEvent_t after_permute = nullptr);
 
 }  // namespace vqmoe

@@ -729,17 +729,8 @@ vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t 
                            int E, int E1, float *logits, uint16_t *x16, cudaStream_t stream,
                            uint32_t *zero2 = nullptr, int nzero2 = 0) {
     size_t smem = (size_t)kRouterTok * H * sizeof(uint16_t);
-    static int configured_smem[64] = {0};   // per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || (int)smem > configured_smem[dev])) {
-        if (cudaFuncSetAttribute(router_logits_kernel,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem) != cudaSuccess)
-            return set_error(VQMOE_LAUNCH_FAILED, "router: smem %zu", smem);
-        if (dev >= 0 && dev < 64) configured_smem[dev] = (int)smem;
-    }
-    vqmoe_status s;
+    vqmoe_status s = ensure_dynamic_smem(reinterpret_cast<const void *>(router_logits_kernel), smem, "router");
+    if (s != VQMOE_OK) return s;
     if (H % 256 == 0 && T >= kBlkMinTok && E1 <= kBlkMaxNt * 8 && !zero2) {
         if (T >= 2 * kBlkMinTok)
             router_logits_dmma16_kernel<4><<<(T + 15) / 16, 256, 0, stream>>>(x, w, wsg, T, H, E, E1, logits, x16);

@@ -37,15 +37,19 @@ struct RoutedIO {
 // at least 32 pairs per expert on average; it needs the xs scratch.
 inline bool prefill_regime(bool vq, int E, int P) { return vq && E <= 512 && (long long)P >= 32LL * E; }
 
-// Words of the expert kernel's control block: tile counter, error flag, and
-// one finished-tile count per expert. Zeroed by the routing kernel.
+// Words of the expert kernel's control block: tile counter, an unused word,
+// and one finished-tile count per expert. Zeroed by the routing kernel.
 inline int expert_ctl_words(int E) { return 2 + E; }
 
 // The routed experts of a layer in one launch: phase 1 = gate/up + SwiGLU
 // (r1, may be null), then phase 2 = w2 (down, or the only linear) on r2.
+// err: the call's status word; wait_polls: the phase 2 dependency wait's
+// poll limit (0: the default, about four seconds); after_permute (optional):
+// an event recorded once the prefill path's inputs are in expert order
+// (right away on the decode path).
 vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,
-                            const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl,
-                            cudaStream_t stream);
+                            const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl, uint32_t *err,
+                            uint32_t wait_polls, cudaStream_t stream, cudaEvent_t after_permute = nullptr);
 // The shared expert's dense matmul (+ SwiGLU when w1 is set): K slicing,
 // its partial buffer [ks][T][nmat][OUT] float and [ceil(OUT/32)] semaphores.
 void plan_shared_dense(int IN, int OUT, int nmat, int *ks, int *kslice, size_t *smem);

@@ -47,7 +47,7 @@ __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, uint32
         if (done) return;
     }
     failed = true;
-    atomicExch(err, 2u);
+    atomicExch(err, kWaitPipeline);
 }
 // mbar_wait by lane 0 of the warp, the other lanes held at __syncwarp
 __device__ __forceinline__ void warp_wait(uint64_t *bar, uint32_t parity, uint32_t *err, bool &failed) {

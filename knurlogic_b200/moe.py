@@ -86,6 +86,9 @@ class SparseMoeBlock(nn.Module):
         self.shared_expert_gate = (_bf16_linear(shared_expert_gate_weight)
                                    if shared_expert_gate_weight is not None else None)
         self.sharding_group = sharding_group
+        # polls before a phase 2 tile gives up waiting for its expert's
+        # phase 1 tiles (0: the library default, about four seconds)
+        self.wait_polls = 0
         sm = switch_mlp
         for name, mod, shape in (("gate_proj", sm.gate_proj, None),
                                  ("up_proj", sm.up_proj, None),
@@ -107,6 +110,7 @@ class SparseMoeBlock(nn.Module):
         b.gate, b.up, b.down = (sm.gate_descriptor(), sm.up_proj.descriptor(),
                                 sm.down_proj.descriptor())
         b.router_mode = self.router_mode
+        b.wait_polls = self.wait_polls
         if self.shared_expert is not None:
             se = self.shared_expert
             b.shared_inter = se.gate_proj.weight.shape[0]
@@ -126,6 +130,14 @@ class SparseMoeBlock(nn.Module):
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
             self._ws = torch.empty(need, dtype=torch.uint8, device=device)
         return self._ws
+
+    def check_status(self, device=None) -> None:
+        """Raise `_lib.VQMoEError` (status TIMEOUT) when one of the last
+        call's bounded device waits ran out -- its output is then wrong.
+        Synchronises the current stream (`vqmoe_workspace_status`)."""
+        if self._ws is None:
+            return
+        _lib.call("vqmoe_workspace_status", self._ws.data_ptr(), c_stream(device or self._ws.device))
 
     def forward_into(self, x2d: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """The block on contiguous [T, H] bf16 into `out` ([T, H] bf16 or
@@ -235,6 +247,10 @@ class CapturedBlock:
             self.block.forward_into(self.x, self.part)
             dist.all_reduce(self.part, op=dist.ReduceOp.SUM, group=self.block.sharding_group)
             self.y.copy_(self.part)
+
+    def check_status(self) -> None:
+        """The last replay's device-side status (`SparseMoeBlock.check_status`)."""
+        self.block.check_status(self.x.device)
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None):
         self.x.copy_(x, non_blocking=True)

@@ -32,10 +32,10 @@ def test_every_declared_symbol_is_exported(so):
 
 
 def test_abi_version_and_struct_layout(so):
-    assert so.vqmoe_abi_version() == 2
+    assert so.vqmoe_abi_version() == 3
     # vqmoe_linear: 4 int32, 4 pointers, 4 int32 (the last: the activation)
     assert ctypes.sizeof(_lib.Linear) == 16 + 4 * 8 + 16
-    # vqmoe_block: ..., 4 shared pointers, router_mode, reserved
+    # vqmoe_block: ..., 4 shared pointers, router_mode, wait_polls
     assert ctypes.sizeof(_lib.Block) == 16 + 8 + 3 * ctypes.sizeof(_lib.Linear) + 4 * 8 + 8
 
 
@@ -75,3 +75,8 @@ def test_bad_arguments_return_a_status_not_a_crash(so):
     st = so.vqmoe_prepare_vq(None, None, 2, 32, 100, None, None, None)
     assert _lib.STATUS[st] == "BAD_SHAPE"          # IN not a multiple of 64
     assert _lib.vq_layout_bytes(2, 48, 320) == (2 * 2 * 2 * 2048, 2 * 2 * 2 * 128 * 2)
+    b = _block()
+    b.wait_polls = -1
+    st = so.vqmoe_sparse_moe_block(ctypes.byref(b), None, 64, None, 0, None, 0, None)
+    assert _lib.STATUS[st] == "BAD_SHAPE" and b"wait_polls" in so.vqmoe_last_error()
+    assert _lib.STATUS[so.vqmoe_workspace_status(None, None)] == "BAD_POINTER"
