@@ -1,7 +1,7 @@
 """Benchmark of the VQ-MoE expert layer on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1|c2|c3|c4]
+                    [--workload c1|c2|c3|c4] [--tp S]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N \
         --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
 
@@ -10,16 +10,18 @@ HBM GB/s as a fraction of the measured roofline.
 
 A step is one call of the Qwen3.5-MoE sparse block (router, fused VQ
 gate/up + SwiGLU, VQ down, shared expert, combine) over one batch of
-synthetic tokens, configuration c2 (H 2048, 128 experts top-8, I 768 +
-shared 768, 64 tokens = 16 sequences x (1 + 3 MTP drafts)) at every N, so
-that the scaling run compares like with like. By default the N GPUs run N
-independent replicas of the layer, each on its own 64 tokens (tokens are
-independent: no collective on the data path; weak scaling). `--tp S`
-tensor-splits the layer S ways instead (gate/up cut on I, down on I,
-float32 partials all-reduced over NCCL), as far as the reference's cut
-rules allow -- c2's I = 768 allows 2 and 4 -- with N / S replicas of the
-split. `--workload c4` (H 4096, 256 experts top-8, I 1536, 256 tokens) is
-the tensor-split block the baseline names for 2/4/8 GPUs.
+synthetic tokens.
+* One GPU: configuration c2 (H 2048, 128 experts top-8, I 768 + shared 768,
+  64 tokens = 16 sequences x (1 + 3 MTP drafts)), the configuration the
+  decode metric is quoted on. The line also carries secondary figures: the
+  c3 prefill step (4096 tokens, Zipf 1.1) with the tcgen05 grouped GEMM's
+  own duration and tensor roofline, and c4 unsplit on one GPU.
+* N GPUs: the tensor-split block the baseline names for 2/4/8 B200 (c4:
+  H 4096, 256 experts top-8, I 1536, 256 tokens), split N ways -- gate/up
+  cut on I, down on I, float32 partials all-reduced over NCCL and rounded
+  once (strong scaling: the same 256 tokens at every N). The line carries
+  the all-reduce's share of the step and, as a secondary figure, N
+  independent c2 replicas. `--workload` / `--tp` pick any other plan.
 
 Inputs larger than L2: the timed loop cycles over several independently
 seeded copies of the layer (> 3x the 126 MB L2 in total), so every step
@@ -29,9 +31,8 @@ HBM; `e2e` times the public captured call (`CapturedBlock`) with the input
 copied from pinned host memory and the output read back every step.
 
 --impl reference times the CPU restatement of the reference semantics
-(`oracle/`, the reference's own MLX code cannot run here) on all host
-threads; each step is a bounded sample (a rotating subset of the routed
-experts, rescaled by its share of the layer's expert work).
+(`oracle/`; the reference's own MLX code cannot run here) on all host
+threads, on the same workload; every step is one whole block call.
 """
 from __future__ import annotations
 
@@ -52,9 +53,6 @@ sys.path.insert(0, str(ROOT))
 METRIC = "VQ-MoE layer tokens/s"
 UNIT = "tokens/s"
 EXPERT_KERNEL = "expert_kernel<true,true>"
-# kernels of one block call: router logits, top-k + routing sort, shared
-# gate/up, shared down, routed experts (both stages), combine
-LAUNCHES_PER_STEP = 6
 
 
 def parse():
@@ -63,9 +61,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", default=None)
+    ap.add_argument("--workload", default=None,
+                    help="c1..c4 (default: c2 on one GPU, c4 split N ways on N GPUs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--tp", type=int, default=1,
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the secondary figures (prefill c3, c4 unsplit, c2 replicas)")
+    ap.add_argument("--tp", type=int, default=None,
                     help="tensor split of the layer (N / tp independent replicas)")
     return ap.parse_args()
 
@@ -171,124 +172,308 @@ class ClockSampler:
 
 # ------------------------------------------------------------- our arm
 
-def run_ours(args, world, rank, local):
-    import torch
-    import torch.distributed as dist
-    from knurlogic_b200 import CapturedBlock, _lib, synth, tensor_split
+def launches_per_call(cfg, T):
+    """Our kernels per block call: router logits + routing (one kernel up
+    to 512 tokens, a top-k and a sort kernel beyond), the shared expert's
+    two matmuls, the input permute of the prefill path, the routed experts
+    (one launch), the combine -- per 2048-token chunk."""
+    from knurlogic_b200.synth import MoEConfig  # noqa: F401
+    n = 0
+    for t0 in range(0, T, 2048):
+        t = min(2048, T - t0)
+        n += 2 + (1 if t > 512 else 0) + (2 if cfg.shared_inter else 0) + 1 + 1
+        if t * cfg.top_k >= 32 * cfg.experts:
+            n += 1
+    return n
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    workload = args.workload or "c2"
-    cfg = synth.CONFIGS[workload]
-    T = cfg.tokens
-    tp, dp = split_plan(cfg, world, args.tp)
-    # tensor-split groups of tp consecutive ranks; each group (a data-parallel
-    # replica) runs the layer on its own batch of tokens
-    group = None
-    if tp > 1:
-        groups = [dist.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(dp)]
-        group = groups[rank // tp]
-    tp_rank, replica = rank % tp, rank // tp
 
-    # copies of the layer: > 3x L2 of weights streamed per cycle
+def build_copies(cfg, tp, tp_rank, group, dev, seed0=100):
+    """Independently seeded copies of the layer (this rank's cut of each),
+    more than 3x the 126 MB L2 of weights in total."""
+    from knurlogic_b200 import synth, tensor_split
     per_layer = synth.algorithmic_bytes(cfg, cfg.experts) / tp
     L = max(2, min(16, math.ceil(3 * 126e6 / per_layer) + 1))
     blocks = []
     for i in range(L):
-        w = synth.make_weights(cfg, seed=100 + i, device=dev, scales="ones")
+        w = synth.make_weights(cfg, seed=seed0 + i, device=dev, scales="ones")
         blocks.append(tensor_split.build_block(w, cfg.top_k, rank=tp_rank, n=tp, group=group))
         del w
-    x = synth.make_input(cfg, seed=7 + replica, device=dev)
-    # one graph per layer copy: block (+ all-reduce under a split)
-    outs = [torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device=dev) for _ in range(L)]
-    parts = [torch.empty(T, cfg.hidden, dtype=torch.float32, device=dev) for _ in range(L)]
+    return blocks
 
-    def step(i):
-        b = blocks[i]
-        if tp == 1:
-            b.forward_into(x, outs[i])
-        else:
-            b.forward_into(x, parts[i])
-            dist.all_reduce(parts[i], group=group)
-            outs[i].copy_(parts[i])
 
-    s = torch.cuda.Stream(device=dev)
-    s.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(s):
-        for i in range(L):
-            step(i)
-    torch.cuda.current_stream(dev).wait_stream(s)
-    torch.cuda.synchronize(dev)
-    graphs = []
-    for i in range(L):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            step(i)
-        graphs.append(g)
-    torch.cuda.synchronize(dev)
+class Graphs:
+    """One CUDA graph per layer copy: the block, plus under a split the
+    float32 all-reduce of the partials and the bf16 rounding."""
+
+    def __init__(self, blocks, x, tp, group, dev):
+        import torch
+        import torch.distributed as dist
+        T, H = x.shape
+        self.L = len(blocks)
+        self.outs = [torch.empty(T, H, dtype=torch.bfloat16, device=dev) for _ in blocks]
+        self.parts = [torch.empty(T, H, dtype=torch.float32, device=dev) for _ in blocks]
+
+        def step(i):
+            b = blocks[i]
+            if tp == 1:
+                b.forward_into(x, self.outs[i])
+            else:
+                b.forward_into(x, self.parts[i])
+                dist.all_reduce(self.parts[i], group=group)
+                self.outs[i].copy_(self.parts[i])
+        self.step = step
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for i in range(self.L):
+                step(i)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        self.graphs = []
+        for i in range(self.L):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step(i)
+            self.graphs.append(g)
+        torch.cuda.synchronize(dev)
+
+    def replay(self, i):
+        self.graphs[i % self.L].replay()
+
+
+def timed(fn, steps, warmup, world, local, dev, clocks=None):
+    """ms for exactly `steps` calls of fn(i) after `warmup` untimed ones:
+    CUDA events on the current stream, a barrier and a synchronize on both
+    sides, the max over ranks."""
+    import torch
+    import torch.distributed as dist
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
-
-    # ---- warm-up, then exactly K timed steps
-    for i in range(args.warmup):
-        graphs[i % L].replay()
-    clocks = ClockSampler(local)
+    for i in range(warmup):
+        fn(i)
     barrier()
     torch.cuda.synchronize(dev)
-    clocks.start()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for i in range(args.steps):
-        graphs[i % L].replay()
-    ev1.record()
+    if clocks:
+        clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        fn(i)
+    e1.record()
     torch.cuda.synchronize(dev)
-    clocks.stop()
+    if clocks:
+        clocks.stop()
     barrier()
-    ms = ev0.elapsed_time(ev1)
+    ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    return ms
+
+
+def default_plan(args, world):
+    """(workload, requested tensor split): c2 on one GPU (the configuration
+    the decode metric is quoted on); on N GPUs the tensor-split block the
+    baseline names for 2/4/8 B200 (c4, split N ways)."""
+    workload = args.workload or ("c4" if world > 1 else "c2")
+    tp = args.tp if args.tp is not None else (world if world > 1 and workload == "c4" else 1)
+    return workload, tp
+
+
+def split_groups(world, tp, rank):
+    import torch.distributed as dist
+    if tp == 1:
+        return None
+    dp = world // tp
+    groups = [dist.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(dp)]
+    return groups[rank // tp]
+
+
+def tp_share(blocks, x, group, world, local, dev, n):
+    """The all-reduce's share of a tensor-split step: per step, the block
+    (float32 partial) and the all-reduce replayed as separate graphs with
+    CUDA events between them, averaged over n steps, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    T, H = x.shape
+    part = torch.empty(T, H, dtype=torch.float32, device=dev)
+    L = len(blocks)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for b in blocks:
+            b.forward_into(x, part)
+        dist.all_reduce(part, group=group)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    gb = []
+    for b in blocks:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            b.forward_into(x, part)
+        gb.append(g)
+    ga = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ga):
+        dist.all_reduce(part, group=group)
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
+    dist.barrier(device_ids=[local])
+    for i in range(n):
+        evs[i][0].record()
+        gb[i % L].replay()
+        evs[i][1].record()
+        ga.replay()
+        evs[i][2].record()
+    torch.cuda.synchronize(dev)
+    rows = evs[min(10, n - 1):]
+    blk = sum(r[0].elapsed_time(r[1]) for r in rows) / len(rows)
+    ar = sum(r[1].elapsed_time(r[2]) for r in rows) / len(rows)
+    t = torch.tensor([blk, ar], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    blk, ar = (float(v) for v in t.tolist())
+    del ga, gb
+    torch.cuda.synchronize(dev)
+    return {"block_ms": round(blk, 5), "allreduce_ms": round(ar, 5),
+            "allreduce_share": round(ar / (blk + ar), 4), "allreduce_bytes": T * H * 4,
+            "note": "block and float32 all-reduce replayed as separate graphs, CUDA events between them; "
+                    "the all-reduce time includes waiting for the slowest rank's block"}
+
+
+def quick_value(workload, tp, rank, world, local, dev, steps, warmup):
+    """tokens/s of `workload` split tp ways (world / tp replicas), graph
+    replays over layer copies: a secondary figure beside the headline."""
+    from knurlogic_b200 import synth
+    cfg = synth.CONFIGS[workload]
+    tp, dp = split_plan(cfg, world, tp)
+    group = split_groups(world, tp, rank)
+    blocks = build_copies(cfg, tp, rank % tp, group, dev, seed0=300)
+    x = synth.make_input(cfg, seed=11 + rank // tp, device=dev)
+    G = Graphs(blocks, x, tp, group, dev)
+    ms = timed(G.replay, steps, warmup, world, local, dev)
+    del G, blocks
+    return {"workload": workload, "tokens": cfg.tokens, "tensor_parallel": tp, "replicas": dp,
+            "value": round(cfg.tokens * dp * steps / (ms / 1e3), 1), "unit": UNIT,
+            "ms_per_step": round(ms / steps, 5), "steps": steps}
+
+
+def prefill_profile(dev, steps=100, warmup=5):
+    """c3 (4096 prefill tokens, Zipf 1.1) on this GPU: the step time of the
+    whole block (graph replays over layer copies, so weights stream from
+    HBM), and the tcgen05 grouped GEMM's own duration per 2048-token launch
+    (CUDA events around it inside the block, through the timed entry), with
+    its tensor roofline against the burst bf16 peak."""
+    import ctypes
+
+    import torch
+
+    from knurlogic_b200 import _lib, synth
+    cfg = synth.CONFIGS["c3"]
+    blocks = build_copies(cfg, 1, 0, None, dev, seed0=200)
+    x = synth.make_input(cfg, seed=9, device=dev)
+    G = Graphs(blocks, x, 1, None, dev)
+    ms = timed(G.replay, steps, warmup, 1, 0, dev)
+    del G
+    step_ms = ms / steps
+    # the grouped GEMM alone, on the first 2048-token launch of the step
+    Tc = 2048
+    xc = x[:Tc].contiguous()
+    n = 60
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(n)]
+    out = torch.empty(Tc, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    descs = [b._desc() for b in blocks]
+    wss = [b.workspace(Tc, dev) for b in blocks]
+    for i in range(n):
+        b = i % len(blocks)
+        arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in evs[i]])
+        _lib.call("vqmoe_sparse_moe_block_timed", ctypes.byref(descs[b]), xc.data_ptr(), Tc,
+                  out.data_ptr(), _lib.OUT_BF16, wss[b].data_ptr(), wss[b].numel(),
+                  stream.cuda_stream, arr, 6)
+    torch.cuda.synchronize(dev)
+    rows = evs[10:]
+    k_ms = sum(r[5].elapsed_time(r[2]) for r in rows) / len(rows)
+    perm_ms = sum(r[1].elapsed_time(r[5]) for r in rows) / len(rows)
+    router_ms = sum(r[0].elapsed_time(r[1]) for r in rows) / len(rows)
+    k_flops = 2 * Tc * cfg.top_k * 3 * cfg.inter * cfg.hidden
+    tpk, kind = tensor_peak()
+    layer_fl = synth.algorithmic_flops(cfg)
+    del blocks
+    torch.cuda.synchronize(dev)
+    return {"workload": "c3", "tokens": cfg.tokens, "steps": steps,
+            "ms_per_step": round(step_ms, 5), "value": round(cfg.tokens / (step_ms / 1e3), 1), "unit": UNIT,
+            "layer_tflops": round(layer_fl / (step_ms / 1e3) / 1e12, 2),
+            "layer_frac": round(layer_fl / (step_ms / 1e3) / 1e12 / tpk, 4),
+            "kernel": "expert_prefill_kernel", "kernel_ms": round(k_ms, 5),
+            "kernel_flops_per_launch": k_flops,
+            "kernel_tflops": round(k_flops / (k_ms / 1e3) / 1e12, 2),
+            "kernel_frac": round(k_flops / (k_ms / 1e3) / 1e12 / tpk, 4),
+            "peak_tflops": tpk, "peak_source": kind + " (burst)",
+            "router_ms_per_launch": round(router_ms, 5), "permute_ms_per_launch": round(perm_ms, 5)}
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from knurlogic_b200 import CapturedBlock, synth
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    workload, tp_req = default_plan(args, world)
+    cfg = synth.CONFIGS[workload]
+    T = cfg.tokens
+    tp, dp = split_plan(cfg, world, tp_req)
+    # tensor-split groups of tp consecutive ranks; each group (a data-parallel
+    # replica) runs the layer on its own batch of tokens
+    group = split_groups(world, tp, rank)
+    replica = rank // tp
+    blocks = build_copies(cfg, tp, rank % tp, group, dev)
+    L = len(blocks)
+    x = synth.make_input(cfg, seed=7 + replica, device=dev)
+
+    # ---- the headline: exactly K graph replays after W warm-up
+    G = Graphs(blocks, x, tp, group, dev)
+    clocks = ClockSampler(local)
+    ms = timed(G.replay, args.steps, args.warmup, world, local, dev, clocks)
     ms_per_step = ms / args.steps
     value = T * dp * args.steps / (ms / 1e3)
+    del G
+    torch.cuda.synchronize(dev)
+
+    comm = tp_share(blocks, x, group, world, local, dev, min(args.steps, 200)) if tp > 1 else None
 
     # ---- stage times of the block (events between its kernels), rank 0
-    stage = None
-    inds_count = None
+    stage, distinct = None, None
     if rank == 0 and T <= 2048:      # the timed entry point takes one launch of tokens
-        stage, inds_count = stage_profile(blocks, x, cfg, dev, args, tp)
+        stage, distinct = stage_profile(blocks, x, cfg, dev, args, tp)
+    if world > 1:
+        dist.barrier(device_ids=[local])
 
     # ---- end to end through the public captured call, host buffers
     xh = x.cpu().pin_memory()
     yh = torch.empty(T, cfg.hidden, dtype=torch.bfloat16).pin_memory()
     cap = [CapturedBlock(b, T) for b in blocks]
-    for i in range(max(3, args.warmup)):
-        cap[i % L](xh, out=yh)
-    barrier()
-    torch.cuda.synchronize(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.steps):
-        cap[i % L](xh, out=yh)
-    e1.record()
-    torch.cuda.synchronize(dev)
-    barrier()
-    ems = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ems], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = float(t.item())
+    ems = timed(lambda i: cap[i % L](xh, out=yh), args.steps, max(3, args.warmup), world, local, dev)
+    cap[0].check_status()
     e2e = {"value": T * dp * args.steps / (ems / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": xh.numel() * xh.element_size(),
            "d2h_bytes_per_step": yh.numel() * yh.element_size()}
-    del cap
     # graphs holding NCCL calls go before the process group does
-    del graphs
+    del cap, blocks
     torch.cuda.synchronize(dev)
+
+    # ---- secondary figures beside the headline
+    secondary = {}
+    if not args.no_secondary:
+        if world == 1 and workload == "c2":
+            secondary["prefill"] = prefill_profile(dev)
+            secondary["c4_tp1"] = quick_value("c4", 1, rank, world, local, dev, 100, 5)
+        elif world > 1 and tp > 1:
+            secondary["c2_replicas"] = quick_value("c2", 1, rank, world, local, dev, 200, 10)
 
     if rank != 0:
         return None
@@ -322,7 +507,7 @@ def run_ours(args, world, rank, local):
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
-        "higher_is_better": True, "scaling": "weak" if dp > 1 or world == 1 else "strong",
+        "higher_is_better": True, "scaling": "weak" if tp == 1 else "strong",
         "vs_baseline": None, "dtype": "vq-u8 codes / fp16 dequant / bf16 io",
         "data": "synthetic (seeded; uniform codes, N(0,0.02) codebooks, N(0,1) tokens)",
         "config": {"workload": workload, "tokens": T, "hidden": cfg.hidden,
@@ -331,13 +516,15 @@ def run_ours(args, world, rank, local):
                    "group": cfg.group, "tensor_parallel": tp, "replicas": dp,
                    "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""), "layer_copies": L,
                    "l2": "inputs larger than L2 (layer copies cycled)",
-                   "distinct_experts": inds_count},
+                   "distinct_experts": distinct},
         "roofline": roof,
         "stages_ms": stage and {k: round(v, 5) for k, v in stage.items() if k.endswith("_ms")},
+        "tensor_split": comm,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "gpu_launches": launches_per_call(cfg, T) * args.steps,
         "clocks": clocks.record(),
+        "secondary": secondary or None,
     }
     return line
 
@@ -461,58 +648,56 @@ def _oracle_inputs(cfg, seed=100):
 
 
 def cpu_baseline(cfg, workload):
-    """The oracle on this host: one full block call (a bounded sample)."""
+    """The oracle on this host: two whole block calls, the second timed."""
     from oracle import cpu_baseline as C
     x, p = _oracle_inputs(cfg)
+    C.time_block(x, p, cfg.top_k, vq=True)
     sec, n = C.time_block(x, p, cfg.top_k, vq=True)
     return {"value": round(x.shape[0] / sec, 2), "unit": UNIT, "cores": n, "kind": "port",
-            "sample": f"one full {workload} block call ({x.shape[0]} tokens), numpy oracle, "
-                      f"experts on {n} threads ({sec:.2f} s)"}
+            "sample": f"one whole {workload} block call ({x.shape[0]} tokens: router, every routed expert, "
+                      f"combine, shared expert), numpy oracle, experts on {n} worker threads, BLAS held "
+                      f"to one thread each ({sec:.2f} s)"}
 
 
 def run_reference(args, world, rank):
-    """The reference arm: the oracle port on all host threads, K steps."""
-    from concurrent.futures import ThreadPoolExecutor
-
-    import numpy as np
-
+    """The reference arm: the oracle port (the CPU restatement of the
+    reference's block) on all host threads. Every step is one whole block
+    call on the arm's workload -- router, every routed expert, combine and
+    shared expert. When K + W such calls would not finish within about two
+    minutes, only the first steps that fit are timed (at least 3; warm-up
+    cut to one call), and the line says how many."""
     from knurlogic_b200 import synth
     from oracle import cpu_baseline as C
-    workload = args.workload or "c2"
+    workload, tp_req = default_plan(args, world)
     cfg = synth.CONFIGS[workload]
-    tp, dp = split_plan(cfg, world, args.tp)
+    tp, dp = split_plan(cfg, world, tp_req)
     x, p = _oracle_inputs(cfg)
     n = C.threads()
-    from oracle import moe_ref as R
-    inds, _, _ = R.router(x, p["router"], cfg.top_k)
-    routed = np.unique(inds)
-    D = len(routed)
-    budget = 120.0 / max(1, args.steps + args.warmup)     # seconds per step
-    with ThreadPoolExecutor(n) as pool:
-        # calibrate: seconds per expert with n experts in flight
+    budget = 120.0
+    with C.pool_of(n) as pool:
         t0 = time.perf_counter()
-        C.block(x, p, cfg.top_k, True, pool, experts=routed[:n])
-        per_expert = (time.perf_counter() - t0) / n
-        m = int(max(1, min(D, budget / max(per_expert, 1e-6))))
-        cursor = 0
-        done_tokens, secs = 0.0, 0.0
-        for i in range(args.warmup + args.steps):
-            sel = np.take(routed, np.arange(cursor, cursor + m) % D)
-            cursor = (cursor + m) % D
-            t0 = time.perf_counter()
-            got, _ = C.block(x, p, cfg.top_k, True, pool, experts=sel)
-            dt = time.perf_counter() - t0
-            if i >= args.warmup:
-                secs += dt
-                done_tokens += x.shape[0] * got / D
-    value = done_tokens / secs
-    sample = (f"per step {m} of the {D} routed experts of one {workload} block call "
-              f"({x.shape[0]} tokens; router included), rescaled by its share of the "
-              f"layer's expert work; numpy oracle on {n} threads")
+        C.block(x, p, cfg.top_k, True, pool)          # first warm-up call, also the estimate
+        est = time.perf_counter() - t0
+        fit = int(budget / max(est, 1e-6))
+        if args.warmup + args.steps <= fit:
+            warm, steps = args.warmup, args.steps
+        else:
+            warm, steps = min(args.warmup, 1), max(3, min(args.steps, fit))
+        for _ in range(max(0, warm - 1)):
+            C.block(x, p, cfg.top_k, True, pool)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            C.block(x, p, cfg.top_k, True, pool)
+        secs = time.perf_counter() - t0
+    T = x.shape[0]
+    value = T * steps / secs
+    sample = (f"every step one whole {workload} block call ({T} tokens: router, every routed expert, "
+              f"combine{', shared expert' if cfg.shared_inter else ''}), numpy oracle, experts on {n} "
+              f"worker threads, BLAS held to one thread each; {steps} of the {args.steps} steps timed")
     return {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(1e3 * secs / args.steps, 3), "higher_is_better": True,
-            "scaling": "weak" if dp > 1 or world == 1 else "strong", "vs_baseline": None,
+            "ms_per_step": round(1e3 * secs / steps, 3), "higher_is_better": True,
+            "scaling": "weak" if tp == 1 else "strong", "vs_baseline": None,
             "dtype": "vq-u8 codes / fp16 dequant / bf16 io", "data": "synthetic (seeded)",
             "config": {"workload": workload, "tokens": cfg.tokens, "tensor_parallel": tp, "replicas": dp},
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": n, "kind": "port",

@@ -205,9 +205,11 @@ VQMOE_API vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate,
  * allocator's out-of-memory handler. Returns VQMOE_WORKSPACE_TOO_SMALL
  * when vqmoe_switch_glu_workspace_size(gate, down, tokens, top_k) exceeds
  * the scratch. The first call on a device takes the scratch's address
- * (cudaGetSymbolAddress): make it before any stream capture. Nothing in the
- * scratch needs to start at zero. One scratch per device: calls that overlap
- * on the same device race; the caller must order them. */
+ * (cudaGetSymbolAddress) and keeps it for that device index: make it before
+ * any stream capture, in the device's primary context (a driver-API context
+ * of the caller's own, or a call after cudaDeviceReset, is not supported).
+ * Nothing in the scratch needs to start at zero. One scratch per device:
+ * calls that overlap on the same device race; the caller must order them. */
 VQMOE_API vqmoe_status vqmoe_switch_glu_noalloc(const vqmoe_linear *gate,
                               const vqmoe_linear *up,
                               const vqmoe_linear *down, const void *x,

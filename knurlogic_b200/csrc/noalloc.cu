@@ -12,10 +12,14 @@
 // module image, and its address is taken with cudaGetSymbolAddress once per
 // device (on the first call on that device, with that device current). Make
 // that first call before any stream capture. Nothing in the scratch has to
-// start at zero: the routing kernel zeroes its work counters on every call
-// and every other byte is written before it is read. There is one scratch per
-// device, so calls that overlap on one device (two streams, or two host
-// threads) race on it: the caller orders them.
+// start at zero: the routing kernel zeroes its work counters on every call,
+// the call clears its status words, and every other byte is written before
+// it is read. There is one scratch per device, so calls that overlap on one
+// device (two streams, or two host threads) race on it: the caller orders
+// them. The address is cached per device index, so the library serves the
+// device's primary context (the one the CUDA runtime uses): a host that
+// makes its own driver-API context current, or calls after
+// cudaDeviceReset, is not supported by this entry point.
 #include <mutex>
 
 #include "common.cuh"

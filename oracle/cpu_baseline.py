@@ -5,13 +5,19 @@ The reference cannot run here (MLX is absent and its VQ runtime is not in
 the repository), so the baseline is this CPU restatement of the reference
 semantics (`moe_ref`): router, per-expert dequantise-then-matmul, combine
 and shared expert, with the experts spread over a thread pool (numpy
-releases the GIL in the dequantisation and the matmuls).
+releases the GIL in the dequantisation and the matmuls). Every timed call is
+a whole block call: all routed experts, the combine and the shared expert.
+
+Threads: one pool worker per host core, and the BLAS library held to one
+thread while the pool runs (`threadpoolctl`), so that the workers do not
+each start a BLAS thread per core (cores x cores threads).
 """
 from __future__ import annotations
 
 import os
 import time
 from concurrent.futures import ThreadPoolExecutor
+from contextlib import contextmanager
 
 import numpy as np
 
@@ -21,6 +27,14 @@ from . import moe_ref as R
 def threads() -> int:
     return max(1, len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity")
                else (os.cpu_count() or 1))
+
+
+@contextmanager
+def pool_of(n: int):
+    """A pool of n workers with BLAS held to one thread each."""
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(limits=1), ThreadPoolExecutor(n) as pool:
+        yield pool
 
 
 def _expert_rows(x, inds, p, vq, e):
@@ -36,32 +50,32 @@ def _expert_rows(x, inds, p, vq, e):
     return pairs, R.linear(ain, p["down"][e])
 
 
-def block(x, p, k, vq, pool: ThreadPoolExecutor, experts=None):
-    """`moe_ref.sparse_moe_block` with the experts on `pool`. With
-    `experts` (a subset of the routed experts) only those experts' rows are
-    computed -- a bounded sample -- and the combine is skipped."""
+def _shared(x, p):
+    return R.shared_expert(x, p["shared_expert_gate"], p["shared_up"], p["shared_gate"],
+                           p["shared_down"])
+
+
+def block(x, p, k, vq, pool: ThreadPoolExecutor):
+    """`moe_ref.sparse_moe_block` with the routed experts (and the shared
+    expert, as one more task) on `pool`."""
     inds, scores, _ = R.router(x, p["router"], k)
     routed = np.unique(inds)
-    todo = routed if experts is None else np.intersect1d(routed, experts)
-    parts = list(pool.map(lambda e: _expert_rows(x, inds, p, vq, int(e)), todo))
-    if experts is not None:
-        return len(todo), len(routed)
+    shared = pool.submit(_shared, x, p) if "shared_gate" in p else None
+    parts = list(pool.map(lambda e: _expert_rows(x, inds, p, vq, int(e)), routed))
     T = x.shape[0]
     y = np.zeros((T * k, p["down"].shape[1]), np.float32)
     for pairs, rows in parts:
         y[pairs] = rows
     out = R.combine(y.reshape(T, k, -1), scores)
-    if "shared_gate" in p:
-        sh = R.shared_expert(x, p["shared_expert_gate"], p["shared_up"],
-                             p["shared_gate"], p["shared_down"])
-        out = R.bf16(out.astype(np.float64) + sh)
+    if shared is not None:
+        out = R.bf16(out.astype(np.float64) + shared.result())
     return out
 
 
 def time_block(x, p, k, vq, n_threads=None, repeats=1):
     """(seconds per full block call, threads) on the host cores."""
     n = n_threads or threads()
-    with ThreadPoolExecutor(n) as pool:
+    with pool_of(n) as pool:
         t0 = time.perf_counter()
         for _ in range(repeats):
             block(x, p, k, vq, pool)

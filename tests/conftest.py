@@ -5,6 +5,8 @@ golden, the host-side logic, and that libvqmoe.so loads and exports what
 include/vqmoe.h declares. `-m gpu` runs the parity tests proper on a B200,
 through the C ABI, against the oracle.
 """
+import json
+import os
 import sys
 from pathlib import Path
 
@@ -81,3 +83,59 @@ def golden_state_dict(g: dict) -> dict:
         "mlp.shared_expert.down_proj.weight": bf(g["shared_down"]),
         "mlp.shared_expert_gate.weight": bf(g["shared_expert_gate"]),
     }
+
+
+# ------------------------------------------------------------ tolerances
+#
+# Layer outputs (bf16) against the oracle, two bars:
+# * max |gpu - oracle| <= REL * max |oracle| -- the north star's 1e-2
+#   relative, on every element;
+# * per element |gpu - oracle| <= ULPS bf16 steps of |oracle| + FLOOR *
+#   rms(oracle), on all but FRAC of the elements. The GPU accumulates in
+#   float32 (tensor cores), the oracle exactly, and the decode kernels apply
+#   each 64-input group's scale to the partial sum (s * (codebook . x)) where
+#   the oracle dequantises fp16(codebook * s): an expert output or SwiGLU
+#   activation now and then rounds to the neighbouring bf16 value. Through
+#   the top-k sum such a step is a step of the summands' magnitude, which
+#   cancellation can make several steps of a small output element -- the
+#   rms floor covers that.
+REL = 1e-2
+ULPS = 2
+FLOOR = 2.0 ** -9
+FRAC = 0.005
+
+
+def bf16_ulp(a):
+    """The bf16 step at |a| (2^(e-7) for |a| in [2^e, 2^(e+1)); the
+    smallest normal's step below it)."""
+    a = np.abs(np.asarray(a, np.float64))
+    _, e = np.frexp(np.maximum(a, 2.0 ** -126))
+    return np.ldexp(1.0, e - 8)
+
+
+def bf16_error_stats(got, ref) -> dict:
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = np.abs(got - ref)
+    u = d / bf16_ulp(ref)
+    rms = float(np.sqrt(np.mean(np.square(ref)))) or 1.0
+    return {"n": int(ref.size), "equal": float((d == 0).mean()),
+            "beyond_1ulp": float((u > 1).mean()), "beyond_2ulp": float((u > 2).mean()),
+            "beyond_bar": float((d > ULPS * bf16_ulp(ref) + FLOOR * rms).mean()),
+            "max_ulp": float(u.max()), "max_rel_rms": float(d.max() / rms),
+            "max_rel": float(d.max() / (np.abs(ref).max() or 1.0))}
+
+
+def assert_bf16_close(got, ref, what=""):
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    assert np.isfinite(got).all(), f"{what}: non-finite output"
+    st = bf16_error_stats(got, ref)
+    log = os.environ.get("VQMOE_TOLERANCE_LOG")
+    if log:
+        with open(log, "a") as f:
+            f.write(json.dumps({"what": what, **st}) + "\n")
+    assert st["max_rel"] <= REL, f"{what}: max diff {st['max_rel']:.3e} of max |ref| > {REL}"
+    assert st["beyond_bar"] <= FRAC, (f"{what}: {st['beyond_bar']:.3%} of elements off by more than "
+                                      f"{ULPS} bf16 steps + 2^-9 rms ({st})")

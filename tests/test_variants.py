@@ -146,7 +146,7 @@ def test_router_variants_match_oracle(mode, name, tokens):
 @pytest.mark.gpu
 @pytest.mark.parametrize("mode", [_lib.ROUTER_TOPK_SOFTMAX, _lib.ROUTER_SOFTMAX_TOPK])
 def test_block_router_variants_match_oracle(mode):
-    from tests.test_gpu_parity import assert_bf16_close
+    from tests.conftest import assert_bf16_close
     cfg = synth.CONFIGS["c2"]
     w = synth.make_weights(cfg, seed=8, scales="random")
     x = synth.make_input(cfg, seed=8)
@@ -161,7 +161,7 @@ def test_block_router_variants_match_oracle(mode):
 def test_geglu_block_matches_oracle(name, tokens):
     """GeGLU experts on the decode path (c1, c2) and on the tcgen05 prefill
     path ("pf": about 256 pairs per expert)."""
-    from tests.test_gpu_parity import assert_bf16_close
+    from tests.conftest import assert_bf16_close
     cfg = (synth.MoEConfig("pf", 16, 4, 512, 256, 192, tokens, router="uniform")
            if name == "pf" else synth.CONFIGS[name])
     w = synth.make_weights(cfg, seed=12, scales="random")
@@ -205,7 +205,7 @@ def test_gemma4_router_and_experts_match_oracle(name, tokens):
     input (the oracle takes the module's RMS-normed rows, an unpinned step
     restated separately), then the GeGLU experts and the weighted sum on the
     decode path (c2) and the tcgen05 prefill path ("pf")."""
-    from tests.test_gpu_parity import assert_bf16_close
+    from tests.conftest import assert_bf16_close
     from knurlogic_b200.gemma4 import Router
     cfg = (synth.MoEConfig("pf", 16, 4, 512, 256, 0, tokens, router="uniform")
            if name == "pf" else synth.CONFIGS[name])
