@@ -385,6 +385,10 @@ def prefill_profile(dev, steps=100, warmup=5):
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(n)]
     out = torch.empty(Tc, cfg.hidden, dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
+    for row in evs:                      # torch creates an event at its first record
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize(dev)
     descs = [b._desc() for b in blocks]
     wss = [b.workspace(Tc, dev) for b in blocks]
     for i in range(n):

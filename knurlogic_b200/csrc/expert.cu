@@ -26,11 +26,9 @@
 //   * looks each code up in a shared-memory codebook and feeds the 8-byte
 //     entry (4 fp16) straight into mma.sync m16n8k16 as the A operand
 //     (fp16 x fp16 -> fp32); B is the tile's token rows from shared memory;
-//   * sums each 64-input scale group on its own and adds it to the row's
-//     total times the group scale in fp32 (4 FMA per MMA fragment). The
-//     weight this applies is the exact product codebook x scale; the
-//     dense decode (vqmoe_dequant) rounds that product to fp16 -- a
-//     difference below 2^-11 of each weight.
+//   * multiplies the entry by its row's 64-input group scale in fp16
+//     (mul.rn.f16x2): the weight is fp16(codebook x scale), exactly what
+//     vqmoe_dequant and the prefill kernel use.
 // Dense tiles (bf16 experts) load A from global memory.
 //
 // Why mma.sync and registers here rather than tcgen05: at 1-64 tokens the
@@ -107,17 +105,26 @@ __device__ __forceinline__ void load_half(HalfBuf<NMAT, MT> &b, const uint8_t *c
 
 // 8 sub-steps from a half buffer; xoff: this lane's staged-row offset of
 // sub-step 0; lanebyte: this lane's codebook copy offset (lane % 16) * 8.
-// Each scale group (4 sub-steps, 64 inputs) is summed on its own from the
-// raw fp16 codebook entries (products exact, fp32 accumulate) and added to
-// the row's total times the group's fp16 scale (4 FMA per fragment).
+// Each looked-up codebook entry (4 fp16) is multiplied by its row's group
+// scale with one mul.rn.f16x2 per two weights -- W = fp16(codebook * scale),
+// the dequantised weight bit for bit (the product of two fp16 values is
+// exact before that one rounding) -- and fed to the fp16 MMA, whose
+// products are exact and whose sums are float32: the same arithmetic as
+// the prefill kernel and vqmoe_dequant.
 template <int NMAT, int MT>
 __device__ __forceinline__ void compute_half(const HalfBuf<NMAT, MT> &b, float (&acc)[NMAT][MT][4],
                                              const uint8_t *cb, uint32_t lanebyte,
                                              const uint8_t *xs, int xoff) {
-    const float zero[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < 2; ++j) {          // the half's two scale groups
-        float gacc[NMAT][MT][4];
+        // the group's scale of rows g (h = 0) and g + 8 (h = 1), as half2
+        uint32_t s2[NMAT][MT][2];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) s2[m][mt][h] = __byte_perm(b.sc[m][mt][h], 0, j ? 0x3232 : 0x1010);
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
             const int q = 4 * j + qq;
@@ -132,25 +139,12 @@ __device__ __forceinline__ void compute_half(const HalfBuf<NMAT, MT> &b, float (
                     const uint32_t a1 = __byte_perm(b.cw[m][mt][1][j], lanebyte, sel);
                     const uint2 e0 = lds2(cb + m * 128, a0);
                     const uint2 e1 = lds2(cb + m * 128, a1);
-                    if (qq == 0)
-                        mma_f16_c(gacc[m][mt], e0.x, e1.x, e0.y, e1.y, bf.x, bf.y, zero);
-                    else
-                        mma_f16(gacc[m][mt], e0.x, e1.x, e0.y, e1.y, bf.x, bf.y);
+                    // A fragment: rows g (e0) and g + 8 (e1), k-slots {2t, 2t+1} then {2t+8, 2t+9}
+                    mma_f16(acc[m][mt], hmul2_u32(e0.x, s2[m][mt][0]), hmul2_u32(e1.x, s2[m][mt][1]),
+                            hmul2_u32(e0.y, s2[m][mt][0]), hmul2_u32(e1.y, s2[m][mt][1]), bf.x, bf.y);
                 }
             }
         }
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                // fragment rows g (elements 0, 1) and g + 8 (elements 2, 3)
-                const float s0 = __half2float(__ushort_as_half((unsigned short)(b.sc[m][mt][0] >> (16 * j))));
-                const float s1 = __half2float(__ushort_as_half((unsigned short)(b.sc[m][mt][1] >> (16 * j))));
-                acc[m][mt][0] = fmaf(s0, gacc[m][mt][0], acc[m][mt][0]);
-                acc[m][mt][1] = fmaf(s0, gacc[m][mt][1], acc[m][mt][1]);
-                acc[m][mt][2] = fmaf(s1, gacc[m][mt][2], acc[m][mt][2]);
-                acc[m][mt][3] = fmaf(s1, gacc[m][mt][3], acc[m][mt][3]);
-            }
     }
 }
 
