@@ -249,6 +249,14 @@ VQMOE_API vqmoe_status vqmoe_router_ex(const void *x, const void *router_w,
                           int32_t *inds, float *scores, float *sgate,
                           void *workspace, size_t workspace_bytes, void *stream);
 
+/* Gemma-4's router input, mx.fast.rms_norm(x, weight, eps) of Router.__call__
+ * (gemma4_text.py:171): out[T, H] bf16 = bf16(bf16(x * r) * weight), r =
+ * 1 / sqrt(mean(x^2) + eps) in float32, the mean of the squares summed
+ * exactly and rounded once to float32. x, weight [H] (Router.scale *
+ * hidden^-0.5, rounded to bf16) and out are bf16. */
+VQMOE_API vqmoe_status vqmoe_rms_norm(const void *x, const void *weight, int32_t tokens,
+                                      int32_t hidden, float eps, void *out, void *stream);
+
 /* Gemma-4's Experts.__call__ (gemma4_text.py:196-214): out[T, H] bf16 =
  * sum over the k slots of bf16(y[t, s] * scores[t, s]), in fp32 and rounded
  * once, with y = vqmoe_switch_glu(gate, up, down, x, indices) (GeGLU via

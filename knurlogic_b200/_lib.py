@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import (POINTER, Structure, c_char_p, c_int32, c_int64, c_size_t,
+from ctypes import (POINTER, Structure, c_char_p, c_float, c_int32, c_int64, c_size_t,
                     c_uint32, c_uint8, c_void_p)
 from pathlib import Path
 
@@ -82,6 +82,7 @@ SIGNATURES = [
     ("vqmoe_router_ex", c_int32,
      [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
       c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("vqmoe_rms_norm", c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),
     ("vqmoe_moe_experts_workspace_size", c_size_t, [POINTER(Linear), POINTER(Linear), c_int32, c_int32]),
     ("vqmoe_moe_experts", c_int32,
      [POINTER(Linear), POINTER(Linear), POINTER(Linear), c_void_p, c_void_p, c_void_p, c_int32, c_int32,

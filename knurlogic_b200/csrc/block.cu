@@ -746,6 +746,15 @@ vqmoe_status vqmoe_router_ex(const void *x, const void *router_w, const void *sg
                          expert_scale, static_cast<cudaStream_t>(stream));
 }
 
+vqmoe_status vqmoe_rms_norm(const void *x, const void *weight, int32_t tokens, int32_t hidden, float eps,
+                            void *out, void *stream) {
+    if (tokens <= 0 || hidden <= 0) return set_error(VQMOE_BAD_SHAPE, "rms_norm: T %d H %d", tokens, hidden);
+    if (!(eps >= 0.0f)) return set_error(VQMOE_BAD_SHAPE, "rms_norm: eps %g", (double)eps);
+    if (!x || !weight || !out) return set_error(VQMOE_BAD_POINTER, "rms_norm: x / weight / out");
+    return launch_rms_norm(static_cast<const uint16_t *>(x), static_cast<const uint16_t *>(weight), tokens, hidden,
+                           eps, static_cast<uint16_t *>(out), static_cast<cudaStream_t>(stream));
+}
+
 vqmoe_status vqmoe_router(const void *x, const void *router_w, const void *sgw, int32_t tokens, int32_t hidden,
                           int32_t num_experts, int32_t top_k, int32_t *inds, float *scores, float *sgate,
                           void *workspace, size_t workspace_bytes, void *stream) {

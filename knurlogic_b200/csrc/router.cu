@@ -801,4 +801,40 @@ vqmoe_status launch_route(const int32_t *inds, int P, int E, int32_t *cnt,
     return check_launch("route_kernel");
 }
 
+// ------------------------------------------------------------ RMS norm
+// Gemma-4's router input, mx.fast.rms_norm(x, w, eps) (gemma4_text.py:
+// 171): out = bf16(bf16(x * r) * w), r = 1 / sqrt(ms + eps) in float32
+// (IEEE square root and division), ms the mean of the squares: each square
+// of a bf16 value is exact in fp64, their sum is accumulated in fp64 and the
+// mean rounded once to float32. One CTA per row.
+__global__ void __launch_bounds__(256)
+rms_norm_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ w, int H, float eps,
+                uint16_t *__restrict__ out) {
+    __shared__ double s_part[8];
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const uint16_t *xr = x + (size_t)row * H;
+    double acc = 0.0;
+    for (int i = tid; i < H; i += blockDim.x) {
+        const double v = (double)bf16_to_f32(xr[i]);
+        acc += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((tid & 31) == 0) s_part[tid >> 5] = acc;
+    __syncthreads();
+    double sum = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum += s_part[i];
+    const float ms = (float)(sum / (double)H);
+    const float r = 1.0f / sqrtf(ms + eps);
+    for (int i = tid; i < H; i += blockDim.x)
+        out[(size_t)row * H + i] = f32_to_bf16(bf16r(bf16_to_f32(xr[i]) * r) * bf16_to_f32(w[i]));
+}
+
+vqmoe_status launch_rms_norm(const uint16_t *x, const uint16_t *w, int T, int H, float eps, uint16_t *out,
+                             cudaStream_t stream) {
+    rms_norm_kernel<<<T, 256, 0, stream>>>(x, w, H, eps, out);
+    return check_launch("rms_norm_kernel");
+}
+
 }  // namespace vqmoe

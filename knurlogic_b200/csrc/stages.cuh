@@ -19,6 +19,8 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
                                  int32_t *list, int32_t *active, int32_t *rank_scratch,
                                  uint32_t *zero, int zero_words, int mode, cudaStream_t stream);
 vqmoe_status launch_to_f16(const uint16_t *x, uint16_t *x16, size_t n, cudaStream_t stream);
+vqmoe_status launch_rms_norm(const uint16_t *x, const uint16_t *w, int T, int H, float eps, uint16_t *out,
+                             cudaStream_t stream);
 
 // The routed experts of one stage: pairs grouped by expert (route_kernel).
 struct RoutedIO {

@@ -11,12 +11,12 @@ Reference: `Router`, `GeGLU` and `Experts` of
 * `Experts(x, top_k_indices, top_k_weights)`: `SwitchGLU` with the GeGLU
   activation, each expert output times its weight, summed over the k slots.
 
-The projection, top-k, softmax and per-expert scale run in
-`vqmoe_router_ex` (exact bf16 logits; the softmax in float32), the experts
-and the weighted sum in `vqmoe_moe_experts`. The router's RMS norm is the
-one step outside the hot path: it runs as torch ops on the GPU, with the
-roundings `oracle.moe_ref.rms_norm` restates (MLX's own kernel cannot be
-run here, so that order of roundings is unpinned).
+The router's RMS norm runs in `vqmoe_rms_norm`, the projection, top-k,
+softmax and per-expert scale in `vqmoe_router_ex` (exact bf16 logits; the
+softmax in float32), the experts and the weighted sum in
+`vqmoe_moe_experts`. The norm's order of roundings (an exact mean of the
+squares rounded once to float32) is this build's reading of MLX's fused
+kernel, which cannot run here: unpinned.
 """
 from __future__ import annotations
 
@@ -47,13 +47,22 @@ class Router(nn.Module):
         self.top_k_experts = top_k_experts
         self.eps = eps
         self._root_size = H ** -0.5
+        # the norm's weight, scale * hidden**-0.5 rounded to bf16 (load time)
+        self.norm_weight = nn.Parameter((self.scale.float() * self._root_size).to(torch.bfloat16),
+                                        requires_grad=False)
 
     def normalize(self, x: torch.Tensor) -> torch.Tensor:
-        """The router input: `rms_norm(x, scale * hidden**-0.5, eps)` in bf16."""
-        w = (self.scale.float() * self._root_size).to(torch.bfloat16).float()
-        xf = x.float()
-        inv = torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
-        return ((xf * inv).to(torch.bfloat16).float() * w).to(torch.bfloat16)
+        """The router input: `rms_norm(x, scale * hidden**-0.5, eps)` in bf16
+        (`vqmoe_rms_norm`)."""
+        require_cuda(x)
+        if x.dtype != torch.bfloat16:
+            raise TypeError(f"x must be bfloat16, got {x.dtype}")
+        H = self.proj.weight.shape[1]
+        xi = _contig(x.reshape(-1, H))
+        out = torch.empty_like(xi)
+        _lib.call("vqmoe_rms_norm", xi.data_ptr(), self.norm_weight.data_ptr(), xi.shape[0], H,
+                  float(self.eps), out.data_ptr(), c_stream(x.device))
+        return out.reshape(x.shape)
 
     def forward(self, x: torch.Tensor):
         require_cuda(x)

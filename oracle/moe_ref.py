@@ -287,12 +287,15 @@ def moe_experts(x: np.ndarray, inds: np.ndarray, scores: np.ndarray, gate_w, up_
 
 def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     """`mx.fast.rms_norm(x, w, eps)` as restated for the Gemma-4 router
-    input (`gemma4_text.py:171`): float32 mean of squares, the normalised
-    value rounded to bf16, then times the bf16 weight, rounded again. The
-    reference's MLX kernel is not available here: this order of roundings
-    is this build's reading of it (unpinned)."""
+    input (`gemma4_text.py:171`): the mean of the squares summed exactly
+    (float64 over bf16 squares, each exact) and rounded once to float32,
+    r = 1 / sqrt(ms + eps) in float32, the normalised value rounded to bf16,
+    then times the bf16 weight, rounded again. The reference's MLX kernel is
+    not available here: this order of roundings is this build's reading of
+    it (unpinned)."""
     xf = np.asarray(x, np.float32)
-    ms = (xf * xf).mean(axis=-1, keepdims=True, dtype=np.float32)
+    xd = xf.astype(np.float64)
+    ms = ((xd * xd).sum(axis=-1, keepdims=True) / xf.shape[-1]).astype(np.float32)
     inv = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
     return bf16(bf16(xf * inv).astype(np.float32) * np.asarray(w, np.float32))
 

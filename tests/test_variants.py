@@ -75,9 +75,26 @@ def test_oracle_rms_norm_matches_torch():
     xt = torch.from_numpy(x)
     inv = torch.rsqrt(xt.pow(2).mean(-1, keepdim=True) + 1e-6)
     ref = ((xt * inv).to(torch.bfloat16).float() * torch.from_numpy(w)).to(torch.bfloat16).float().numpy()
-    # float32 rsqrt against numpy's 1/sqrt: the rare bf16 tie may land apart
+    # float32 rsqrt and a float32 mean against the exact mean and 1/sqrt:
+    # the rare bf16 tie may land apart
     assert (ours != ref).mean() < 1e-3
     assert np.all(np.abs(ours - ref) <= np.abs(ref) * 2.0 ** -7)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H", [256, 2816, 4096])
+def test_router_rms_norm_is_bit_exact(H):
+    """`vqmoe_rms_norm` (Gemma-4's router input) against the oracle's
+    restatement, bit for bit: the exact mean of the squares rounded once,
+    IEEE square root and division, two bf16 roundings."""
+    from knurlogic_b200.gemma4 import Router
+    g = np.random.default_rng(H)
+    x = torch.from_numpy(R.bf16(g.normal(0, 2, (37, H)).astype(np.float32))).to(torch.bfloat16)
+    scale = torch.from_numpy(g.uniform(0.5, 1.5, H).astype(np.float32))
+    r = Router(torch.zeros(4, H).to(DEV), scale.to(DEV), torch.ones(4).to(DEV), 2)
+    got = to_np(r.normalize(x.to(DEV)))
+    ref = R.rms_norm(x.float().numpy(), r.norm_weight.float().cpu().numpy(), r.eps)
+    assert np.array_equal(got, ref), f"{int((got != ref).sum())} of {ref.size} differ"
 
 
 def test_moe_experts_arguments_are_checked():
