@@ -72,16 +72,25 @@ typedef enum {
 /* Weight formats of one switch (expert) linear. */
 enum {
     VQMOE_FMT_DENSE_BF16 = 0,    /* weight [E, OUT, IN] bf16 (SwitchLinear) */
-    VQMOE_FMT_VQ_U8 = 1          /* codes and scales in the device layout
+    VQMOE_FMT_VQ_U8 = 1,         /* codes and scales in the device layout
                                     (vqmoe_prepare_vq); codebook [K, dim] fp16
                                     (the reference's, shared by all experts) */
+    VQMOE_FMT_VQ_REF = 2         /* codes and scales in the reference layout
+                                    (deepseek_v4.py:111-130): codes [E, OUT,
+                                    IN/dim], one code per entry, uint8 when
+                                    K <= 256, uint16 above; vq_scales [E, OUT,
+                                    IN/group]; codebook [K, dim] fp16 with dim
+                                    2, 4 or 8, K <= 65536 (the wider formats
+                                    the tiled fast path does not take) */
 };
 
 /* One switch linear: y[r] = x[r] @ W[expert(r)]^T, W [E, OUT, IN].
  * Mirrors VQSwitchLinear(codes, codebook, vq_scales, group_size=,
- * pack_bits=0) (deepseek_v4.py:126-130). Supported VQ: dim 4, K <= 256,
- * group_size 64, IN % 64 == 0, OUT % 16 == 0. Dense: IN % 16 == 0,
- * OUT % 16 == 0. Pointers 16-byte aligned. */
+ * pack_bits=0) (deepseek_v4.py:126-130). VQ_U8: dim 4, K <= 256,
+ * group_size 64, IN % 64 == 0, OUT % 16 == 0. VQ_REF: dim 2, 4 or 8,
+ * K <= 65536, group_size a multiple of dim dividing IN, IN % 64 == 0,
+ * OUT % 16 == 0; a SwitchGLU's three linears are all VQ_REF or none is.
+ * Dense: IN % 16 == 0, OUT % 16 == 0. Pointers 16-byte aligned. */
 typedef struct {
     int32_t format;
     int32_t num_experts;
@@ -308,6 +317,12 @@ VQMOE_API vqmoe_status vqmoe_unprepare_codes(const uint8_t *codes_dev,
 /* *bad_count (device uint32, zeroed by the caller) += the number of codes
  * >= codebook_size among codes[0, count). A loader calls it once; the
  * kernels trust the codes. */
+VQMOE_API vqmoe_status vqmoe_count_bad_codes_u16(const uint16_t *codes,
+                                                 int64_t count,
+                                                 int32_t codebook_size,
+                                                 uint32_t *bad_count,
+                                                 void *stream);
+/* The same over uint8 codes. */
 VQMOE_API vqmoe_status vqmoe_count_bad_codes(const uint8_t *codes,
                                              int64_t count,
                                              int32_t codebook_size,

@@ -16,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libvqmoe.so"
 
 FMT_DENSE_BF16 = 0
 FMT_VQ_U8 = 1
+FMT_VQ_REF = 2          # reference-layout codes (uint8 / uint16), dim 2, 4 or 8
 OUT_BF16 = 0
 OUT_F32 = 1
 ACT_SWIGLU = 0          # vqmoe_linear.activation of a SwitchGLU's gate linear
@@ -94,6 +95,8 @@ SIGNATURES = [
     ("vqmoe_prepare_vq", c_int32,
      [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     ("vqmoe_count_bad_codes", c_int32,
+     [c_void_p, c_int64, c_int32, c_void_p, c_void_p]),
+    ("vqmoe_count_bad_codes_u16", c_int32,
      [c_void_p, c_int64, c_int32, c_void_p, c_void_p]),
     ("vqmoe_unprepare_codes", c_int32,
      [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),

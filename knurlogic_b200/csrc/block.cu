@@ -141,6 +141,21 @@ static vqmoe_status check_linear(const vqmoe_linear *w, const char *name) {
             return set_error(VQMOE_BAD_POINTER, "%s: weight null or not 16-byte aligned", name);
         return VQMOE_OK;
     }
+    if (w->format == VQMOE_FMT_VQ_REF) {
+        if ((w->dim != 2 && w->dim != 4 && w->dim != 8) || w->codebook_size <= 0 || w->codebook_size > 65536)
+            return set_error(VQMOE_BAD_FORMAT, "%s: VQ dim %d / K %d unsupported (dim 2, 4 or 8; K <= 65536)",
+                             name, w->dim, w->codebook_size);
+        if (w->group_size <= 0 || w->group_size % w->dim || w->in_features % w->group_size)
+            return set_error(VQMOE_BAD_FORMAT, "%s: VQ group_size %d (a multiple of dim %d dividing in %d)",
+                             name, w->group_size, w->dim, w->in_features);
+        if (w->in_features % 64)
+            return set_error(VQMOE_BAD_SHAPE, "%s: in_features %d is not a multiple of 64", name,
+                             w->in_features);
+        if (!w->codes || !w->codebook || !w->scales || !aligned16(w->codes) || !aligned16(w->codebook) ||
+            !aligned16(w->scales))
+            return set_error(VQMOE_BAD_POINTER, "%s: codes/codebook/scales null or not 16-byte aligned", name);
+        return VQMOE_OK;
+    }
     if (w->format != VQMOE_FMT_VQ_U8)
         return set_error(VQMOE_BAD_FORMAT, "%s: unknown format %d", name, w->format);
     if (w->dim != 4 || w->codebook_size <= 0 || w->codebook_size > 256)
@@ -160,6 +175,14 @@ static vqmoe_status check_linear(const vqmoe_linear *w, const char *name) {
 }
 
 static bool aligned_ptr(const void *p) { return p && aligned16(p); }
+
+// a SwitchGLU's linears are all in the reference VQ layout or none is
+static vqmoe_status check_glu_formats(const vqmoe_linear *g, const vqmoe_linear *u, const vqmoe_linear *d) {
+    const int n = (g->format == VQMOE_FMT_VQ_REF) + (u->format == VQMOE_FMT_VQ_REF) + (d->format == VQMOE_FMT_VQ_REF);
+    if (n != 0 && n != 3)
+        return set_error(VQMOE_BAD_FORMAT, "gate/up/down: reference-layout VQ on some linears but not all");
+    return VQMOE_OK;
+}
 
 // workspace carving: each region 256-byte aligned
 struct Carve {
@@ -241,7 +264,7 @@ static BlockWs carve_block(void *ws, const vqmoe_block *b, int T) {
     w.inds = c.take<int32_t>(P);
     w.scores = c.take<float>(P);
     w.sgate = c.take<float>(T);
-    w.x16 = b->gate.format == VQMOE_FMT_VQ_U8 ? c.take<uint16_t>((size_t)T * H) : nullptr;
+    w.x16 = is_vq(b->gate.format) ? c.take<uint16_t>((size_t)T * H) : nullptr;
     carve_route(c, w.rt, E, P, H, T, Is);
     w.act = c.take<uint16_t>((size_t)P * I);
     w.act_s = c.take<uint16_t>((size_t)T * Is);
@@ -293,6 +316,7 @@ static vqmoe_status check_block(const vqmoe_block *b, int T) {
                              "switch_mlp shapes: gate/up must be [E=%d, I, H=%d], down [E, H, I]", E, H);
     if (b->gate.format != b->up.format)
         return set_error(VQMOE_BAD_FORMAT, "gate_proj and up_proj formats differ");
+    if ((s = check_glu_formats(&b->gate, &b->up, &b->down)) != VQMOE_OK) return s;
     if ((s = check_glu_activation(&b->gate)) != VQMOE_OK) return s;
     if (b->router_mode < VQMOE_ROUTER_SOFTMAX_TOPK_RENORM || b->router_mode > VQMOE_ROUTER_SOFTMAX_TOPK)
         return set_error(VQMOE_BAD_FORMAT, "router_mode %d (0..2)", b->router_mode);
@@ -393,8 +417,8 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                               cudaStream_t st, cudaEvent_t *ev = nullptr, int n_ev = 0) {
     const int H = b->hidden, E = b->num_experts, k = b->top_k, P = T * k;
     const bool shared = b->shared_inter > 0;
-    const bool vq_in = b->gate.format == VQMOE_FMT_VQ_U8;
-    const bool vq_dn = b->down.format == VQMOE_FMT_VQ_U8;
+    const bool vq_in = is_vq(b->gate.format);
+    const bool vq_dn = is_vq(b->down.format);
     vqmoe_status s;
     if ((s = mark(ev, n_ev, 0, st)) != VQMOE_OK) return s;
     SideStream *side = nullptr;
@@ -449,7 +473,7 @@ static GluWs carve_glu(void *ws, const vqmoe_linear *first, const vqmoe_linear *
     const int E = first->num_experts, P = T * k;
     const bool dual = down != nullptr;
     w.status = c.take<uint32_t>(kStatusBytes / sizeof(uint32_t));
-    w.x16 = first->format == VQMOE_FMT_VQ_U8 ? c.take<uint16_t>((size_t)rows_x * first->in_features)
+    w.x16 = is_vq(first->format) ? c.take<uint16_t>((size_t)rows_x * first->in_features)
                                              : nullptr;
     const int H = first->in_features, I = first->out_features;
     carve_route(c, w.rt, E, P, H, T, 0);
@@ -593,6 +617,7 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
         down->in_features != I || up->num_experts != E || down->num_experts != E ||
         gate->format != up->format)
         return set_error(VQMOE_BAD_SHAPE, "switch_glu: inconsistent gate/up/down shapes");
+    if ((s = check_glu_formats(gate, up, down)) != VQMOE_OK) return s;
     if (E > 1024) return set_error(VQMOE_BAD_SHAPE, "switch_glu: %d experts (<= 1024)", E);
     if (!aligned_ptr(x) || !aligned_ptr(y) || !indices || !aligned_ptr(workspace))
         return set_error(VQMOE_BAD_POINTER, "x / indices / y / workspace");
@@ -602,7 +627,7 @@ vqmoe_status vqmoe_switch_glu(const vqmoe_linear *gate, const vqmoe_linear *up,
         return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, w.bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((s = clear_status(w.status, st)) != VQMOE_OK) return s;
-    const bool vq_in = gate->format == VQMOE_FMT_VQ_U8, vq_dn = down->format == VQMOE_FMT_VQ_U8;
+    const bool vq_in = is_vq(gate->format), vq_dn = is_vq(down->format);
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
         const int T = std::min(chunk, tokens - t0), P = T * top_k;
         const int32_t *ind = indices + (size_t)t0 * top_k;
@@ -652,6 +677,7 @@ vqmoe_status vqmoe_moe_experts(const vqmoe_linear *gate, const vqmoe_linear *up,
         down->in_features != I || up->num_experts != E || down->num_experts != E ||
         gate->format != up->format)
         return set_error(VQMOE_BAD_SHAPE, "moe_experts: inconsistent gate/up/down shapes");
+    if ((s = check_glu_formats(gate, up, down)) != VQMOE_OK) return s;
     if (E > 1024) return set_error(VQMOE_BAD_SHAPE, "moe_experts: %d experts (<= 1024)", E);
     if (!aligned_ptr(x) || !aligned_ptr(out) || !indices || !scores || !aligned_ptr(workspace))
         return set_error(VQMOE_BAD_POINTER, "x / indices / scores / out / workspace");
@@ -663,7 +689,7 @@ vqmoe_status vqmoe_moe_experts(const vqmoe_linear *gate, const vqmoe_linear *up,
     uint16_t *ybuf = reinterpret_cast<uint16_t *>(static_cast<char *>(workspace) + moe_experts_ybuf_offset(w));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((s = clear_status(w.status, st)) != VQMOE_OK) return s;
-    const bool vq_in = gate->format == VQMOE_FMT_VQ_U8, vq_dn = down->format == VQMOE_FMT_VQ_U8;
+    const bool vq_in = is_vq(gate->format), vq_dn = is_vq(down->format);
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
         const int T = std::min(chunk, tokens - t0), P = T * top_k;
         const int32_t *ind = indices + (size_t)t0 * top_k;
@@ -704,7 +730,7 @@ vqmoe_status vqmoe_switch_linear(const vqmoe_linear *w, const void *x, int32_t x
         return set_error(VQMOE_WORKSPACE_TOO_SMALL, "workspace %zu < %zu bytes", workspace_bytes, ws.bytes);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((s = clear_status(ws.status, st)) != VQMOE_OK) return s;
-    const bool vq = w->format == VQMOE_FMT_VQ_U8;
+    const bool vq = is_vq(w->format);
     const int IN = w->in_features, E = w->num_experts;
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
         const int T = std::min(chunk, tokens - t0), P = T * top_k;

@@ -195,6 +195,8 @@ constexpr size_t kStatusBytes = 256;
 constexpr uint32_t kWaitDependency = 1;   // a phase 2 tile's wait for its expert's phase 1 tiles
 constexpr uint32_t kWaitPipeline = 2;     // an mbarrier wait inside a tcgen05 pipeline
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+// a VQ weight format (codebook + codes + scales), either layout
+inline bool is_vq(int format) { return format == VQMOE_FMT_VQ_U8 || format == VQMOE_FMT_VQ_REF; }
 inline bool aligned16(const void *p) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }

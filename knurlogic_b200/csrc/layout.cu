@@ -94,6 +94,39 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ dcodes, const uint16_
     }
 }
 
+// The same over uint16 codes
+__global__ void count_bad_codes_u16_kernel(const uint16_t *__restrict__ codes, long long n, int K,
+                                           uint32_t *__restrict__ bad_count) {
+    uint32_t bad = 0;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        bad += codes[i] >= K;
+    for (int o = 16; o > 0; o >>= 1) bad += __shfl_xor_sync(0xffffffffu, bad, o);
+    if ((threadIdx.x & 31) == 0 && bad) atomicAdd(bad_count, bad);
+}
+
+// Reference-layout VQ (codes [E][OUT][IN/dim], 1 or 2 bytes per code;
+// scales [E][OUT][IN/group]): W = fp16(codebook[code][j] * scale) for
+// experts [first, first + count), one code (dim weights) per thread.
+__global__ void dequant_ref_kernel(const uint8_t *__restrict__ codes, int cbytes, const uint16_t *__restrict__ cb,
+                                   const uint16_t *__restrict__ scales, int OUT, int IN, int dim, int group,
+                                   int first, int count, uint16_t *__restrict__ out) {
+    const int NC = IN / dim, NG = IN / group;
+    const long long n = (long long)count * OUT * NC;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int u = (int)(i % NC);
+        const long long er = i / NC;
+        const long long src = (long long)first * OUT * NC + i;
+        const uint32_t code = cbytes == 1 ? (uint32_t)codes[src] : (uint32_t)reinterpret_cast<const uint16_t *>(codes)[src];
+        const uint32_t s = scales[((long long)first * OUT + er) * NG + (u * dim) / group];
+        const uint32_t s2 = s | (s << 16);
+        const uint32_t *e = reinterpret_cast<const uint32_t *>(cb + (size_t)code * dim);
+        uint32_t *o = reinterpret_cast<uint32_t *>(out + er * IN + (long long)u * dim);
+        for (int j = 0; j < dim / 2; ++j) o[j] = hmul2_u32(e[j], s2);
+    }
+}
+
 static int grid_for(long long n) {
     return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)sm_count() * 16));
 }
@@ -157,8 +190,36 @@ vqmoe_status vqmoe_count_bad_codes(const uint8_t *codes, int64_t count, int32_t 
     return check_launch("count_bad_codes_kernel");
 }
 
+vqmoe_status vqmoe_count_bad_codes_u16(const uint16_t *codes, int64_t count, int32_t codebook_size,
+                                       uint32_t *bad_count, void *stream) {
+    if (!codes || !bad_count || count <= 0)
+        return set_error(VQMOE_BAD_POINTER, "count_bad_codes_u16: pointers / count");
+    if (codebook_size <= 0 || codebook_size > 65536)
+        return set_error(VQMOE_BAD_FORMAT, "codebook_size %d (1..65536)", codebook_size);
+    count_bad_codes_u16_kernel<<<grid_for(count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        codes, count, codebook_size, bad_count);
+    return check_launch("count_bad_codes_u16_kernel");
+}
+
 vqmoe_status vqmoe_dequant(const vqmoe_linear *w, int32_t first, int32_t count, void *out,
                            void *stream) {
+    if (w && w->format == VQMOE_FMT_VQ_REF) {
+        if (w->num_experts <= 0 || w->out_features <= 0 || w->in_features <= 0 ||
+            (w->dim != 2 && w->dim != 4 && w->dim != 8) || w->group_size <= 0 || w->group_size % w->dim ||
+            w->in_features % w->group_size || w->codebook_size <= 0 || w->codebook_size > 65536)
+            return set_error(VQMOE_BAD_FORMAT, "dequant: reference-layout VQ geometry");
+        if (first < 0 || count <= 0 || first + count > w->num_experts)
+            return set_error(VQMOE_BAD_SHAPE, "dequant: experts [%d, %d) of %d", first, first + count,
+                             w->num_experts);
+        if (!w->codes || !w->codebook || !w->scales || !aligned16(out) || !aligned16(w->codebook))
+            return set_error(VQMOE_BAD_POINTER, "dequant: pointers");
+        const long long n = (long long)count * w->out_features * (w->in_features / w->dim);
+        dequant_ref_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const uint8_t *>(w->codes), w->codebook_size <= 256 ? 1 : 2,
+            static_cast<const uint16_t *>(w->codebook), static_cast<const uint16_t *>(w->scales), w->out_features,
+            w->in_features, w->dim, w->group_size, first, count, static_cast<uint16_t *>(out));
+        return check_launch("dequant_ref_kernel");
+    }
     if (!w || w->format != VQMOE_FMT_VQ_U8) return set_error(VQMOE_BAD_FORMAT, "dequant: not a VQ linear");
     vqmoe_status s = check_geom(w->num_experts, w->out_features, w->in_features);
     if (s != VQMOE_OK) return s;

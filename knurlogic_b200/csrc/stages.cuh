@@ -52,6 +52,10 @@ inline int expert_ctl_words(int E) { return 2 + E; }
 vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,
                             const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl, uint32_t *err,
                             uint32_t wait_polls, cudaStream_t stream, cudaEvent_t after_permute = nullptr);
+// The routed experts with reference-layout VQ weights (VQMOE_FMT_VQ_REF):
+// phase 1 (r1, may be null) then phase 2, two launches.
+vqmoe_status launch_experts_ref(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,
+                                const vqmoe_linear *w2, const RoutedIO &r2, cudaStream_t stream);
 // The shared expert's dense matmul (+ SwiGLU when w1 is set): K slicing,
 // its partial buffer [ks][T][nmat][OUT] float and [ceil(OUT/32)] semaphores.
 void plan_shared_dense(int IN, int OUT, int nmat, int *ks, int *kslice, size_t *smem);

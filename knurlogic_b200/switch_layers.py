@@ -141,19 +141,23 @@ class SwitchLinear(_SwitchBase):
 
 
 class VQSwitchLinear(_SwitchBase):
-    """VQ experts: codes [E, OUT, IN/dim] uint8 (one code per entry),
-    codebook [K, dim] fp16 (shared by all experts, never split), vq_scales
-    [E, OUT, IN/group] fp16.
+    """VQ experts: codes [E, OUT, IN/dim] with one code per entry (uint8
+    when K <= 256, uint16 above: `deepseek_v4.py:111-121`), codebook
+    [K, dim] fp16 with dim 2, 4 or 8 (shared by all experts, never split),
+    vq_scales [E, OUT, IN/group] fp16.
 
     Weight of expert e, row o, input i (the dequantisation this build
     defines; the reference runtime is absent):
         W = fp16(codebook[codes[e, o, i // dim], i % dim] * vq_scales[e, o, i // group])
     and the activations enter the matmul as fp16.
 
-    `codes` and `vq_scales` stay in the reference layout; the kernels read a
-    tiled copy (`vqmoe_prepare_vq`) made on the module's device at first use.
-    Packed codes (`pack_bits` > 0, uint32 words of ceil(log2 K)-bit fields)
-    are rejected: their bit order is not pinned by the reference."""
+    `codes` and `vq_scales` stay in the reference layout. uint8 codes of a
+    dim-4 codebook with 64-input groups take the fast path: the kernels read
+    a tiled copy (`vqmoe_prepare_vq`) made on the module's device at first
+    use. Every other format (dim 2 or 8, K up to 65536, other group sizes)
+    runs on the reference layout itself (`VQMOE_FMT_VQ_REF`). Packed codes
+    (`pack_bits` > 0, uint32 words of ceil(log2 K)-bit fields) are rejected:
+    their bit order is not pinned by the reference."""
 
     def __init__(self, codes: torch.Tensor, codebook: torch.Tensor,
                  vq_scales: torch.Tensor, *, group_size: int, pack_bits: int = 0,
@@ -180,9 +184,17 @@ class VQSwitchLinear(_SwitchBase):
         if ngrp <= 0 or IN % ngrp or IN // ngrp != int(group_size):
             raise ValueError(f"in={IN} does not divide into {ngrp} scale groups "
                              f"of {group_size}")
-        if codes.dtype != torch.uint8 or K > 256:
-            raise ValueError(f"codes must be uint8 with K <= 256 (got {codes.dtype}, K={K})")
+        want = torch.uint8 if K <= 256 else torch.uint16
+        if K > 65536 or codes.dtype != want:
+            raise ValueError(f"codes for K={K} must be {want} with one code per entry "
+                             f"(K <= 65536), got {codes.dtype}")
+        if dim not in (2, 4, 8):
+            raise ValueError(f"VQ dim {dim} is not supported (2, 4 or 8)")
+        if int(group_size) % dim:
+            raise ValueError(f"group_size {group_size} is not a multiple of dim {dim}")
         self.group_size = int(group_size)
+        # the tiled fast path, or the reference layout as it is
+        self.fast = K <= 256 and dim == 4 and self.group_size == 64
         self.pack_bits = 0
         self._k_expect = K
         self.register_buffer("codes", codes.contiguous(), persistent=True)
@@ -203,10 +215,11 @@ class VQSwitchLinear(_SwitchBase):
         return self.codes.shape[2] * self.codebook.shape[1]
 
     def prepared(self):
-        """(codes, scales) in the device layout the kernels read (tiles of
-        32 rows x 256 inputs, `vqmoe_prepare_vq`), made once per device and
-        weight version. Checks every code against the codebook size (one
-        host synchronisation, at first use: call it before capturing a
+        """(codes, scales) as the kernels read them: on the fast path the
+        tiled device layout (tiles of 32 rows x 256 inputs,
+        `vqmoe_prepare_vq`), made once per device and weight version; else
+        the module's own tensors. Checks every code against the codebook size
+        (one host synchronisation, at first use: call it before capturing a
         CUDA graph)."""
         c, vs = self.codes, self.vq_scales
         require_cuda(c, vs)
@@ -214,14 +227,15 @@ class VQSwitchLinear(_SwitchBase):
         if self._dev is None or self._dev[0] != key:
             E, OUT, W = c.shape
             K, dim = (int(n) for n in self.codebook.shape)
-            if dim != 4:
-                raise NotImplementedError(f"VQ dim {dim} is not supported (dim 4)")
             bad = torch.zeros(1, dtype=torch.int32, device=c.device)
-            _lib.call("vqmoe_count_bad_codes", c.data_ptr(), c.numel(), K,
-                      bad.data_ptr(), _stream(c))
+            _lib.call("vqmoe_count_bad_codes" if c.dtype == torch.uint8 else "vqmoe_count_bad_codes_u16",
+                      c.data_ptr(), c.numel(), K, bad.data_ptr(), _stream(c))
             n_bad = int(bad.item())
             if n_bad:
                 raise ValueError(f"{n_bad} VQ codes are >= the codebook size {K}")
+            if not self.fast:
+                self._dev = (key, c, vs)
+                return c, vs
             IN = W * dim
             nc, ns = _lib.vq_layout_bytes(E, OUT, IN)
             dc = torch.empty(nc, dtype=torch.uint8, device=c.device)
@@ -234,7 +248,8 @@ class VQSwitchLinear(_SwitchBase):
     def descriptor(self) -> _lib.Linear:
         dc, ds = self.prepared()
         require_cuda(self.codebook)
-        return _lib.Linear(format=_lib.FMT_VQ_U8, num_experts=self.num_experts,
+        return _lib.Linear(format=_lib.FMT_VQ_U8 if self.fast else _lib.FMT_VQ_REF,
+                           num_experts=self.num_experts,
                            out_features=self.output_dims,
                            in_features=self.input_dims, codes=dc.data_ptr(),
                            codebook=self.codebook.data_ptr(),

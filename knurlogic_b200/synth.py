@@ -14,11 +14,13 @@ c3  c2's layer at 4096 prefill tokens, router logits biased so expert
 c4  256 experts, top-8, H 4096, I 1536, 256 tokens (the tensor-split
     configuration's MoE layer), router N(0, 0.02)
 
-Every VQ matrix: uint8 codes U[0, 256), its own 256 x 4 fp16 codebook
-N(0, 0.02), vq_scales [E, OUT, IN/64] fp16 -- 1.0 ("ones", the 2-bit
-headline; the kernel still reads them) or 0.5 + U(0, 1) ("random", the
-numerics tests). Activations N(0, 1) rounded to bf16. Shared expert and
-its gate bf16 N(0, 0.02).
+Every VQ matrix: codes U[0, K) (uint8 for K <= 256, else uint16), its own
+K x dim fp16 codebook N(0, 0.02) (K 256, dim 4 unless the configuration
+names others: the reference's VQ fixture is K 2048, dim 2, group 64),
+vq_scales [E, OUT, IN/group] fp16 -- 1.0 ("ones", the 2-bit headline; the
+kernel still reads them) or 0.5 + U(0, 1) ("random", the numerics tests).
+Activations N(0, 1) rounded to bf16. Shared expert and its gate bf16
+N(0, 0.02).
 """
 from __future__ import annotations
 
@@ -93,8 +95,12 @@ def make_weights(cfg: MoEConfig, seed: int = 0, device="cpu",
     w[prefix + "gate.weight"] = r.to(torch.bfloat16)
     for name, out, inp in (("gate_proj", I, H), ("up_proj", I, H), ("down_proj", H, I)):
         q = f"{prefix}switch_mlp.{name}."
-        w[q + "codes"] = torch.randint(0, cfg.codebook_size, (E, out, inp // cfg.dim),
-                                       generator=g, device=device, dtype=torch.uint8)
+        if cfg.codebook_size <= 256:
+            w[q + "codes"] = torch.randint(0, cfg.codebook_size, (E, out, inp // cfg.dim),
+                                           generator=g, device=device, dtype=torch.uint8)
+        else:
+            w[q + "codes"] = torch.randint(0, cfg.codebook_size, (E, out, inp // cfg.dim), generator=g,
+                                           device=device, dtype=torch.int32).to(torch.uint16)
         w[q + "codebook"] = _normal((cfg.codebook_size, cfg.dim), 0.02, g, device,
                                     torch.float16)
         ng = inp // cfg.group
@@ -129,7 +135,8 @@ def algorithmic_bytes(cfg: MoEConfig, distinct_experts: int, tokens: int | None 
     the router weight, the activations in and out."""
     T = cfg.tokens if tokens is None else tokens
     H, I = cfg.hidden, cfg.inter
-    per = 3 * H * I // cfg.dim
+    code_bytes = 1 if cfg.codebook_size <= 256 else 2
+    per = 3 * H * I // cfg.dim * code_bytes
     if with_scales:
         per += 3 * 2 * H * I // cfg.group
     b = distinct_experts * per + 3 * cfg.codebook_size * cfg.dim * 2

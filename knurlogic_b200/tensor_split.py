@@ -71,8 +71,10 @@ def refusals(shapes: dict, n: int, prefix: str = "mlp.") -> list:
             out.append(f"{name}: {shape[ax]} {unit} do not divide by {n}")
             continue
         part = shape[ax] // n
-        if leaf == "codes" and kind == S2A and (part * 4) % 64:
-            out.append(f"{name}: a rank's {part * 4} inputs are not a multiple "
+        # the codebook's dim turns a rank's codes into inputs (4 unless named)
+        dim = tuple(shapes.get(name[:-len("codes")] + "codebook", (0, 4)))[-1] if leaf == "codes" else 4
+        if leaf == "codes" and kind == S2A and (part * dim) % 64:
+            out.append(f"{name}: a rank's {part * dim} inputs are not a multiple "
                        f"of 64 (whole scale groups and 256-input code chunks)")
         if leaf in ("codes", "vq_scales", "weight") and kind == A2S and part % 16:
             out.append(f"{name}: a rank's {part} output rows are not a multiple of 16")
