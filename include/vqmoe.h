@@ -48,8 +48,10 @@ extern "C" {
 /* 2: vqmoe_linear.activation (was reserved), vqmoe_block.router_mode and
  * its trailing reserved word, vqmoe_router_ex, vqmoe_moe_experts.
  * 3: vqmoe_block.wait_polls (was reserved), vqmoe_workspace_status; every
- * workspace starts with VQMOE_STATUS_BYTES of status words. */
-#define VQMOE_ABI_VERSION 3
+ * workspace starts with VQMOE_STATUS_BYTES of status words.
+ * 4: vqmoe_linear.biases / .bits / .reserved (affine-quantized experts,
+ * VQMOE_FMT_AFFINE). */
+#define VQMOE_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define VQMOE_API __attribute__((visibility("default")))
@@ -75,13 +77,22 @@ enum {
     VQMOE_FMT_VQ_U8 = 1,         /* codes and scales in the device layout
                                     (vqmoe_prepare_vq); codebook [K, dim] fp16
                                     (the reference's, shared by all experts) */
-    VQMOE_FMT_VQ_REF = 2         /* codes and scales in the reference layout
+    VQMOE_FMT_VQ_REF = 2,        /* codes and scales in the reference layout
                                     (deepseek_v4.py:111-130): codes [E, OUT,
                                     IN/dim], one code per entry, uint8 when
                                     K <= 256, uint16 above; vq_scales [E, OUT,
                                     IN/group]; codebook [K, dim] fp16 with dim
                                     2, 4 or 8, K <= 65536 (the wider formats
                                     the tiled fast path does not take) */
+    VQMOE_FMT_AFFINE = 3         /* affine-quantized experts, mlx-lm's
+                                    QuantizedSwitchLinear (switch_layers.py:
+                                    24-86, mx.gather_qmm mode "affine"):
+                                    weight [E, OUT, IN*bits/32] uint32, each row
+                                    a little-endian bit stream of `bits`-bit
+                                    values q (element j at bits [j*bits,
+                                    (j+1)*bits)); scales and biases [E, OUT,
+                                    IN/group] bf16; W = bf16(fmaf(scale, q,
+                                    bias)); activations stay bf16 */
 };
 
 /* One switch linear: y[r] = x[r] @ W[expert(r)]^T, W [E, OUT, IN].
@@ -89,7 +100,9 @@ enum {
  * pack_bits=0) (deepseek_v4.py:126-130). VQ_U8: dim 4, K <= 256,
  * group_size 64, IN % 64 == 0, OUT % 16 == 0. VQ_REF: dim 2, 4 or 8,
  * K <= 65536, group_size a multiple of dim dividing IN, IN % 64 == 0,
- * OUT % 16 == 0; a SwitchGLU's three linears are all VQ_REF or none is.
+ * OUT % 16 == 0. AFFINE (QuantizedSwitchLinear): bits 2, 3, 4, 5, 6 or 8,
+ * group_size 32, 64 or 128, IN % 64 == 0, OUT % 16 == 0. A SwitchGLU's
+ * three linears share one of VQ_REF and AFFINE, or use neither.
  * Dense: IN % 16 == 0, OUT % 16 == 0. Pointers 16-byte aligned. */
 typedef struct {
     int32_t format;
@@ -105,6 +118,9 @@ typedef struct {
     int32_t group_size;          /* inputs per vq_scales entry */
     int32_t activation;          /* on the gate linear of a SwitchGLU: VQMOE_ACT_*;
                                     0 elsewhere */
+    const void *biases;          /* AFFINE: [E, OUT, IN/group] bf16 */
+    int32_t bits;                /* AFFINE: 2, 3, 4, 5, 6 or 8 */
+    int32_t reserved;            /* 0 */
 } vqmoe_linear;
 
 /* Activation between the gate and up projections of a SwitchGLU, set on its
@@ -280,8 +296,9 @@ VQMOE_API vqmoe_status vqmoe_moe_experts(const vqmoe_linear *gate,
                           void *out, void *workspace, size_t workspace_bytes,
                           void *stream);
 
-/* Dense fp16 weights of experts [first, first + count): out [count, OUT, IN]
- * fp16, W = fp16(codebook[code][j] * scale). */
+/* Dense weights of experts [first, first + count): out [count, OUT, IN],
+ * fp16 W = fp16(codebook[code][j] * scale) for the VQ formats, bf16 W =
+ * bf16(fmaf(scale, q, bias)) for AFFINE. */
 VQMOE_API vqmoe_status vqmoe_dequant(const vqmoe_linear *w, int32_t first,
                                      int32_t count, void *out, void *stream);
 

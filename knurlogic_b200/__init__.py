@@ -5,9 +5,10 @@ Drop-in modules with the reference's interface (`VQSwitchLinear`,
 sm_100a CUDA behind a C ABI (include/vqmoe.h). Tensor parallelism follows
 the reference's split rules (`tensor_split`).
 """
-from .switch_layers import GeGLU, SwiGLU, SwitchGLU, SwitchLinear, VQSwitchLinear  # noqa: F401
+from .switch_layers import (GeGLU, QuantizedSwitchLinear, SwiGLU, SwitchGLU, SwitchLinear,  # noqa: F401
+                            VQSwitchLinear)
 from .moe import CapturedBlock, SharedExpert, SparseMoeBlock  # noqa: F401
 from . import gemma4  # noqa: F401
 
-__all__ = ["SwitchGLU", "SwitchLinear", "VQSwitchLinear", "SwiGLU", "GeGLU", "SharedExpert", "CapturedBlock",
-           "SparseMoeBlock"]
+__all__ = ["SwitchGLU", "SwitchLinear", "VQSwitchLinear", "QuantizedSwitchLinear", "SwiGLU", "GeGLU",
+           "SharedExpert", "CapturedBlock", "SparseMoeBlock"]

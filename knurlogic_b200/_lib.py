@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libvqmoe.so"
 FMT_DENSE_BF16 = 0
 FMT_VQ_U8 = 1
 FMT_VQ_REF = 2          # reference-layout codes (uint8 / uint16), dim 2, 4 or 8
+FMT_AFFINE = 3          # affine-quantized (QuantizedSwitchLinear): packed q, scales, biases
 OUT_BF16 = 0
 OUT_F32 = 1
 ACT_SWIGLU = 0          # vqmoe_linear.activation of a SwitchGLU's gate linear
@@ -37,7 +38,8 @@ class Linear(Structure):
                 ("weight", c_void_p), ("codes", c_void_p),
                 ("codebook", c_void_p), ("scales", c_void_p),
                 ("codebook_size", c_int32), ("dim", c_int32),
-                ("group_size", c_int32), ("activation", c_int32)]
+                ("group_size", c_int32), ("activation", c_int32),
+                ("biases", c_void_p), ("bits", c_int32), ("reserved", c_int32)]
 
 
 class Block(Structure):

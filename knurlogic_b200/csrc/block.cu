@@ -126,6 +126,8 @@ combine_kernel(const uint16_t *__restrict__ ybuf, int T, int k, int H,
 
 // ---------------------------------------------------------- validation
 
+static bool aligned_ptr(const void *p) { return p && aligned16(p); }
+
 static vqmoe_status check_linear(const vqmoe_linear *w, const char *name) {
     if (!w) return set_error(VQMOE_BAD_POINTER, "%s: null descriptor", name);
     if (w->num_experts <= 0 || w->out_features <= 0 || w->in_features <= 0)
@@ -139,6 +141,19 @@ static vqmoe_status check_linear(const vqmoe_linear *w, const char *name) {
                              w->in_features);
         if (!w->weight || !aligned16(w->weight))
             return set_error(VQMOE_BAD_POINTER, "%s: weight null or not 16-byte aligned", name);
+        return VQMOE_OK;
+    }
+    if (w->format == VQMOE_FMT_AFFINE) {
+        const int b = w->bits;
+        if (b != 2 && b != 3 && b != 4 && b != 5 && b != 6 && b != 8)
+            return set_error(VQMOE_BAD_FORMAT, "%s: affine bits %d (2, 3, 4, 5, 6 or 8)", name, b);
+        if (w->group_size != 32 && w->group_size != 64 && w->group_size != 128)
+            return set_error(VQMOE_BAD_FORMAT, "%s: affine group_size %d (32, 64 or 128)", name, w->group_size);
+        if (w->in_features % 64 || w->in_features % w->group_size)
+            return set_error(VQMOE_BAD_SHAPE, "%s: in_features %d (a multiple of 64 and of the group)", name,
+                             w->in_features);
+        if (!aligned_ptr(w->weight) || !aligned_ptr(w->scales) || !aligned_ptr(w->biases))
+            return set_error(VQMOE_BAD_POINTER, "%s: weight/scales/biases null or not 16-byte aligned", name);
         return VQMOE_OK;
     }
     if (w->format == VQMOE_FMT_VQ_REF) {
@@ -174,13 +189,13 @@ static vqmoe_status check_linear(const vqmoe_linear *w, const char *name) {
     return VQMOE_OK;
 }
 
-static bool aligned_ptr(const void *p) { return p && aligned16(p); }
-
-// a SwitchGLU's linears are all in the reference VQ layout or none is
+// a SwitchGLU's linears share one general-kernel format (reference-layout
+// VQ or affine) or use none
 static vqmoe_status check_glu_formats(const vqmoe_linear *g, const vqmoe_linear *u, const vqmoe_linear *d) {
-    const int n = (g->format == VQMOE_FMT_VQ_REF) + (u->format == VQMOE_FMT_VQ_REF) + (d->format == VQMOE_FMT_VQ_REF);
-    if (n != 0 && n != 3)
-        return set_error(VQMOE_BAD_FORMAT, "gate/up/down: reference-layout VQ on some linears but not all");
+    if ((is_general(g->format) || is_general(u->format) || is_general(d->format)) &&
+        (g->format != u->format || g->format != d->format))
+        return set_error(VQMOE_BAD_FORMAT,
+                         "gate/up/down: reference-layout VQ or affine on some linears but not all");
     return VQMOE_OK;
 }
 

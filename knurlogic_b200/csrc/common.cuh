@@ -197,6 +197,8 @@ constexpr uint32_t kWaitPipeline = 2;     // an mbarrier wait inside a tcgen05 p
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // a VQ weight format (codebook + codes + scales), either layout
 inline bool is_vq(int format) { return format == VQMOE_FMT_VQ_U8 || format == VQMOE_FMT_VQ_REF; }
+// a format the general (dequantise-into-shared-memory) expert kernel serves
+inline bool is_general(int format) { return format == VQMOE_FMT_VQ_REF || format == VQMOE_FMT_AFFINE; }
 inline bool aligned16(const void *p) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }

@@ -611,7 +611,7 @@ static RoutedSet set_of(const RoutedIO &r, const vqmoe_linear *w0, const vqmoe_l
 vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,
                             const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl, uint32_t *err,
                             uint32_t wait_polls, cudaStream_t stream, cudaEvent_t after_permute) {
-    if (w2->format == VQMOE_FMT_VQ_REF || (r1 && gate->format == VQMOE_FMT_VQ_REF)) {
+    if (is_general(w2->format) || (r1 && is_general(gate->format))) {
         if (after_permute && cudaEventRecord(after_permute, stream) != cudaSuccess) return check_launch("event");
         return launch_experts_ref(gate, up, r1, w2, r2, stream);
     }

@@ -18,6 +18,12 @@
 // matrix: K x dim up to 16384 values) and are read through L1 otherwise.
 // Phase 1 (gate and up, SwiGLU / GeGLU) and phase 2 (down, x the routing
 // weight) are two launches.
+//
+// The same kernel serves affine-quantized experts (VQMOE_FMT_AFFINE,
+// mlx-lm's QuantizedSwitchLinear, switch_layers.py:24-86): each row of the
+// packed uint32 weight is a little-endian bit stream of `bits`-bit values q,
+// dequantised as W = bf16(fmaf(scale, q, bias)) with its group's scale and
+// bias, and the bf16 activations enter a bf16 mma.sync as they are.
 #include <algorithm>
 
 #include "experts.cuh"
@@ -36,16 +42,17 @@ constexpr int kCbMax = 32768;             // shared-memory codebook budget per m
 constexpr int kTileBytes = kRows * kStride;
 
 struct Mat {
-    const uint8_t *codes;                 // [E][OUT][IN / dim], 1 or 2 bytes per code
+    const uint8_t *codes;                 // [E][OUT][IN / dim], 1 or 2 bytes per code; AFFINE: packed q words
     const uint16_t *cb;                   // [K][dim] fp16 bits
-    const uint16_t *scales;               // [E][OUT][IN / group] fp16 bits
-    int K, dim, group, cbytes;
+    const uint16_t *scales;               // [E][OUT][IN / group] fp16 bits (AFFINE: bf16)
+    const uint16_t *biases;               // AFFINE: [E][OUT][IN / group] bf16 bits
+    int K, dim, group, cbytes, bits;
 };
 
 struct Args {
     const int32_t *cnt, *off, *list, *active;
     int E, k, x_per_pair;
-    const uint16_t *x;                    // fp16 rows
+    const uint16_t *x;                    // fp16 rows (VQ), bf16 rows (AFFINE)
     int IN, OUT;
     uint16_t *out;                        // [P][OUT]
     int out_f16;
@@ -100,8 +107,41 @@ __device__ __forceinline__ void dequant_chunk(const Mat &m, const uint16_t *cb, 
     }
 }
 
+// AFFINE: rows [row0, row0 + 64) x inputs [i0, i0 + 256) of expert e,
+// W = bf16(fmaf(scale, q, bias)), 8 inputs (16 output bytes) per thread
+__device__ __forceinline__ void dequant_chunk_affine(const Mat &m, int e, int row0, int i0, int IN, int OUT,
+                                                     uint8_t *tile) {
+    const int words_row = IN * m.bits / 32, ngrp_row = IN / m.group;
+    const uint32_t mask = (1u << m.bits) - 1u;
+    const uint32_t *wq = reinterpret_cast<const uint32_t *>(m.codes);
+    for (int v = threadIdx.x; v < kRows * (kChunk / 8); v += kThreads) {
+        const int r = v / (kChunk / 8), j8 = v - r * (kChunk / 8);
+        const int row = row0 + r, i = i0 + 8 * j8;
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        if (row < OUT && i < IN) {
+            const size_t rr = (size_t)e * OUT + row;
+            // the 8 values' bits: at most 64 bits from the first word they touch
+            const long long bit = (long long)i * m.bits;
+            const int wi = (int)(bit >> 5), off = (int)(bit & 31);
+            const uint32_t *wr = wq + rr * words_row;
+            unsigned long long win = __ldg(wr + wi);
+            if (off + 8 * m.bits > 32) win |= (unsigned long long)__ldg(wr + wi + 1) << 32;
+            win >>= off;
+            const size_t gi = rr * ngrp_row + i / m.group;
+            const float s = bf16_to_f32(__ldg(m.scales + gi)), b = bf16_to_f32(__ldg(m.biases + gi));
+            uint32_t h[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                h[j] = f32_to_bf16(__fmaf_rn(s, (float)(uint32_t)((win >> (j * m.bits)) & mask), b));
+            o = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+        }
+        *reinterpret_cast<uint4 *>(tile + r * kStride + j8 * 16) = o;
+    }
+}
+
 template <int NMAT, int DIM>
 __global__ void __launch_bounds__(kThreads, 1) expert_ref_kernel(const Args a) {
+    constexpr bool AFF = DIM == 0;             // affine-quantized weights, bf16 operands
     constexpr bool DUAL = NMAT == 2;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_pairs[kPairs];
@@ -117,8 +157,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_ref_kernel(const Args a) {
     for (int m = 0; m < NMAT; ++m) {
         const Mat &M = a.m[m];
         wt[m] = smem + NMAT * kCbMax + m * kTileBytes;
-        const int vals = M.K * DIM;
-        if (vals * 2 <= kCbMax) {
+        const int vals = AFF ? 0 : M.K * DIM;
+        if (AFF) {
+            cb[m] = nullptr;
+        } else if (vals * 2 <= kCbMax) {
             uint16_t *dst = reinterpret_cast<uint16_t *>(smem + m * kCbMax);
             for (int i = tid; i < vals / 2; i += kThreads)
                 reinterpret_cast<uint32_t *>(dst)[i] = __ldg(reinterpret_cast<const uint32_t *>(M.cb) + i);
@@ -156,7 +198,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_ref_kernel(const Args a) {
                 cp_async16(smem_u32(xt + tk * kStride + j * 16), a.x + (size_t)xr * IN + (ok ? f : 0), ok ? 16 : 0);
             }
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) dequant_chunk<DIM>(a.m[m], cb[m], e, row0, i0, IN, OUT, wt[m]);
+            for (int m = 0; m < NMAT; ++m) {
+                if (AFF) dequant_chunk_affine(a.m[m], e, row0, i0, IN, OUT, wt[m]);
+                else dequant_chunk<DIM == 0 ? 2 : DIM>(a.m[m], cb[m], e, row0, i0, IN, OUT, wt[m]);
+            }
             cp_async_wait_all();
             __syncthreads();
             if (nta == 0) continue;
@@ -178,8 +223,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_ref_kernel(const Args a) {
                         const uint2 bv = *reinterpret_cast<const uint2 *>(
                             xt + (32 * tg + 8 * j + g) * kStride + 32 * q + 8 * t);
 #pragma unroll
-                        for (int m = 0; m < NMAT; ++m)
-                            mma_f16(acc[m][j], av[m][0].x, av[m][1].x, av[m][0].y, av[m][1].y, bv.x, bv.y);
+                        for (int m = 0; m < NMAT; ++m) {
+                            if (AFF) mma_bf16(acc[m][j], av[m][0].x, av[m][1].x, av[m][0].y, av[m][1].y, bv.x, bv.y);
+                            else mma_f16(acc[m][j], av[m][0].x, av[m][1].x, av[m][0].y, av[m][1].y, bv.x, bv.y);
+                        }
                     }
                 }
             }
@@ -215,6 +262,7 @@ static vqmoe_status launch(const Args &a, cudaStream_t stream) {
 
 template <int NMAT>
 static vqmoe_status launch_dim(const Args &a, int dim, cudaStream_t stream) {
+    if (a.m[0].bits) return launch<NMAT, 0>(a, stream);
     switch (dim) {
         case 2: return launch<NMAT, 2>(a, stream);
         case 4: return launch<NMAT, 4>(a, stream);
@@ -232,6 +280,12 @@ static Mat mat_of(const vqmoe_linear *w) {
     m.dim = w->dim;
     m.group = w->group_size;
     m.cbytes = w->codebook_size <= 256 ? 1 : 2;
+    if (w->format == VQMOE_FMT_AFFINE) {
+        m.codes = static_cast<const uint8_t *>(w->weight);
+        m.biases = static_cast<const uint16_t *>(w->biases);
+        m.bits = w->bits;
+        m.K = m.dim = 0;
+    }
     return m;
 }
 

@@ -127,6 +127,30 @@ __global__ void dequant_ref_kernel(const uint8_t *__restrict__ codes, int cbytes
     }
 }
 
+// AFFINE (weight [E][OUT][IN*bits/32] uint32, each row a little-endian bit
+// stream of `bits`-bit values; scales / biases [E][OUT][IN/group] bf16):
+// W = bf16(fmaf(scale, q, bias)) for experts [first, first + count), one
+// weight per thread
+__global__ void dequant_affine_kernel(const uint32_t *__restrict__ wq, const uint16_t *__restrict__ scales,
+                                      const uint16_t *__restrict__ biases, int OUT, int IN, int bits, int group,
+                                      int first, int count, uint16_t *__restrict__ out) {
+    const int words_row = IN * bits / 32, NG = IN / group;
+    const long long n = (long long)count * OUT * IN;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int u = (int)(i % IN);
+        const long long er = i / IN;
+        const long long row = (long long)first * OUT + er;
+        const long long bit = (long long)u * bits;
+        const uint32_t *wr = wq + row * words_row;
+        unsigned long long win = wr[bit >> 5];
+        if ((int)(bit & 31) + bits > 32) win |= (unsigned long long)wr[(bit >> 5) + 1] << 32;
+        const uint32_t q = (uint32_t)(win >> (bit & 31)) & ((1u << bits) - 1u);
+        const float s = bf16_to_f32(scales[row * NG + u / group]), b = bf16_to_f32(biases[row * NG + u / group]);
+        out[i] = f32_to_bf16(__fmaf_rn(s, (float)q, b));
+    }
+}
+
 static int grid_for(long long n) {
     return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)sm_count() * 16));
 }
@@ -203,6 +227,23 @@ vqmoe_status vqmoe_count_bad_codes_u16(const uint16_t *codes, int64_t count, int
 
 vqmoe_status vqmoe_dequant(const vqmoe_linear *w, int32_t first, int32_t count, void *out,
                            void *stream) {
+    if (w && w->format == VQMOE_FMT_AFFINE) {
+        const int b = w->bits;
+        if (w->num_experts <= 0 || w->out_features <= 0 || w->in_features <= 0 ||
+            (b != 2 && b != 3 && b != 4 && b != 5 && b != 6 && b != 8) || w->group_size <= 0 ||
+            w->in_features % w->group_size || (w->in_features * b) % 32)
+            return set_error(VQMOE_BAD_FORMAT, "dequant: affine geometry");
+        if (first < 0 || count <= 0 || first + count > w->num_experts)
+            return set_error(VQMOE_BAD_SHAPE, "dequant: experts [%d, %d) of %d", first, first + count,
+                             w->num_experts);
+        if (!w->weight || !w->scales || !w->biases || !out) return set_error(VQMOE_BAD_POINTER, "dequant: pointers");
+        const long long n = (long long)count * w->out_features * w->in_features;
+        dequant_affine_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const uint32_t *>(w->weight), static_cast<const uint16_t *>(w->scales),
+            static_cast<const uint16_t *>(w->biases), w->out_features, w->in_features, b, w->group_size, first,
+            count, static_cast<uint16_t *>(out));
+        return check_launch("dequant_affine_kernel");
+    }
     if (w && w->format == VQMOE_FMT_VQ_REF) {
         if (w->num_experts <= 0 || w->out_features <= 0 || w->in_features <= 0 ||
             (w->dim != 2 && w->dim != 4 && w->dim != 8) || w->group_size <= 0 || w->group_size % w->dim ||

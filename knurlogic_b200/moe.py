@@ -22,7 +22,7 @@ import torch
 from torch import nn
 
 from . import _lib
-from .switch_layers import (SwitchGLU, SwitchLinear, VQSwitchLinear, c_stream,
+from .switch_layers import (QuantizedSwitchLinear, SwitchGLU, SwitchLinear, VQSwitchLinear, c_stream,
                             require_cuda)
 
 
@@ -169,10 +169,13 @@ class SparseMoeBlock(nn.Module):
     @classmethod
     def from_weights(cls, w: dict, top_k: int, prefix: str = "mlp.",
                      group_size: int | None = None, sharding_group=None,
-                     router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM, activation=None):
+                     router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM, activation=None,
+                     bits: int | None = None):
         """Build from a state dict with the reference's names:
         `{prefix}gate.weight`; `{prefix}switch_mlp.{gate,up,down}_proj.`
-        `{codes, codebook, vq_scales}` (VQ) or `.weight` (bf16), or the HF
+        `{codes, codebook, vq_scales}` (VQ), `{weight, scales, biases}`
+        (affine-quantized; `group_size` default 64, `bits` from the packed
+        width) or `.weight` (bf16), or the HF
         fused `{prefix}experts.gate_up_proj [E, 2I, H]` /
         `{prefix}experts.down_proj [E, H, I]` (split as
         `qwen3_5_moe.py:36-50`); `{prefix}shared_expert.{gate,up,down}_proj.`
@@ -196,6 +199,13 @@ class SparseMoeBlock(nn.Module):
                     IN = codes.shape[-1] * cb.shape[-1]
                     gs = group_size or IN // vs.shape[-1]
                     projs[n] = VQSwitchLinear(codes, cb, vs, group_size=gs)
+                elif q + "scales" in w and q + "biases" in w:
+                    # affine-quantized (mlx's weight / scales / biases); the
+                    # bits follow from the packed width at the group size
+                    wt, sc = w[q + "weight"], w[q + "scales"]
+                    gs = group_size or 64
+                    nbits = bits or (wt.shape[-1] * 32) // (sc.shape[-1] * gs)
+                    projs[n] = QuantizedSwitchLinear(wt, sc, w[q + "biases"], group_size=gs, bits=nbits)
                 elif q + "weight" in w:
                     projs[n] = SwitchLinear(w[q + "weight"])
                 else:

@@ -271,6 +271,72 @@ class VQSwitchLinear(_SwitchBase):
         return out
 
 
+class QuantizedSwitchLinear(_SwitchBase):
+    """Affine-quantized experts, mlx-lm's `QuantizedSwitchLinear`
+    (`switch_layers.py:24-86`, called through `mx.gather_qmm` in mode
+    "affine"): `weight [E, OUT, IN*bits/32]` uint32 -- each row a
+    little-endian bit stream of `bits`-bit values q, element j at bits
+    [j*bits, (j+1)*bits), as `mx.quantize` packs them -- and `scales`,
+    `biases [E, OUT, IN/group_size]` bf16.
+
+    Weight of expert e, row o, input i (this build's rounding; MLX's own
+    kernels cannot run here): W = bf16(fmaf(scale, q, bias)) with the
+    group's scale and bias; the bf16 activations enter a bf16 matmul as they
+    are. `bits` 2, 3, 4, 5, 6 or 8; `group_size` 32, 64 or 128. The
+    reference's optional per-expert output `bias` is not taken."""
+
+    def __init__(self, weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
+                 group_size: int = 64, bits: int = 4, mode: str = "affine", bias: torch.Tensor | None = None):
+        super().__init__()
+        if mode != "affine":
+            raise NotImplementedError(f"quantization mode {mode!r}: only 'affine' is supported")
+        if bias is not None:
+            raise NotImplementedError("a per-expert output bias on a quantized switch linear is not supported")
+        if weight.dim() != 3 or scales.dim() != 3 or biases is None or biases.shape != scales.shape:
+            raise ValueError("affine experts need weight [E, OUT, W], scales and biases [E, OUT, IN/group]")
+        if int(bits) not in (2, 3, 4, 5, 6, 8) or int(group_size) not in (32, 64, 128):
+            raise ValueError(f"bits {bits} (2, 3, 4, 5, 6, 8) / group_size {group_size} (32, 64, 128)")
+        E, OUT, W = (int(n) for n in weight.shape)
+        IN = int(scales.shape[-1]) * int(group_size)
+        if tuple(scales.shape[:2]) != (E, OUT) or W * 32 != IN * int(bits):
+            raise ValueError(f"weight {tuple(weight.shape)} holds {W * 32 // int(bits)} {bits}-bit values per "
+                             f"row; scales {tuple(scales.shape)} at group {group_size} describe {IN}")
+        if weight.dtype not in (torch.uint32, torch.int32):
+            raise ValueError(f"weight must be packed uint32 words, got {weight.dtype}")
+        self.group_size, self.bits, self.mode = int(group_size), int(bits), mode
+        self.register_buffer("weight", weight.contiguous())
+        self.register_buffer("scales", scales.to(torch.bfloat16).contiguous())
+        self.register_buffer("biases", biases.to(torch.bfloat16).contiguous())
+
+    @property
+    def num_experts(self):
+        return self.weight.shape[0]
+
+    @property
+    def output_dims(self):
+        return self.weight.shape[1]
+
+    @property
+    def input_dims(self):
+        return self.scales.shape[2] * self.group_size
+
+    def descriptor(self) -> _lib.Linear:
+        require_cuda(self.weight, self.scales, self.biases)
+        return _lib.Linear(format=_lib.FMT_AFFINE, num_experts=self.num_experts,
+                           out_features=self.output_dims, in_features=self.input_dims,
+                           weight=self.weight.data_ptr(), scales=self.scales.data_ptr(),
+                           biases=self.biases.data_ptr(), group_size=self.group_size, bits=self.bits)
+
+    def dequantize(self, first: int = 0, count: int | None = None) -> torch.Tensor:
+        """Dense bf16 weights of experts [first, first + count)."""
+        count = self.num_experts - first if count is None else count
+        out = torch.empty((count, self.output_dims, self.input_dims), dtype=torch.bfloat16,
+                          device=self.weight.device)
+        d = self.descriptor()
+        _lib.call("vqmoe_dequant", ctypes_ref(d), first, count, out.data_ptr(), _stream(out))
+        return out
+
+
 class SwiGLU(nn.Module):
     """`_SwiGLU` (`qwen3_5.py:108-112`): bf16(bf16(silu(gate)) * x), silu in
     float32. A marker for `SwitchGLU(activation=...)`: the kernels apply it

@@ -44,6 +44,8 @@ class MoEConfig:
     dim: int = 4
     codebook_size: int = 256
     group: int = 64
+    quant: str = "vq"           # vq | affine (mlx's weight / scales / biases)
+    bits: int = 4               # affine bits per weight
 
     def with_tokens(self, t: int) -> "MoEConfig":
         return replace(self, tokens=t)
@@ -79,6 +81,30 @@ def zipf_bias(cfg: MoEConfig, seed: int) -> torch.Tensor:
     return torch.log(p).to(torch.float32)
 
 
+def pack_affine(q: torch.Tensor, bits: int) -> torch.Tensor:
+    """`bits`-bit values [..., IN] -> mlx's affine packing: each row a
+    little-endian bit stream in uint32 words (element j at bits
+    [j*bits, (j+1)*bits)), returned as int32 words (the same bits)."""
+    import numpy as np
+    qn = q.to(torch.int64).cpu().numpy()
+    stream = ((qn[..., :, None] >> np.arange(bits)) & 1).astype(np.uint8)
+    stream = stream.reshape(*qn.shape[:-1], qn.shape[-1] * bits)
+    words = np.packbits(stream, axis=-1, bitorder="little").view(np.int32)
+    return torch.from_numpy(np.ascontiguousarray(words)).to(q.device)
+
+
+def _affine_matrix(E, out, inp, cfg: MoEConfig, g: torch.Generator, device) -> dict:
+    """q uniform over [0, 2^bits); per group a bf16 scale 0.04 (0.5 + U(0,1))
+    / (2^bits - 1) and a bf16 bias that centres the range (weights about
+    N(0, 0.02)-sized)."""
+    levels = (1 << cfg.bits) - 1
+    q = torch.randint(0, levels + 1, (E, out, inp), generator=g, device=device)
+    ng = inp // cfg.group
+    s = (0.5 + torch.rand((E, out, ng), generator=g, device=device)) * (0.04 / levels)
+    b = -s * (levels / 2) + torch.randn((E, out, ng), generator=g, device=device) * 0.002
+    return {"weight": pack_affine(q, cfg.bits), "scales": s.to(torch.bfloat16), "biases": b.to(torch.bfloat16)}
+
+
 def make_weights(cfg: MoEConfig, seed: int = 0, device="cpu",
                  scales: str = "ones", prefix: str = "mlp.") -> dict:
     """State dict with the reference's names (reference layout for codes)."""
@@ -95,6 +121,10 @@ def make_weights(cfg: MoEConfig, seed: int = 0, device="cpu",
     w[prefix + "gate.weight"] = r.to(torch.bfloat16)
     for name, out, inp in (("gate_proj", I, H), ("up_proj", I, H), ("down_proj", H, I)):
         q = f"{prefix}switch_mlp.{name}."
+        if cfg.quant == "affine":
+            for leaf, t in _affine_matrix(E, out, inp, cfg, g, device).items():
+                w[q + leaf] = t
+            continue
         if cfg.codebook_size <= 256:
             w[q + "codes"] = torch.randint(0, cfg.codebook_size, (E, out, inp // cfg.dim),
                                            generator=g, device=device, dtype=torch.uint8)

@@ -78,7 +78,8 @@ def refusals(shapes: dict, n: int, prefix: str = "mlp.") -> list:
                        f"of 64 (whole scale groups and 256-input code chunks)")
         if leaf in ("codes", "vq_scales", "weight") and kind == A2S and part % 16:
             out.append(f"{name}: a rank's {part} output rows are not a multiple of 16")
-        if leaf == "weight" and kind == S2A and part % 16:
+        affine = leaf == "weight" and (name[:-len("weight")] + "biases") in shapes
+        if leaf == "weight" and kind == S2A and part % 16 and not affine:
             out.append(f"{name}: a rank's {part} inputs are not a multiple of 16")
     return out
 

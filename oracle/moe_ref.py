@@ -374,3 +374,45 @@ def tp_sparse_moe_block(x, p, k, vq, n):
     for r in range(n):
         acc += sparse_moe_block(x, shard_block_params(p, r, n), k, vq)
     return bf16(acc.astype(np.float32))
+
+
+# ----------------------------------------------------------- affine experts
+
+def unpack_affine(weight: np.ndarray, bits: int) -> np.ndarray:
+    """The `bits`-bit values of mlx's affine packing (`mx.quantize`, read by
+    `mx.gather_qmm` in `switch_layers.py:71-86`): each row of uint32 words
+    is a little-endian bit stream, element j at bits [j*bits, (j+1)*bits).
+    Returns [..., IN] int64."""
+    w = np.ascontiguousarray(np.asarray(weight).astype(np.uint32))
+    raw = np.unpackbits(w.view(np.uint8), axis=-1, bitorder="little")      # [..., W*32]
+    IN = raw.shape[-1] // bits
+    b = raw[..., :IN * bits].reshape(*raw.shape[:-1], IN, bits).astype(np.int64)
+    return (b << np.arange(bits, dtype=np.int64)).sum(axis=-1)
+
+
+def dequant_affine(weight: np.ndarray, scales: np.ndarray, biases: np.ndarray, group_size: int,
+                   bits: int) -> np.ndarray:
+    """Dense weights of affine-quantized experts, [E, OUT, IN] float32 holding
+    bf16 values: W = bf16(f32(scale * q + bias)), the product and sum exact
+    (float64 over a bf16 scale, a small integer and a bf16 bias), rounded once
+    to float32 -- what a fused multiply-add gives -- then to bf16. The scale
+    and bias are the group's (`mx.quantize`'s affine layout). This rounding is
+    the build's definition: MLX's kernels cannot run here (unpinned)."""
+    q = unpack_affine(weight, bits).astype(np.float64)
+    s = np.repeat(np.asarray(scales, np.float64), group_size, axis=-1)
+    b = np.repeat(np.asarray(biases, np.float64), group_size, axis=-1)
+    return bf16((q * s + b).astype(np.float32))
+
+
+class LazyAffine:
+    """Dequantised affine experts one expert at a time (`w[e]`)."""
+
+    def __init__(self, weight, scales, biases, group_size: int, bits: int):
+        self.weight, self.scales, self.biases = weight, scales, biases
+        self.group_size, self.bits = group_size, bits
+        E, OUT, W = weight.shape
+        self.shape = (E, OUT, W * 32 // bits)
+
+    def __getitem__(self, e: int) -> np.ndarray:
+        return dequant_affine(self.weight[e:e + 1], self.scales[e:e + 1], self.biases[e:e + 1],
+                              self.group_size, self.bits)[0]

@@ -38,9 +38,10 @@ def to_np(t):
     return t.detach().cpu().numpy()
 
 
-def oracle_params(w: dict, prefix: str = "mlp.") -> dict:
-    """Oracle parameters (numpy; VQ experts as lazily dequantised views)
-    from a state dict with the reference's names."""
+def oracle_params(w: dict, prefix: str = "mlp.", group_size: int = 64) -> dict:
+    """Oracle parameters (numpy; VQ and affine experts as lazily dequantised
+    views) from a state dict with the reference's names; `group_size` is the
+    affine experts' group (their packed width gives the bits)."""
     from oracle import moe_ref as R
     p = {"router": to_np(w[prefix + "gate.weight"])}
     for n, key in (("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
@@ -51,6 +52,10 @@ def oracle_params(w: dict, prefix: str = "mlp.") -> dict:
             vs = to_np(w[q + "vq_scales"])
             gs = codes.shape[-1] * cb.shape[-1] // vs.shape[-1]
             p[key] = R.LazyVQ(codes, cb, vs, gs)
+        elif q + "biases" in w:
+            wt, sc = to_np(w[q + "weight"]), to_np(w[q + "scales"])
+            bits = wt.shape[-1] * 32 // (sc.shape[-1] * group_size)
+            p[key] = R.LazyAffine(wt, sc, to_np(w[q + "biases"]), group_size, bits)
         else:
             p[key] = to_np(w[q + "weight"])
     if prefix + "shared_expert.gate_proj.weight" in w:

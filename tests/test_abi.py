@@ -32,9 +32,10 @@ def test_every_declared_symbol_is_exported(so):
 
 
 def test_abi_version_and_struct_layout(so):
-    assert so.vqmoe_abi_version() == 3
-    # vqmoe_linear: 4 int32, 4 pointers, 4 int32 (the last: the activation)
-    assert ctypes.sizeof(_lib.Linear) == 16 + 4 * 8 + 16
+    assert so.vqmoe_abi_version() == 4
+    # vqmoe_linear: 4 int32, 4 pointers, 4 int32 (the last: the activation),
+    # the affine biases pointer, bits, a reserved word
+    assert ctypes.sizeof(_lib.Linear) == 16 + 4 * 8 + 16 + 8 + 8
     # vqmoe_block: ..., 4 shared pointers, router_mode, wait_polls
     assert ctypes.sizeof(_lib.Block) == 16 + 8 + 3 * ctypes.sizeof(_lib.Linear) + 4 * 8 + 8
 
