@@ -35,7 +35,8 @@ import numpy as np
 __all__ = [
     "bf16", "f16", "f16_sat", "dequant", "prepare_vq",
     "linear", "router", "switch_linear", "switch_glu", "sparse_moe_block",
-    "tp_sparse_moe_block", "shard_block_params", "LazyVQ",
+    "tp_sparse_moe_block", "shard_block_params", "LazyVQ", "LazyAffine", "dequant_affine",
+    "unpack_affine",
 ]
 
 
@@ -342,6 +343,10 @@ def shard_block_params(p: dict, rank: int, n: int) -> dict:
     `shared_expert_gate` replicated (dequantised weights are cut the same
     way the codes and vq_scales are, and the codebook is never cut)."""
     def a2s(w):
+        if isinstance(w, LazyAffine):
+            o = w.shape[1] // n
+            cut = slice(rank * o, (rank + 1) * o)
+            return LazyAffine(w.weight[:, cut], w.scales[:, cut], w.biases[:, cut], w.group_size, w.bits)
         if isinstance(w, LazyVQ):
             o = w.shape[1] // n
             return LazyVQ(w.codes[:, rank * o:(rank + 1) * o], w.codebook,
@@ -350,6 +355,10 @@ def shard_block_params(p: dict, rank: int, n: int) -> dict:
         return w[..., rank * o:(rank + 1) * o, :]
 
     def s2a(w):
+        if isinstance(w, LazyAffine):
+            c, g = w.weight.shape[-1] // n, w.scales.shape[-1] // n
+            return LazyAffine(w.weight[..., rank * c:(rank + 1) * c], w.scales[..., rank * g:(rank + 1) * g],
+                              w.biases[..., rank * g:(rank + 1) * g], w.group_size, w.bits)
         if isinstance(w, LazyVQ):
             c = w.codes.shape[-1] // n
             g = w.scales.shape[-1] // n
