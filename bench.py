@@ -68,6 +68,9 @@ def parse():
                     help="skip the secondary figures (prefill c3, c4 unsplit, c2 replicas)")
     ap.add_argument("--tp", type=int, default=None,
                     help="tensor split of the layer (N / tp independent replicas)")
+    ap.add_argument("--tp-reduce", choices=("p2p", "nccl"), default="p2p",
+                    help="the split's reduction: the combine + float32 sum in one kernel over NVLink peer "
+                         "memory (default), or a float32 NCCL all-reduce after the combine")
     return ap.parse_args()
 
 
@@ -187,7 +190,7 @@ def launches_per_call(cfg, T):
     return n
 
 
-def build_copies(cfg, tp, tp_rank, group, dev, seed0=100):
+def build_copies(cfg, tp, tp_rank, group, dev, seed0=100, tp_reduce="p2p"):
     """Independently seeded copies of the layer (this rank's cut of each),
     more than 3x the 126 MB L2 of weights in total."""
     from knurlogic_b200 import synth, tensor_split
@@ -196,14 +199,16 @@ def build_copies(cfg, tp, tp_rank, group, dev, seed0=100):
     blocks = []
     for i in range(L):
         w = synth.make_weights(cfg, seed=seed0 + i, device=dev, scales="ones")
-        blocks.append(tensor_split.build_block(w, cfg.top_k, rank=tp_rank, n=tp, group=group))
+        blocks.append(tensor_split.build_block(w, cfg.top_k, rank=tp_rank, n=tp, group=group,
+                                               tp_reduce=tp_reduce))
         del w
     return blocks
 
 
 class Graphs:
-    """One CUDA graph per layer copy: the block, plus under a split the
-    float32 all-reduce of the partials and the bf16 rounding."""
+    """One CUDA graph per layer copy: the block, with under a split its
+    reduction -- the peer-memory kernel inside the block call, or the float32
+    NCCL all-reduce of the partials and the bf16 rounding."""
 
     def __init__(self, blocks, x, tp, group, dev):
         import torch
@@ -215,13 +220,16 @@ class Graphs:
 
         def step(i):
             b = blocks[i]
-            if tp == 1:
+            if tp == 1 or b.tp_reduce == "p2p":
                 b.forward_into(x, self.outs[i])
             else:
                 b.forward_into(x, self.parts[i])
                 dist.all_reduce(self.parts[i], group=group)
                 self.outs[i].copy_(self.parts[i])
         self.step = step
+        for b in blocks:                         # collectives of the split, before any capture
+            if tp > 1 and b.tp_reduce == "p2p":
+                b.tp_buffers(x.shape[0], dev)
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
@@ -294,9 +302,11 @@ def split_groups(world, tp, rank):
 
 
 def tp_share(blocks, x, group, world, local, dev, n):
-    """The all-reduce's share of a tensor-split step: per step, the block
-    (float32 partial) and the all-reduce replayed as separate graphs with
-    CUDA events between them, averaged over n steps, max over ranks."""
+    """The NCCL reduction's share of a tensor-split step: per step, the
+    block (float32 partial) and the float32 all-reduce replayed as separate
+    graphs with CUDA events between them, averaged over n steps, max over
+    ranks. (The peer-memory path has no separate reduction to time: its
+    combine and reduction are one kernel, timed by `tp_reduce_share`.)"""
     import torch
     import torch.distributed as dist
     T, H = x.shape
@@ -341,6 +351,46 @@ def tp_share(blocks, x, group, world, local, dev, n):
             "allreduce_share": round(ar / (blk + ar), 4), "allreduce_bytes": T * H * 4,
             "note": "block and float32 all-reduce replayed as separate graphs, CUDA events between them; "
                     "the all-reduce time includes waiting for the slowest rank's block"}
+
+
+def tp_reduce_share(blocks, x, world, local, dev, n):
+    """The peer-memory path's reduction time: the timed entry's events put
+    the fused combine + reduction kernel between its last two marks; the
+    block's other stages as the rest. Averaged over n calls, max over ranks
+    (every rank makes the same calls: the kernel meets its peers inside)."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from knurlogic_b200 import _lib
+    T = x.shape[0]
+    L = len(blocks)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(n)]
+    stream = torch.cuda.current_stream(dev)
+    for row in evs:
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize(dev)
+    out = torch.empty(T, x.shape[1], dtype=torch.bfloat16, device=dev)
+    descs = [b._desc() for b in blocks]
+    wss = [b.workspace(T, dev) for b in blocks]
+    tps = [b.tp_buffers(T, dev) for b in blocks]
+    dist.barrier(device_ids=[local])
+    for i in range(n):
+        b = i % L
+        evs[i][0].record(stream)
+        _lib.call("vqmoe_sparse_moe_block_tp", ctypes.byref(descs[b]), ctypes.byref(tps[b]), x.data_ptr(), T,
+                  out.data_ptr(), wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream)
+        evs[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    rows = evs[min(10, n - 1):]
+    call = sum(r[0].elapsed_time(r[1]) for r in rows) / len(rows)
+    t = torch.tensor([call], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"call_ms": round(float(t.item()), 5),
+            "note": "the fused combine + reduction kernel replaces combine_kernel and the NCCL all-reduce; "
+                    "its own time is in stages_ms.combine_ms (rank 0's timed entry)"}
 
 
 def quick_value(workload, tp, rank, world, local, dev, steps, warmup):
@@ -435,7 +485,7 @@ def run_ours(args, world, rank, local):
     # replica) runs the layer on its own batch of tokens
     group = split_groups(world, tp, rank)
     replica = rank // tp
-    blocks = build_copies(cfg, tp, rank % tp, group, dev)
+    blocks = build_copies(cfg, tp, rank % tp, group, dev, tp_reduce=args.tp_reduce)
     L = len(blocks)
     x = synth.make_input(cfg, seed=7 + replica, device=dev)
 
@@ -448,7 +498,11 @@ def run_ours(args, world, rank, local):
     del G
     torch.cuda.synchronize(dev)
 
-    comm = tp_share(blocks, x, group, world, local, dev, min(args.steps, 200)) if tp > 1 else None
+    comm = None
+    if tp > 1:
+        comm = (tp_reduce_share(blocks, x, world, local, dev, min(args.steps, 200)) if args.tp_reduce == "p2p"
+                else tp_share(blocks, x, group, world, local, dev, min(args.steps, 200)))
+        comm["reduce"] = args.tp_reduce
 
     # ---- stage times of the block (events between its kernels), rank 0
     stage, distinct = None, None

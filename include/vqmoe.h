@@ -209,6 +209,39 @@ VQMOE_API vqmoe_status vqmoe_sparse_moe_block_timed(
     int32_t out_dtype, void *workspace, size_t workspace_bytes, void *stream,
     void *const *events, int32_t n_events);
 
+/* A tensor-split rank's view of its split's symmetric buffers, for
+ * vqmoe_sparse_moe_block_tp: this rank, the number of ranks (<= 8), and
+ * every rank's buffer (buffer_bytes >= vqmoe_tp_buffer_bytes) as this rank
+ * addresses it -- peer memory over NVLink (CUDA IPC or symmetric memory).
+ * The caller zeroes each buffer once, before the split's first call, and
+ * has every rank see that done (a barrier) before any rank calls. */
+typedef struct {
+    int32_t rank;
+    int32_t world;
+    void *buffers[8];
+    int64_t buffer_bytes;
+    int32_t wait_polls;          /* polls of each cross-rank wait; 0: about four seconds */
+    int32_t reserved;            /* 0 */
+} vqmoe_tp;
+
+/* Bytes of one rank's buffer for blocks of `hidden` at up to `tokens`
+ * tokens per call. */
+VQMOE_API size_t vqmoe_tp_buffer_bytes(int32_t hidden, int32_t tokens);
+
+/* The tensor-split SparseMoeBlock: this rank's cut of the block (router,
+ * experts, shared expert on its cut), then ONE kernel that combines the
+ * rank's bf16 partial and reduces it with the other ranks' over peer memory
+ * -- the float32 sum in rank order, rounded once to bf16 (Reduce,
+ * src/knurlogic/engine/split/tensor.py:159-187) -- into out [T, H] bf16 on
+ * every rank. Every rank of the split makes the same calls in the same
+ * order (the ranks meet inside the kernel at bounded barriers; a wait that
+ * runs out is reported by vqmoe_workspace_status). hidden % (8 * world)
+ * == 0. */
+VQMOE_API vqmoe_status vqmoe_sparse_moe_block_tp(const vqmoe_block *blk, const vqmoe_tp *tp,
+                                                 const void *x, int32_t tokens, void *out,
+                                                 void *workspace, size_t workspace_bytes,
+                                                 void *stream);
+
 /* SwitchGLU.__call__: y[T, k, H] bf16 = down(bf16(act(gate(x))) * up(x))
  * for each (token, slot) of indices [T, k] int32; act = gate->activation
  * (SwiGLU or GeGLU). */

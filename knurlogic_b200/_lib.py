@@ -42,6 +42,12 @@ class Linear(Structure):
                 ("biases", c_void_p), ("bits", c_int32), ("reserved", c_int32)]
 
 
+class Tp(Structure):
+    """vqmoe_tp"""
+    _fields_ = [("rank", c_int32), ("world", c_int32), ("buffers", c_void_p * 8),
+                ("buffer_bytes", c_int64), ("wait_polls", c_int32), ("reserved", c_int32)]
+
+
 class Block(Structure):
     """vqmoe_block"""
     _fields_ = [("hidden", c_int32), ("num_experts", c_int32),
@@ -57,6 +63,9 @@ class Block(Structure):
 SIGNATURES = [
     ("vqmoe_abi_version", c_int32, []),
     ("vqmoe_workspace_status", c_int32, [c_void_p, c_void_p]),
+    ("vqmoe_tp_buffer_bytes", c_size_t, [c_int32, c_int32]),
+    ("vqmoe_sparse_moe_block_tp", c_int32,
+     [POINTER(Block), POINTER(Tp), c_void_p, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_last_error", c_char_p, []),
     ("vqmoe_block_workspace_size", c_size_t, [POINTER(Block), c_int32]),
     ("vqmoe_switch_glu_workspace_size", c_size_t,

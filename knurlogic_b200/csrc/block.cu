@@ -429,7 +429,8 @@ static vqmoe_status run_shared(const vqmoe_block *b, const uint16_t *x, int T, c
 
 static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                               void *out, int out_f32, const BlockWs &w,
-                              cudaStream_t st, cudaEvent_t *ev = nullptr, int n_ev = 0) {
+                              cudaStream_t st, cudaEvent_t *ev = nullptr, int n_ev = 0,
+                              const TpArgs *tp = nullptr) {
     const int H = b->hidden, E = b->num_experts, k = b->top_k, P = T * k;
     const bool shared = b->shared_inter > 0;
     const bool vq_in = is_vq(b->gate.format);
@@ -464,6 +465,15 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
     if (shared && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
         return check_launch("side stream join");
     if ((s = mark(ev, n_ev, 3, st)) != VQMOE_OK) return s;
+    if (tp) {
+        // the combine and the split's reduction, one kernel over peer memory
+        TpArgs a = *tp;
+        a.err = w.status;
+        if ((s = launch_tp_reduce(w.ybuf, T, k, H, shared ? w.sh : nullptr, w.sgate, a,
+                                  static_cast<uint16_t *>(out), st)) != VQMOE_OK)
+            return s;
+        return mark(ev, n_ev, 4, st);
+    }
     const size_t nvec = (size_t)T * (H / 8);
     const int grid = (int)std::min<size_t>((nvec + 255) / 256, (size_t)sm_count() * 8);
     combine_kernel<<<grid, 256, 0, st>>>(w.ybuf, T, k, H, shared ? w.sh : nullptr, w.sgate, out, out_f32);
@@ -573,7 +583,7 @@ size_t vqmoe_block_workspace_size(const vqmoe_block *blk, int32_t tokens) {
 
 static vqmoe_status block_impl(const vqmoe_block *blk, const void *x, int32_t tokens, void *out,
                                int32_t out_dtype, void *workspace, size_t workspace_bytes,
-                               void *stream, cudaEvent_t *ev, int n_ev) {
+                               void *stream, cudaEvent_t *ev, int n_ev, const TpArgs *tp = nullptr) {
     vqmoe_status s = check_block(blk, tokens);
     if (s != VQMOE_OK) return s;
     if (!aligned_ptr(x) || !aligned_ptr(out) || !aligned_ptr(workspace))
@@ -591,7 +601,7 @@ static vqmoe_status block_impl(const vqmoe_block *blk, const void *x, int32_t to
         const int T = std::min(chunk, tokens - t0);
         s = run_block(blk, static_cast<const uint16_t *>(x) + (size_t)t0 * blk->hidden, T,
                       static_cast<char *>(out) + (size_t)t0 * blk->hidden * osz,
-                      out_dtype == VQMOE_OUT_F32, w, st, t0 == 0 ? ev : nullptr, n_ev);
+                      out_dtype == VQMOE_OUT_F32, w, st, t0 == 0 ? ev : nullptr, n_ev, tp);
         if (s != VQMOE_OK) return s;
     }
     return VQMOE_OK;
@@ -602,6 +612,37 @@ vqmoe_status vqmoe_sparse_moe_block(const vqmoe_block *blk, const void *x, int32
                                     size_t workspace_bytes, void *stream) {
     return block_impl(blk, x, tokens, out, out_dtype, workspace, workspace_bytes, stream,
                       nullptr, 0);
+}
+
+size_t vqmoe_tp_buffer_bytes(int32_t hidden, int32_t tokens) {
+    if (hidden <= 0 || tokens <= 0) return 0;
+    const size_t T = (size_t)std::min<int>(tokens, kMaxTokensPerLaunch);
+    return kTpFlagBytes + 2 * T * (size_t)hidden * sizeof(uint16_t);
+}
+
+vqmoe_status vqmoe_sparse_moe_block_tp(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x, int32_t tokens,
+                                       void *out, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!tp) return set_error(VQMOE_BAD_POINTER, "block_tp: null split descriptor");
+    if (tp->world < 1 || tp->world > kTpMaxRanks || tp->rank < 0 || tp->rank >= tp->world)
+        return set_error(VQMOE_BAD_SHAPE, "block_tp: rank %d of %d (at most %d ranks)", tp->rank, tp->world,
+                         kTpMaxRanks);
+    if (tp->wait_polls < 0) return set_error(VQMOE_BAD_SHAPE, "block_tp: wait_polls %d", tp->wait_polls);
+    if (!blk || blk->hidden % (8 * tp->world))
+        return set_error(VQMOE_BAD_SHAPE, "block_tp: hidden %d is not a multiple of 8 x %d ranks",
+                         blk ? blk->hidden : 0, tp->world);
+    if (tokens <= 0) return set_error(VQMOE_BAD_SHAPE, "tokens %d", tokens);
+    if ((size_t)tp->buffer_bytes < vqmoe_tp_buffer_bytes(blk->hidden, tokens))
+        return set_error(VQMOE_WORKSPACE_TOO_SMALL, "block_tp: buffers of %lld < %zu bytes",
+                         (long long)tp->buffer_bytes, vqmoe_tp_buffer_bytes(blk->hidden, tokens));
+    TpArgs a{};
+    a.rank = tp->rank;
+    a.n = tp->world;
+    a.wait_polls = (uint32_t)tp->wait_polls;
+    for (int q = 0; q < tp->world; ++q) {
+        if (!aligned_ptr(tp->buffers[q])) return set_error(VQMOE_BAD_POINTER, "block_tp: buffer of rank %d", q);
+        a.base[q] = static_cast<uint8_t *>(tp->buffers[q]);
+    }
+    return block_impl(blk, x, tokens, out, VQMOE_OUT_BF16, workspace, workspace_bytes, stream, nullptr, 0, &a);
 }
 
 vqmoe_status vqmoe_sparse_moe_block_timed(const vqmoe_block *blk, const void *x, int32_t tokens,

@@ -52,6 +52,21 @@ inline int expert_ctl_words(int E) { return 2 + E; }
 vqmoe_status launch_experts(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,
                             const vqmoe_linear *w2, const RoutedIO &r2, uint32_t *ctl, uint32_t *err,
                             uint32_t wait_polls, cudaStream_t stream, cudaEvent_t after_permute = nullptr);
+// The tensor split's combine + float32 reduction over peer memory
+// (tp_reduce.cu). base[q]: rank q's symmetric buffer as this rank addresses
+// it: kTpFlagBytes of flags, then its partial [T][H] bf16, then its result
+// region [T][H] bf16.
+constexpr int kTpMaxRanks = 8;
+constexpr size_t kTpFlagBytes = 256;
+struct TpArgs {
+    int rank, n;
+    uint8_t *base[kTpMaxRanks];
+    uint32_t *err;             // the call's status word
+    uint32_t wait_polls;       // polls of each barrier wait (0: about four seconds)
+};
+vqmoe_status launch_tp_reduce(const uint16_t *ybuf, int T, int k, int H, const uint16_t *sh, const float *sg,
+                              const TpArgs &a, uint16_t *out, cudaStream_t stream);
+
 // The routed experts with reference-layout VQ weights (VQMOE_FMT_VQ_REF):
 // phase 1 (r1, may be null) then phase 2, two launches.
 vqmoe_status launch_experts_ref(const vqmoe_linear *gate, const vqmoe_linear *up, const RoutedIO *r1,

@@ -1,0 +1,197 @@
+// The tensor-split block's combine and float32 reduction in one kernel,
+// over NVLink peer memory.
+//
+// Reference: under a tensor split every rank runs the whole MoE block on its
+// cut and the block output is summed across ranks in float32, then rounded
+// once (Reduce, src/knurlogic/engine/split/tensor.py:159-187; the in-model
+// all_sum of qwen3_5.py:189-190). Here each rank's kernel
+//   A  combines its routed outputs and gated shared expert into its bf16
+//      partial (qwen3_5.py:181-187, the same roundings as combine_kernel),
+//      written into its part of a buffer every rank can address;
+//   B  reduces one column slice of the output: the n ranks' partials of the
+//      slice, read over NVLink, summed in float32 in rank order and rounded
+//      once to bf16, stored into every rank's result region (two-shot:
+//      each partial crosses NVLink once, each result once);
+//   C  copies its result region into the caller's output.
+// Between the phases the ranks meet at flag barriers: a CTA's writes, a
+// system-scope fence, a local counter; the CTA that completes the count
+// release-stores the call's epoch into every rank's arrival flag for it,
+// and every CTA acquire-spins (bounded) until all n ranks' flags carry the
+// epoch. The epoch is each rank's count of finished calls, kept in device
+// memory and advanced by the call's last CTA (which also clears the call's
+// local counters), so a CUDA graph replays the kernel with the right epoch
+// every time; all ranks make the same calls in the same order, so their
+// epochs agree. Data other ranks wrote is read with ld.global.cv (fetched
+// again, never from a line L1 kept from an earlier call). A wait that runs
+// out stores kWaitDependency in the call's status word and the kernel goes
+// on (its output is then wrong; nothing hangs).
+//
+// Each rank's symmetric buffer: kTpFlagBytes of flags and counters, its
+// partial [T][H] bf16, its result region [T][H] bf16.
+#include <algorithm>
+
+#include "stages.cuh"
+
+namespace vqmoe {
+
+namespace tp {
+
+// flag words of a rank's buffer
+constexpr int kEpoch = 0, kCountA = 1, kCountB = 2, kCountC = 3;
+constexpr int kArriveA = 8, kArriveB = 8 + kTpMaxRanks;
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint4 ld_cv_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.cv.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint32_t *flags_of(const TpArgs &a, int rank) {
+    return reinterpret_cast<uint32_t *>(a.base[rank]);
+}
+
+// Thread 0 of every CTA: the CTA's writes so far are done; the last CTA of
+// the rank to get here announces the rank to every peer (arrival slot
+// `arrive` + rank), then every CTA waits until all ranks have announced.
+__device__ void rank_barrier(const TpArgs &a, int count, int arrive, uint32_t epoch) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t *mine = flags_of(a, a.rank);
+        __threadfence_system();
+        const uint32_t old = atomicAdd(mine + count, 1u);
+        if (old == gridDim.x - 1) {
+            __threadfence_system();
+            for (int q = 0; q < a.n; ++q) st_release_sys(flags_of(a, q) + arrive + a.rank, epoch + 1);
+        }
+        const long polls = a.wait_polls ? (long)a.wait_polls : (1L << 22);
+        for (int q = 0; q < a.n; ++q) {
+            unsigned ns = 32;
+            for (long i = 1;; ++i) {
+                if (ld_acquire_sys(mine + arrive + q) >= epoch + 1) break;
+                if (i >= polls) {
+                    atomicExch(a.err, kWaitDependency);
+                    break;
+                }
+                __nanosleep(ns);
+                if (ns < 1024) ns <<= 1;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(256)
+tp_reduce_kernel(const uint16_t *__restrict__ ybuf, int T, int k, int H, const uint16_t *__restrict__ sh,
+                 const float *__restrict__ sg, const TpArgs a, uint16_t *__restrict__ out) {
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(flags_of(a, a.rank) + kEpoch);
+    const int vpr = H / 8;
+    const size_t nvec = (size_t)T * vpr;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    uint16_t *part = reinterpret_cast<uint16_t *>(a.base[a.rank] + kTpFlagBytes);
+    // ---- A: this rank's bf16 partial, as combine_kernel rounds it
+    for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < nvec; v += stride) {
+        const int tkn = (int)(v / vpr), c8 = (int)(v - (size_t)tkn * vpr);
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll 8
+        for (int s = 0; s < k; ++s) {
+            const uint4 y = __ldg(reinterpret_cast<const uint4 *>(ybuf + ((size_t)tkn * k + s) * H + c8 * 8));
+            const uint32_t u[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] += bf16_to_f32(u[j] & 0xFFFFu);
+                acc[2 * j + 1] += bf16_to_f32(u[j] >> 16);
+            }
+        }
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = bf16r(acc[i]);
+        if (sh) {
+            const float gate = sg[tkn];
+            const uint4 sv = *reinterpret_cast<const uint4 *>(sh + (size_t)tkn * H + c8 * 8);
+            const uint32_t u[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                r[2 * j] = bf16r(r[2 * j] + bf16r(gate * bf16_to_f32(u[j] & 0xFFFFu)));
+                r[2 * j + 1] = bf16r(r[2 * j + 1] + bf16r(gate * bf16_to_f32(u[j] >> 16)));
+            }
+        }
+        uint32_t p[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[j] = (uint32_t)f32_to_bf16(r[2 * j]) | ((uint32_t)f32_to_bf16(r[2 * j + 1]) << 16);
+        *reinterpret_cast<uint4 *>(part + v * 8) = make_uint4(p[0], p[1], p[2], p[3]);
+    }
+    rank_barrier(a, kCountA, kArriveA, epoch);
+    // ---- B: this rank's column slice, summed over the ranks in rank order
+    const size_t part_bytes = (size_t)T * H * 2;
+    const int spr = vpr / a.n;                       // vectors of the slice per row
+    const size_t nsl = (size_t)T * spr;
+    for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < nsl; v += stride) {
+        const int tkn = (int)(v / spr), c8 = a.rank * spr + (int)(v - (size_t)tkn * spr);
+        const size_t off = ((size_t)tkn * vpr + c8) * 16;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+        for (int q = 0; q < a.n; ++q) {
+            const uint4 pv = ld_cv_v4(a.base[q] + kTpFlagBytes + off);
+            const uint32_t u[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] += bf16_to_f32(u[j] & 0xFFFFu);
+                acc[2 * j + 1] += bf16_to_f32(u[j] >> 16);
+            }
+        }
+        uint32_t p[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[j] = (uint32_t)f32_to_bf16(acc[2 * j]) | ((uint32_t)f32_to_bf16(acc[2 * j + 1]) << 16);
+        const uint4 res = make_uint4(p[0], p[1], p[2], p[3]);
+        for (int q = 0; q < a.n; ++q)
+            *reinterpret_cast<uint4 *>(a.base[q] + kTpFlagBytes + part_bytes + off) = res;
+    }
+    rank_barrier(a, kCountB, kArriveB, epoch);
+    // ---- C: the result into the caller's output
+    const uint8_t *red = a.base[a.rank] + kTpFlagBytes + part_bytes;
+    for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < nvec; v += stride)
+        reinterpret_cast<uint4 *>(out)[v] = ld_cv_v4(red + v * 16);
+    // the call's last CTA (every CTA has read the epoch and passed both
+    // barriers by then) clears the counters and advances the epoch
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t *mine = flags_of(a, a.rank);
+        const uint32_t old = atomicAdd(mine + kCountC, 1u);
+        if (old == gridDim.x - 1) {
+            mine[kCountA] = 0u;
+            mine[kCountB] = 0u;
+            mine[kCountC] = 0u;
+            __threadfence();
+            atomicExch(mine + kEpoch, epoch + 1);
+        }
+    }
+}
+
+}  // namespace tp
+
+vqmoe_status launch_tp_reduce(const uint16_t *ybuf, int T, int k, int H, const uint16_t *sh, const float *sg,
+                              const TpArgs &a, uint16_t *out, cudaStream_t stream) {
+    // every CTA must be resident at once (they meet at the barriers): one
+    // per SM at most, fewer when the work is small
+    const size_t nvec = (size_t)T * (H / 8);
+    const int grid = (int)std::max<size_t>(1, std::min<size_t>((nvec + 255) / 256, (size_t)sm_count()));
+    tp::tp_reduce_kernel<<<grid, 256, 0, stream>>>(ybuf, T, k, H, sh, sg, a, out);
+    return check_launch("tp_reduce_kernel");
+}
+
+}  // namespace vqmoe

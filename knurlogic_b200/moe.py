@@ -11,8 +11,11 @@ always renormalised (`norm_topk_prob = True`, vendored edit 7).
 The whole block is one `vqmoe_sparse_moe_block` call (router, fused
 gate/up + SwiGLU, down with the routing weight, shared expert, combine).
 Under a tensor split (`sharding_group`), each rank runs the block on its
-cut and the float32 partials are all-reduced over NCCL, then rounded once
-to bf16 (`src/knurlogic/engine/split/tensor.py:159-187`).
+cut and the ranks' partials are summed in float32 and rounded once to bf16
+(`src/knurlogic/engine/split/tensor.py:159-187`): by default in one kernel
+with the combine, over NVLink peer memory (`vqmoe_sparse_moe_block_tp`,
+buffers from torch's symmetric memory); `tp_reduce="nccl"` all-reduces
+float32 partials over NCCL instead.
 """
 from __future__ import annotations
 
@@ -68,8 +71,13 @@ class SparseMoeBlock(nn.Module):
     def __init__(self, gate_weight: torch.Tensor, switch_mlp: SwitchGLU,
                  top_k: int, shared_expert: SharedExpert | None = None,
                  shared_expert_gate_weight: torch.Tensor | None = None,
-                 sharding_group=None, router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM):
+                 sharding_group=None, router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM,
+                 tp_reduce: str = "p2p"):
         super().__init__()
+        if tp_reduce not in ("p2p", "nccl"):
+            raise ValueError(f"tp_reduce {tp_reduce!r} ('p2p' or 'nccl')")
+        self.tp_reduce = tp_reduce
+        self._tp = None
         E, H = gate_weight.shape
         self.num_experts, self.hidden = int(E), int(H)
         self.top_k = int(top_k)
@@ -139,12 +147,44 @@ class SparseMoeBlock(nn.Module):
             return
         _lib.call("vqmoe_workspace_status", self._ws.data_ptr(), c_stream(device or self._ws.device))
 
+    def tp_buffers(self, tokens: int, device):
+        """This rank's view of the split's symmetric buffers (`vqmoe_tp`),
+        made once per device and size: a torch symmetric-memory buffer of
+        `vqmoe_tp_buffer_bytes` per rank, zeroed, exchanged with the other
+        ranks (a collective: every rank calls it in the same order), and a
+        barrier so that no rank's kernel meets another's unzeroed flags."""
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        need = _lib.lib().vqmoe_tp_buffer_bytes(self.hidden, min(tokens, 2048))
+        if self._tp is not None and self._tp[0] >= need and self._tp[1].device == device:
+            return self._tp[2]
+        g = self.sharding_group
+        buf = symm_mem.empty(need, dtype=torch.uint8, device=device)
+        buf.zero_()
+        torch.cuda.synchronize(device)
+        hdl = symm_mem.rendezvous(buf, g)
+        d = _lib.Tp()
+        d.rank, d.world = dist.get_rank(g), dist.get_world_size(g)
+        for q in range(d.world):
+            d.buffers[q] = hdl.buffer_ptrs[q]
+        d.buffer_bytes = need
+        dist.barrier(group=g)
+        self._tp = (need, buf, d, hdl)
+        return d
+
     def forward_into(self, x2d: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """The block on contiguous [T, H] bf16 into `out` ([T, H] bf16 or
-        float32 -- float32 holds the bf16 result widened, for a reduction)."""
+        float32 -- float32 holds the bf16 result widened, for a reduction).
+        Under a split with `tp_reduce="p2p"` (bf16 `out`) the result is the
+        whole split's, reduced over peer memory."""
         T = x2d.shape[0]
         b = self._desc()
         ws = self.workspace(T, x2d.device)
+        if self.sharding_group is not None and self.tp_reduce == "p2p" and out.dtype == torch.bfloat16:
+            tp = self.tp_buffers(T, x2d.device)
+            _lib.call("vqmoe_sparse_moe_block_tp", ctypes.byref(b), ctypes.byref(tp), x2d.data_ptr(), T,
+                      out.data_ptr(), ws.data_ptr(), ws.numel(), c_stream(x2d.device))
+            return out
         odt = _lib.OUT_F32 if out.dtype == torch.float32 else _lib.OUT_BF16
         _lib.call("vqmoe_sparse_moe_block", ctypes.byref(b), x2d.data_ptr(), T,
                   out.data_ptr(), odt, ws.data_ptr(), ws.numel(), c_stream(x2d.device))
@@ -158,7 +198,7 @@ class SparseMoeBlock(nn.Module):
         x2d = x.reshape(-1, self.hidden)
         if not x2d.is_contiguous():
             x2d = x2d.contiguous()
-        if self.sharding_group is None:
+        if self.sharding_group is None or self.tp_reduce == "p2p":
             out = torch.empty_like(x2d)
             return self.forward_into(x2d, out).reshape(shape)
         part = torch.empty(x2d.shape, dtype=torch.float32, device=x.device)
@@ -170,7 +210,7 @@ class SparseMoeBlock(nn.Module):
     def from_weights(cls, w: dict, top_k: int, prefix: str = "mlp.",
                      group_size: int | None = None, sharding_group=None,
                      router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM, activation=None,
-                     bits: int | None = None):
+                     bits: int | None = None, tp_reduce: str = "p2p"):
         """Build from a state dict with the reference's names:
         `{prefix}gate.weight`; `{prefix}switch_mlp.{gate,up,down}_proj.`
         `{codes, codebook, vq_scales}` (VQ), `{weight, scales, biases}`
@@ -218,7 +258,7 @@ class SparseMoeBlock(nn.Module):
                               w[f"{p}shared_expert.down_proj.weight"])
             seg = w[f"{p}shared_expert_gate.weight"]
         return cls(w[f"{p}gate.weight"], SwitchGLU(**projs, activation=activation), top_k, se, seg,
-                   sharding_group=sharding_group, router_mode=router_mode)
+                   sharding_group=sharding_group, router_mode=router_mode, tp_reduce=tp_reduce)
 
 
 class CapturedBlock:
@@ -229,7 +269,8 @@ class CapturedBlock:
     device) into the graph's static input, replays the graph, and copies
     the result into `out` (host or device) when given; otherwise it returns
     the static output buffer (overwritten by the next call). Under a tensor
-    split the float32 all-reduce is part of the graph."""
+    split the reduction is part of the graph (the peer-memory kernel, or the
+    float32 NCCL all-reduce)."""
 
     def __init__(self, block: SparseMoeBlock, tokens: int):
         dev = block.gate.weight.device
@@ -238,7 +279,9 @@ class CapturedBlock:
         self.x = torch.zeros(tokens, H, dtype=torch.bfloat16, device=dev)
         self.y = torch.empty(tokens, H, dtype=torch.bfloat16, device=dev)
         self.part = (torch.empty(tokens, H, dtype=torch.float32, device=dev)
-                     if block.sharding_group is not None else None)
+                     if block.sharding_group is not None and block.tp_reduce == "nccl" else None)
+        if block.sharding_group is not None and block.tp_reduce == "p2p":
+            block.tp_buffers(tokens, dev)          # a collective: before the capture
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):

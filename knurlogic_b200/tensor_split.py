@@ -103,10 +103,11 @@ def shard_state_dict(w: dict, rank: int, n: int, prefix: str = "mlp.") -> dict:
 
 
 def build_block(w: dict, top_k: int, rank: int = 0, n: int = 1, group=None,
-                prefix: str = "mlp."):
+                prefix: str = "mlp.", tp_reduce: str = "p2p"):
     """A SparseMoeBlock holding rank `rank`'s cut; `group` is the process
-    group its float32 partials are all-reduced over (None when n == 1)."""
+    group its partials are reduced over (None when n == 1), by the
+    peer-memory kernel (`tp_reduce="p2p"`) or NCCL ("nccl")."""
     from .moe import SparseMoeBlock
     ws = shard_state_dict(w, rank, n, prefix) if n > 1 else w
     return SparseMoeBlock.from_weights(ws, top_k, prefix=prefix,
-                                       sharding_group=group if n > 1 else None)
+                                       sharding_group=group if n > 1 else None, tp_reduce=tp_reduce)
