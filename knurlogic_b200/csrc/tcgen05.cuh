@@ -125,8 +125,8 @@ __device__ __forceinline__ void arrive_expect_tx(uint64_t *bar, uint32_t bytes) 
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
-// 2-D tensor copy global -> shared, completing on `bar` (no multicast); the
-// map is a kernel parameter (__grid_constant__)
+// 2-D tensor copy global -> this CTA's shared memory, completing on `bar`;
+// the map is a kernel parameter (__grid_constant__)
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *map, int c0, int c1, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, "

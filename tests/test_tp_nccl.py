@@ -55,8 +55,12 @@ def _rank(rank, port, q):
                 ys.append(to_np(cap(synth.make_input(CFG, seed=seed).to(dev)).clone()))
             cap.check_status()
             out[mode] = ys
-            del cap
+            del cap, blk
             torch.cuda.synchronize(dev)
+        # every rank's kernels and collectives end here, before rank 0's checks
+        # (a failed check must not leave a peer inside a collective)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
         if rank == 0:
             p = oracle_params(w)
             res = []
@@ -66,7 +70,6 @@ def _rank(rank, port, q):
                 assert_bf16_close(out["nccl"][i], ref, f"tp2 nccl call {i}")
                 res.append(int((out["p2p"][i] != out["nccl"][i]).sum()))
             q.put(res)
-        dist.barrier()
     except Exception as e:  # report, never hang the other rank's test
         q.put(f"rank {rank}: {e!r}")
         raise
