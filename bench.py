@@ -353,11 +353,13 @@ def tp_share(blocks, x, group, world, local, dev, n):
                     "the all-reduce time includes waiting for the slowest rank's block"}
 
 
-def tp_reduce_share(blocks, x, world, local, dev, n):
-    """The peer-memory path's reduction time: the timed entry's events put
-    the fused combine + reduction kernel between its last two marks; the
-    block's other stages as the rest. Averaged over n calls, max over ranks
-    (every rank makes the same calls: the kernel meets its peers inside)."""
+def tp_reduce_share(blocks, x, tp, local, dev, n):
+    """The peer-memory reduction's share of a split step. Per step the same
+    layer copy runs twice: the unsplit entry into bf16 (its combine kernel,
+    no reduction) and the split entry (the fused combine + reduction kernel,
+    which meets the peers inside), CUDA events around each; the difference
+    of the averages is what the reduction adds. Averaged over n steps, max
+    over ranks (every rank makes the same calls)."""
     import ctypes
 
     import torch
@@ -366,7 +368,7 @@ def tp_reduce_share(blocks, x, world, local, dev, n):
     from knurlogic_b200 import _lib
     T = x.shape[0]
     L = len(blocks)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(n)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
     stream = torch.cuda.current_stream(dev)
     for row in evs:
         for e in row:
@@ -380,17 +382,25 @@ def tp_reduce_share(blocks, x, world, local, dev, n):
     for i in range(n):
         b = i % L
         evs[i][0].record(stream)
+        _lib.call("vqmoe_sparse_moe_block", ctypes.byref(descs[b]), x.data_ptr(), T, out.data_ptr(),
+                  _lib.OUT_BF16, wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream)
+        evs[i][1].record(stream)
         _lib.call("vqmoe_sparse_moe_block_tp", ctypes.byref(descs[b]), ctypes.byref(tps[b]), x.data_ptr(), T,
                   out.data_ptr(), wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream)
-        evs[i][1].record(stream)
+        evs[i][2].record(stream)
     torch.cuda.synchronize(dev)
     rows = evs[min(10, n - 1):]
-    call = sum(r[0].elapsed_time(r[1]) for r in rows) / len(rows)
-    t = torch.tensor([call], device=dev)
+    plain = sum(r[0].elapsed_time(r[1]) for r in rows) / len(rows)
+    fused = sum(r[1].elapsed_time(r[2]) for r in rows) / len(rows)
+    t = torch.tensor([plain, fused], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return {"call_ms": round(float(t.item()), 5),
-            "note": "the fused combine + reduction kernel replaces combine_kernel and the NCCL all-reduce; "
-                    "its own time is in stages_ms.combine_ms (rank 0's timed entry)"}
+    plain, fused = (float(v) for v in t.tolist())
+    return {"block_ms": round(plain, 5), "split_call_ms": round(fused, 5),
+            "reduce_extra_ms": round(fused - plain, 5), "reduce_share": round((fused - plain) / fused, 4),
+            "nvlink_bytes_per_rank": 2 * T * x.shape[1] * 2 * (tp - 1) // tp,
+            "note": "the same copy run unsplit-entry (combine kernel, no reduction) then split-entry (the fused "
+                    "combine + float32 reduction over NVLink peer memory); the extra includes waiting for the "
+                    "slowest rank"}
 
 
 def quick_value(workload, tp, rank, world, local, dev, steps, warmup):
@@ -500,7 +510,7 @@ def run_ours(args, world, rank, local):
 
     comm = None
     if tp > 1:
-        comm = (tp_reduce_share(blocks, x, world, local, dev, min(args.steps, 200)) if args.tp_reduce == "p2p"
+        comm = (tp_reduce_share(blocks, x, tp, local, dev, min(args.steps, 200)) if args.tp_reduce == "p2p"
                 else tp_share(blocks, x, group, world, local, dev, min(args.steps, 200)))
         comm["reduce"] = args.tp_reduce
 

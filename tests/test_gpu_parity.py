@@ -202,11 +202,12 @@ def test_out_of_range_codes_are_refused():
         m.prepared()
 
 
-@pytest.mark.parametrize("n", [2, 4])
+@pytest.mark.parametrize("n", [2, 4, 8])
 def test_tensor_split_emulated_on_one_gpu(n):
-    """Each rank's cut of C2 (T = 16) through the C ABI with float32 output,
-    summed in float32 and rounded once: the reference's Reduce."""
-    cfg = synth.CONFIGS["c2"]
+    """Each rank's cut (T = 16) through the C ABI with float32 output,
+    summed in float32 and rounded once: the reference's Reduce. C2 for 2
+    and 4 ranks; its I 768 refuses 8, which runs at I 1536 (c4's width)."""
+    cfg = synth.CONFIGS["c2"] if n < 8 else synth.MoEConfig("tp8", 32, 8, 1024, 1536, 512, 16)
     w = synth.make_weights(cfg, seed=12, scales="random")
     x = synth.make_input(cfg, seed=12, tokens=16).to(DEV)
     acc = torch.zeros(16, cfg.hidden, dtype=torch.float32, device=DEV)

@@ -1,6 +1,6 @@
-"""The tensor split on two GPUs (skipped with fewer): each rank builds its cut
-with `tensor_split.build_block` and runs the block through the C ABI; the
-ranks' partials are reduced either by the peer-memory kernel (the combine
+"""The tensor split on 2, 4 and 8 GPUs (each skipped with fewer): each rank
+builds its cut with `tensor_split.build_block` and runs the block through
+the C ABI; the ranks' partials are reduced either by the peer-memory kernel (the combine
 and the float32 reduction in one kernel, `vqmoe_sparse_moe_block_tp`, over
 torch symmetric-memory buffers) or over NCCL. Rank 0 compares both with the
 oracle's tensor-split block and checks that they agree with each other, over
@@ -19,8 +19,8 @@ from oracle import moe_ref as R
 from tests.conftest import assert_bf16_close, oracle_params, to_np
 
 pytestmark = pytest.mark.gpu
-N = 2
-CFG = synth.MoEConfig("tp2", 16, 4, 512, 256, 128, 24)
+# I 512 and a shared I 256 leave whole scale groups on each of up to 8 ranks
+CFG = synth.MoEConfig("tpn", 16, 4, 512, 512, 256, 24)
 
 
 def _free_port():
@@ -29,7 +29,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, port, q):
+def _rank(rank, N, port, q):
     import datetime
 
     import torch.distributed as dist
@@ -66,9 +66,12 @@ def _rank(rank, port, q):
             res = []
             for i, seed in enumerate((8, 9, 10, 11, 12)):
                 ref = R.tp_sparse_moe_block(to_np(synth.make_input(CFG, seed=seed)), p, CFG.top_k, vq=True, n=N)
-                assert_bf16_close(out["p2p"][i], ref, f"tp2 p2p call {i}")
-                assert_bf16_close(out["nccl"][i], ref, f"tp2 nccl call {i}")
-                res.append(int((out["p2p"][i] != out["nccl"][i]).sum()))
+                assert_bf16_close(out["p2p"][i], ref, f"tp{N} p2p call {i}")
+                assert_bf16_close(out["nccl"][i], ref, f"tp{N} nccl call {i}")
+                a = out["p2p"][i].astype(np.float32)
+                b = out["nccl"][i].astype(np.float32)
+                ulp = np.abs(a - b) / np.maximum(np.abs(a), 1e-30)
+                res.append((int((a != b).sum()), float(ulp.max())))
             q.put(res)
     except Exception as e:  # report, never hang the other rank's test
         q.put(f"rank {rank}: {e!r}")
@@ -77,12 +80,14 @@ def _rank(rank, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < N, reason="needs 2 GPUs")
-def test_two_gpu_tensor_split_matches_the_oracle():
+@pytest.mark.parametrize("N", [2, 4, 8])
+def test_tensor_split_across_gpus_matches_the_oracle(N):
+    if torch.cuda.device_count() < N:
+        pytest.skip(f"needs {N} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, port, q)) for r in range(N)]
+    procs = [ctx.Process(target=_rank, args=(r, N, port, q)) for r in range(N)]
     for p in procs:
         p.start()
     for p in procs:
@@ -93,6 +98,11 @@ def test_two_gpu_tensor_split_matches_the_oracle():
     res = q.get(timeout=5)
     assert not isinstance(res, str), res
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    # the two reductions sum the same bf16 partials in float32: equal bits
-    # but for the order of a sum of two terms, which is exact
-    assert res == [0] * 5, res
+    # the two reductions sum the same bf16 partials in float32, the kernel in
+    # rank order and NCCL in its own: two terms give equal bits; more may
+    # round differently where the partials' magnitudes are far apart
+    if N == 2:
+        assert [d for d, _ in res] == [0] * 5, res
+    else:
+        n_out = CFG.tokens * CFG.hidden
+        assert all(d <= n_out // 1000 and u <= 2.0 ** -7 for d, u in res), res
