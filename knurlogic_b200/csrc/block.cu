@@ -404,13 +404,17 @@ static vqmoe_status side_stream(SideStream **out) {
     return VQMOE_OK;
 }
 
-// From this many tokens the shared expert runs as tcgen05 dense GEMMs.
-constexpr int kDensePrefillTokens = 256;
-
+// The shared expert on stream st: gate/up + SwiGLU into act_s, then down
+// into sh. Where both matmuls take 64-input windows, the tcgen05 kernel at
+// every token count: on its side stream it holds few SMs (one CTA per 128
+// weight rows) for longer, which costs the routed-expert kernel running
+// beside it less than a kernel spread over every SM (measured at c2: 118 us
+// per block against 121 us for the K-sliced kernels and 123 us for a
+// cluster K-split on all SMs); else the K-sliced mma.sync kernels.
 static vqmoe_status run_shared(const vqmoe_block *b, const uint16_t *x, int T, const BlockWs &w,
                                cudaStream_t st) {
     const RouteWs &rt = w.rt;
-    if (T >= kDensePrefillTokens && b->hidden % 64 == 0 && b->shared_inter % 64 == 0) {
+    if (b->hidden % 64 == 0 && b->shared_inter % 64 == 0) {
         vqmoe_status s = launch_dense_prefill(x, b->shared_gate_w, b->shared_up_w, T, b->hidden,
                                               b->shared_inter, w.act_s, w.status + 1, st);
         if (s != VQMOE_OK) return s;
