@@ -315,6 +315,19 @@ VQMOE_API vqmoe_status vqmoe_router_ex(const void *x, const void *router_w,
 VQMOE_API vqmoe_status vqmoe_rms_norm(const void *x, const void *weight, int32_t tokens,
                                       int32_t hidden, float eps, void *out, void *stream);
 
+/* The decoder stack's residual add and RMSNorm, one pass per row
+ * (DecoderLayer.__call__ and RMSNorm.__call__, qwen3_5.py:120-130, 578-587):
+ * sum = bf16(x + residual) when residual is given (written to sum_out when
+ * that is given), then norm_out = bf16(f32(f32(sum) * rs) * weight) with
+ * rs = 1 / sqrt(mean(sum^2) + eps) in float32 (the mean of the squares
+ * summed exactly, rounded once to float32) and weight [hidden] float32 --
+ * the (1 + weight) gain the reference keeps in float32. Also the per-head
+ * q/k norms of the attention (rows = tokens x heads, hidden = head_dim).
+ * x, residual, sum_out, norm_out: [rows, hidden] bf16. */
+VQMOE_API vqmoe_status vqmoe_add_rms_norm(const void *x, const void *residual, const float *weight,
+                                          int32_t rows, int32_t hidden, float eps, void *sum_out,
+                                          void *norm_out, void *stream);
+
 /* Gemma-4's Experts.__call__ (gemma4_text.py:196-214): out[T, H] bf16 =
  * sum over the k slots of bf16(y[t, s] * scores[t, s]), in fp32 and rounded
  * once, with y = vqmoe_switch_glu(gate, up, down, x, indices) (GeGLU via

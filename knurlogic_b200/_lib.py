@@ -95,6 +95,8 @@ SIGNATURES = [
      [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
       c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_rms_norm", c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),
+    ("vqmoe_add_rms_norm", c_int32,
+     [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]),
     ("vqmoe_moe_experts_workspace_size", c_size_t, [POINTER(Linear), POINTER(Linear), c_int32, c_int32]),
     ("vqmoe_moe_experts", c_int32,
      [POINTER(Linear), POINTER(Linear), POINTER(Linear), c_void_p, c_void_p, c_void_p, c_int32, c_int32,

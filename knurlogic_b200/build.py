@@ -18,7 +18,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libvqmoe.so"
 SOURCES = ("router.cu", "expert.cu", "expert_prefill.cu", "expert_ref.cu", "dense_prefill.cu", "block.cu",
-           "layout.cu", "noalloc.cu", "tp_reduce.cu")
+           "layout.cu", "noalloc.cu", "tp_reduce.cu", "decoder.cu")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
          "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr"]
