@@ -248,13 +248,23 @@ class TextModel:
     normed hidden states (for the LM head) and the hidden states before the
     final norm (what the MTP head reads: h_source "pre_norm")."""
 
-    def __init__(self, w: dict, cfg: DecoderConfig, device):
+    def __init__(self, w: dict, cfg: DecoderConfig, device, consume: bool = False):
+        """consume: drop each layer's raw expert tensors from `w` once its
+        MoE block has converted them (halves the peak memory of a build)."""
         self.cfg = cfg
         self.embed_tokens = w["model.embed_tokens.weight"]
-        self.layers = [DecoderLayer(w, f"model.layers.{i}.", cfg) for i in range(cfg.layers)]
+        self.layers = []
+        for i in range(cfg.layers):
+            self.layers.append(DecoderLayer(w, f"model.layers.{i}.", cfg))
+            if consume:
+                _drop(w, f"model.layers.{i}.mlp.switch_mlp.")
+                _release(self.layers[-1].mlp)
         self.norm = _gain(w["model.norm.weight"])
         self.lm_head = w["lm_head.weight"]
         self.mtp = MTPHead(w, cfg, self) if cfg.mtp else None
+        if consume and self.mtp is not None:
+            _drop(w, "mtp.layers.0.mlp.switch_mlp.")
+            _release(self.mtp.layer.mlp)
         share_workspace([l.mlp for l in self.all_layers()], device)
 
     def all_layers(self):
@@ -310,6 +320,20 @@ class MTPHead:
         return normed, pre
 
 
+def _release(block: SparseMoeBlock) -> None:
+    """Drop the artifact-layout copies of a block's VQ experts (the kernels
+    read their own layout)."""
+    sw = block.switch_mlp
+    for lin in (sw.gate_proj, sw.up_proj, sw.down_proj):
+        if hasattr(lin, "release_source"):
+            lin.release_source()
+
+
+def _drop(w: dict, prefix: str) -> None:
+    for k in [k for k in w if k.startswith(prefix)]:
+        del w[k]
+
+
 def share_workspace(blocks: list, device, tokens: int = 2048) -> None:
     """One scratch for every layer's MoE block: the layers run one after
     another on one stream, so a single workspace (sized for the largest
@@ -325,7 +349,7 @@ def share_workspace(blocks: list, device, tokens: int = 2048) -> None:
 def build(cfg: DecoderConfig, seed: int = 0, device="cuda") -> TextModel:
     """A random-init decoder (weights generated on `device`)."""
     dev = torch.device(device)
-    return TextModel(make_weights(cfg, seed=seed, device=dev), cfg, dev)
+    return TextModel(make_weights(cfg, seed=seed, device=dev), cfg, dev, consume=True)
 
 
 # -------------------------------------------------------------- generation

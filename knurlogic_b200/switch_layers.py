@@ -222,6 +222,8 @@ class VQSwitchLinear(_SwitchBase):
         (one host synchronisation, at first use: call it before capturing a
         CUDA graph)."""
         c, vs = self.codes, self.vq_scales
+        if c.is_meta:                                    # released: the device layout is all there is
+            return self._dev[1], self._dev[2]
         require_cuda(c, vs)
         key = (c.device, c.data_ptr(), c._version, vs.data_ptr(), vs._version)
         if self._dev is None or self._dev[0] != key:
@@ -245,6 +247,20 @@ class VQSwitchLinear(_SwitchBase):
             self._dev = (key, dc, ds)
         return self._dev[1], self._dev[2]
 
+    def release_source(self) -> None:
+        """Keep only what the kernels read. On the fast path the tiled
+        device layout is a converted copy of `codes` and `vq_scales`; this
+        drops the artifact-layout tensors (they become shape-only tensors on
+        the meta device, so `num_experts` / `output_dims` / `input_dims`
+        still answer) to halve the module's device memory -- for a whole
+        model held on one GPU. The reference layout is the kernels' own
+        (nothing to drop)."""
+        if not self.fast or self.codes.is_meta:
+            return
+        self.prepared()
+        self.codes = torch.empty(self.codes.shape, dtype=self.codes.dtype, device="meta")
+        self.vq_scales = torch.empty(self.vq_scales.shape, dtype=self.vq_scales.dtype, device="meta")
+
     def descriptor(self) -> _lib.Linear:
         dc, ds = self.prepared()
         require_cuda(self.codebook)
@@ -264,7 +280,7 @@ class VQSwitchLinear(_SwitchBase):
         21-33`)."""
         count = self.num_experts - first if count is None else count
         out = torch.empty((count, self.output_dims, self.input_dims),
-                          dtype=torch.float16, device=self.codes.device)
+                          dtype=torch.float16, device=self.codebook.device)
         d = self.descriptor()
         _lib.call("vqmoe_dequant", ctypes_ref(d), first, count, out.data_ptr(),
                   _stream(out))

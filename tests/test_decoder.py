@@ -162,3 +162,17 @@ def test_mtp_on_a_one_layer_trunk_with_two_drafts():
     drafted, stats = decoder.generate_mtp(model, prompts, 16, k=2)
     assert torch.equal(plain, drafted)
     assert 0 <= stats["accepted"] <= stats["drafted"]
+
+
+@pytest.mark.gpu
+def test_released_sources_leave_the_block_unchanged():
+    cfg = synth.MoEConfig("r", 8, 2, 256, 256, 128, 12)
+    w = synth.make_weights(cfg, seed=9, device=DEV, scales="random")
+    from knurlogic_b200 import SparseMoeBlock
+    blk = SparseMoeBlock.from_weights(w, cfg.top_k)
+    x = synth.make_input(cfg, seed=9).to(DEV)
+    before = blk(x)
+    decoder._release(blk)
+    up = blk.switch_mlp.up_proj
+    assert up.codes.is_meta and (up.num_experts, up.output_dims, up.input_dims) == (8, 256, 256)
+    assert torch.equal(blk(x), before)
