@@ -151,7 +151,13 @@ class KVCache:
         return self.k.shape[1]
 
 
-def rope(x: torch.Tensor, pos0: int, dims: int, base: float) -> torch.Tensor:
+def _positions(pos0, L: int, device) -> torch.Tensor:
+    """pos0 .. pos0 + L - 1 on the device; pos0 an int, or a 0-d int64
+    device tensor (a CUDA graph's position, advanced between replays)."""
+    return torch.arange(L, device=device) + pos0
+
+
+def rope(x: torch.Tensor, pos0, dims: int, base: float) -> torch.Tensor:
     """mlx `nn.RoPE(dims, traditional=False, base)` at offset pos0 over the
     first `dims` features of each head (x [B, L, heads, d] bf16): the two
     halves of those features rotated by pos * base^(-2i/dims), in float32,
@@ -159,7 +165,8 @@ def rope(x: torch.Tensor, pos0: int, dims: int, base: float) -> torch.Tensor:
     L = x.shape[1]
     half = dims // 2
     inv = base ** (-torch.arange(0, half, device=x.device, dtype=torch.float32) * 2.0 / dims)
-    ang = torch.arange(pos0, pos0 + L, device=x.device, dtype=torch.float32)[:, None] * inv[None, :]
+    pos = _positions(pos0, L, x.device).to(torch.float32)
+    ang = pos[:, None] * inv[None, :]
     cos, sin = torch.cos(ang)[None, :, None, :], torch.sin(ang)[None, :, None, :]
     xf = x[..., :dims].float()
     x1, x2 = xf[..., :half], xf[..., half:]
@@ -182,7 +189,10 @@ class Attention:
         self.q_norm = _gain(w[p + "q_norm.weight"])
         self.k_norm = _gain(w[p + "k_norm.weight"])
 
-    def __call__(self, x: torch.Tensor, cache: KVCache, pos0: int) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, cache: KVCache, pos0) -> torch.Tensor:
+        """pos0: the first new position -- an int, or a 0-d device tensor,
+        with which the step reads the whole cache under a mask and so can
+        be captured in a CUDA graph and replayed at any position."""
         c = self.cfg
         B, L, _ = x.shape
         nh, kv, d = c.heads, c.kv_heads, c.head_dim
@@ -193,21 +203,40 @@ class Attention:
         values = F.linear(x, self.wv).view(B, L, kv, d)
         queries = rope(queries, pos0, c.rotary_dims, c.rope_theta)
         keys = rope(keys, pos0, c.rotary_dims, c.rope_theta)
+        rep = nh // kv
+        if torch.is_tensor(pos0):
+            idx = _positions(pos0, L, x.device)
+            cache.k.index_copy_(1, idx, keys)
+            cache.v.index_copy_(1, idx, values)
+            Q = queries.view(B, L, kv, rep, d).permute(0, 2, 3, 1, 4).reshape(B, kv, rep * L, d)
+            mask = torch.arange(cache.max_len, device=x.device)[None, :] <= idx.repeat(rep)[:, None]
+            o = F.scaled_dot_product_attention(Q, cache.k.transpose(1, 2), cache.v.transpose(1, 2), attn_mask=mask,
+                                               scale=d ** -0.5)
+            o = o.view(B, kv, rep, L, d).permute(0, 3, 1, 2, 4).reshape(B, L, nh * d)
+            return F.linear(o * _sigmoid_bf16(gate), self.wo)
         if pos0 + L > cache.max_len:
             raise ValueError(f"KV cache of {cache.max_len} positions: writing {pos0}..{pos0 + L}")
         cache.k[:, pos0:pos0 + L] = keys
         cache.v[:, pos0:pos0 + L] = values
         S = pos0 + L
-        Q = queries.transpose(1, 2)
-        K = cache.k[:, :S].transpose(1, 2)
+        K = cache.k[:, :S].transpose(1, 2)                     # [B, kv, S, d]
         V = cache.v[:, :S].transpose(1, 2)
         if pos0 == 0:
-            o = F.scaled_dot_product_attention(Q, K, V, is_causal=True, scale=d ** -0.5, enable_gqa=True)
+            o = F.scaled_dot_product_attention(queries.transpose(1, 2), K, V, is_causal=True, scale=d ** -0.5,
+                                               enable_gqa=True).transpose(1, 2)
         else:
-            # query l (position pos0 + l) sees keys 0 .. pos0 + l
-            mask = torch.arange(S, device=x.device)[None, :] <= (pos0 + torch.arange(L, device=x.device))[:, None]
-            o = F.scaled_dot_product_attention(Q, K, V, attn_mask=mask, scale=d ** -0.5, enable_gqa=True)
-        o = o.transpose(1, 2).reshape(B, L, nh * d)
+            # decode / verify: the query heads of one key-value head become
+            # rows of one attention over that head's keys (no copies of K, V);
+            # row (r, l), position pos0 + l, sees keys 0 .. pos0 + l
+            Q = queries.view(B, L, kv, rep, d).permute(0, 2, 3, 1, 4).reshape(B, kv, rep * L, d)
+            if L == 1:
+                o = F.scaled_dot_product_attention(Q, K, V, scale=d ** -0.5)
+            else:
+                qpos = (pos0 + torch.arange(L, device=x.device)).repeat(rep)
+                mask = torch.arange(S, device=x.device)[None, :] <= qpos[:, None]
+                o = F.scaled_dot_product_attention(Q, K, V, attn_mask=mask, scale=d ** -0.5)
+            o = o.view(B, kv, rep, L, d).permute(0, 3, 1, 2, 4)
+        o = o.reshape(B, L, nh * d)
         return F.linear(o * _sigmoid_bf16(gate), self.wo)
 
 
@@ -355,27 +384,98 @@ def build(cfg: DecoderConfig, seed: int = 0, device="cuda") -> TextModel:
 # -------------------------------------------------------------- generation
 
 def _argmax(model: TextModel, normed: torch.Tensor) -> torch.Tensor:
-    return model.logits(normed).argmax(dim=-1)
+    """The greedy choice from float32 logits (bf16 operands, float32
+    output): at a vocabulary of 152k the bf16-rounded logits tie often, and
+    a tie would be broken by rounding noise that differs between a 1-wide
+    and a (k+1)-wide forward."""
+    H = normed.shape[-1]
+    lg = torch.mm(normed.reshape(-1, H), model.lm_head.t(), out_dtype=torch.float32)
+    return lg.argmax(dim=-1).view(normed.shape[:-1])
+
+
+class _Captured:
+    """`fn` (no arguments; it reads static input tensors the caller fills
+    between calls) captured as one CUDA graph; calling replays it and
+    returns its static outputs. One eager run before the capture warms the
+    kernels: its cache writes land on positions the first replay writes
+    again before anything reads them."""
+
+    def __init__(self, fn):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = fn()
+
+    def __call__(self):
+        self.graph.replay()
+        return self.out
+
+
+class _Clock:
+    """CUDA events at the end of the prefill and of the decoding; the
+    device times land in `stats` (prefill_ms, decode_ms) at the end."""
+
+    def __init__(self, stats: dict | None):
+        self.stats = stats
+        self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if stats is not None else None
+        if self.ev:
+            self.ev[0].record()
+
+    def mark(self, i: int):
+        if self.ev:
+            self.ev[i].record()
+
+    def done(self):
+        if self.ev:
+            self.ev[2].record()
+            self.ev[2].synchronize()
+            self.stats["prefill_ms"] = self.ev[0].elapsed_time(self.ev[1])
+            self.stats["decode_ms"] = self.ev[1].elapsed_time(self.ev[2])
 
 
 @torch.no_grad()
-def generate_greedy(model: TextModel, prompts: torch.Tensor, steps: int) -> torch.Tensor:
+def generate_greedy(model: TextModel, prompts: torch.Tensor, steps: int, graphs: bool = False,
+                    stats: dict | None = None) -> torch.Tensor:
     """Plain greedy decoding: the prompt in one forward, then one token per
-    forward. prompts [B, P] int64 -> the next `steps` tokens [B, steps]."""
+    forward. prompts [B, P] int64 -> the next `steps` tokens [B, steps].
+    graphs: each one-token step is one CUDA-graph replay (the position a
+    device tensor). stats: filled with the device time of the prefill (and
+    first token) and of the decoding (prefill_ms, decode_ms)."""
     B, P = prompts.shape
+    clock = _Clock(stats)
     caches = model.new_caches(B, P + steps + 1, prompts.device)
     normed, _ = model(prompts, caches, 0)
     nxt = _argmax(model, normed[:, -1])
+    clock.mark(1)
     out = [nxt]
-    for s in range(1, steps):
-        normed, _ = model(nxt[:, None], caches, P + s - 1)
-        nxt = _argmax(model, normed[:, -1])
-        out.append(nxt)
+    if graphs and steps > 1:
+        tok = nxt[:, None].clone()
+        pos = torch.full((), P, dtype=torch.int64, device=prompts.device)
+
+        def step():
+            return _argmax(model, model(tok, caches, pos)[0][:, -1])
+
+        g = _Captured(step)
+        for _ in range(1, steps):
+            y = g()
+            out.append(y.clone())
+            tok.copy_(y[:, None])
+            pos.add_(1)
+    else:
+        for s in range(1, steps):
+            normed, _ = model(nxt[:, None], caches, P + s - 1)
+            nxt = _argmax(model, normed[:, -1])
+            out.append(nxt)
+    clock.done()
     return torch.stack(out, dim=1)
 
 
 @torch.no_grad()
-def generate_mtp(model: TextModel, prompts: torch.Tensor, steps: int, k: int = 3):
+def generate_mtp(model: TextModel, prompts: torch.Tensor, steps: int, k: int = 3, graphs: bool = False):
     """Greedy decoding with the MTP head drafting k tokens a step and one
     (k+1)-wide trunk forward verifying them (block_loop.py's loop, greedy
     verdicts): every row commits the same count, m = the fewest drafts any
@@ -384,12 +484,16 @@ def generate_mtp(model: TextModel, prompts: torch.Tensor, steps: int, k: int = 3
     m. The head's cache takes only committed positions, from the verify's
     hidden states (a (k+1)-row head forward that also gives the next first
     draft); drafts 2..k chain the head on its own output.
-    Returns (tokens [B, steps], {"steps", "drafted", "accepted"}); the tokens
-    are plain greedy decoding's."""
+    graphs: the verify, the head's catch-up and its one-row draft each
+    replay as one CUDA graph; one host read per step (m).
+    Returns (tokens [B, steps], {"steps", "drafted", "accepted",
+    "prefill_ms", "decode_ms"}); the tokens are plain greedy decoding's."""
     if model.mtp is None:
         raise ValueError("the model has no MTP head")
     B, P = prompts.shape
     dev = prompts.device
+    stats = {"steps": 0, "drafted": 0, "accepted": 0}
+    clock = _Clock(stats)
     max_len = P + steps + 2 * k + 2
     caches = model.new_caches(B, max_len, dev)
     hc = model.mtp.new_cache(B, max_len, dev)
@@ -399,27 +503,70 @@ def generate_mtp(model: TextModel, prompts: torch.Tensor, steps: int, k: int = 3
     hn, hp = model.mtp(pre, torch.cat([prompts[:, 1:], t1[:, None]], dim=1), hc, 0)
     g = hp[:, -1:]
     drafts = [_argmax(model, hn[:, -1])]
+    del normed, pre, hn, hp
+    clock.mark(1)                                                    # (the graph captures count as decoding)
     L = P                                                            # committed trunk positions
     out = [t1]
-    stats = {"steps": 0, "drafted": 0, "accepted": 0}
+    if graphs:
+        H = model.cfg.hidden
+        vtok = torch.zeros((B, k + 1), dtype=torch.int64, device=dev)
+        vpos = torch.full((), L, dtype=torch.int64, device=dev)
+        dtok = torch.zeros((B, 1), dtype=torch.int64, device=dev)
+        dg = torch.zeros((B, 1, H), dtype=torch.bfloat16, device=dev)
+        dpos = torch.full((), L, dtype=torch.int64, device=dev)
+
+        def fv():
+            n, p = model(vtok, caches, vpos)
+            return _argmax(model, n), p
+
+        verify = _Captured(fv)
+        vy, vpre = verify.out
+
+        def fc():
+            n, p = model.mtp(vpre, vy, hc, vpos)
+            return _argmax(model, n), p
+
+        def fd():
+            n, p = model.mtp(dg, dtok, hc, dpos)
+            return _argmax(model, n)[:, 0], p
+
+        catchup, draft = _Captured(fc), _Captured(fd)
     while len(out) < steps:
         for i in range(1, k):                                        # head rows L .. L + k - 2
-            hn, g = model.mtp(g, drafts[-1][:, None], hc, L - 1 + i)
-            drafts.append(_argmax(model, hn[:, -1]))
+            if graphs:
+                dg.copy_(g)
+                dtok.copy_(drafts[-1][:, None])
+                dpos.fill_(L - 1 + i)
+                di, g = draft()
+                drafts.append(di.clone())
+            else:
+                hn, g = model.mtp(g, drafts[-1][:, None], hc, L - 1 + i)
+                drafts.append(_argmax(model, hn[:, -1]))
         d = torch.stack(drafts, dim=1)                               # [B, k]
-        normed, pre = model(torch.cat([t1[:, None], d], dim=1), caches, L)   # trunk rows L .. L + k
-        y = _argmax(model, normed)                                   # [B, k + 1]
+        if graphs:                                                   # trunk rows L .. L + k
+            vtok[:, 0] = t1
+            vtok[:, 1:] = d
+            vpos.fill_(L)
+            y, pre = verify()
+        else:
+            normed, pre = model(torch.cat([t1[:, None], d], dim=1), caches, L)
+            y = _argmax(model, normed)                               # [B, k + 1]
         agree = torch.cumprod((d == y[:, :k]).to(torch.int32), dim=1).sum(dim=1)
         m = int(agree.min().item())
         stats["steps"] += 1
         stats["drafted"] += B * k
         stats["accepted"] += B * m
         out.extend(drafts[:m])
-        t1 = y[:, m]
+        t1 = y[:, m].clone()
         out.append(t1)
         # head rows L .. L + k: (trunk hidden at L + i, token L + i + 1 = y_i for i <= m)
-        hn, hp = model.mtp(pre, y, hc, L)
-        g = hp[:, m:m + 1]
-        drafts = [_argmax(model, hn[:, m])]
+        if graphs:
+            hy, hp = catchup()
+            drafts = [hy[:, m].clone()]
+        else:
+            hn, hp = model.mtp(pre, y, hc, L)
+            drafts = [_argmax(model, hn[:, m])]
+        g = hp[:, m:m + 1].clone()
         L += m + 1
+    clock.done()
     return torch.stack(out[:steps], dim=1), stats

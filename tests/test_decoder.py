@@ -176,3 +176,17 @@ def test_released_sources_leave_the_block_unchanged():
     up = blk.switch_mlp.up_proj
     assert up.codes.is_meta and (up.num_experts, up.output_dims, up.input_dims) == (8, 256, 256)
     assert torch.equal(blk(x), before)
+
+
+@pytest.mark.gpu
+def test_graph_replayed_decoding_emits_the_same_tokens():
+    """Each decode step as one CUDA-graph replay (the position a device
+    tensor, the whole cache read under a mask) gives the eager loop's tokens,
+    for plain greedy decoding and for MTP drafting."""
+    w = decoder.make_weights(TINY, seed=7, device=DEV)
+    model = decoder.TextModel(w, TINY, torch.device(DEV))
+    prompts = torch.randint(0, TINY.vocab, (3, 12), generator=torch.Generator().manual_seed(7)).to(DEV)
+    plain = decoder.generate_greedy(model, prompts, 20)
+    assert torch.equal(decoder.generate_greedy(model, prompts, 20, graphs=True), plain)
+    drafted, stats = decoder.generate_mtp(model, prompts, 20, k=3, graphs=True)
+    assert torch.equal(drafted, plain) and stats["steps"] > 0
