@@ -64,6 +64,10 @@ def parse():
     ap.add_argument("--workload", default=None,
                     help="c1..c4 (default: c2 on one GPU, c4 split N ways on N GPUs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true",
+                    help="skip the C5 decoder figure (build, two 8192-token prefills of 32 sequences)")
+    ap.add_argument("--decoder-tokens", type=int, default=17,
+                    help="generated tokens timed per sequence in the C5 decoder figure")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the secondary figures (prefill c3, c4 unsplit, c2 replicas)")
     ap.add_argument("--tp", type=int, default=None,
@@ -403,6 +407,46 @@ def tp_reduce_share(blocks, x, tp, local, dev, n):
                     "slowest rank"}
 
 
+def decoder_profile(dev, gen, batch=32, prompt=8192, k=3):
+    """The baseline's C5 decoder (48 layers, hidden 4096, GQA 32/4 x 128,
+    256 VQ experts top-8 + a shared expert, vocab 151936, a one-layer MTP
+    head drafting 3) with random-init weights on ONE B200: 32 sequences of
+    8192 uniform random prompt tokens, then the first `gen` generated tokens
+    by plain greedy decoding and by MTP drafting, each decode step a CUDA
+    graph replay; device times by CUDA events. Random weights make the
+    head's drafts unrelated to the trunk's choices (acceptance near 0), so
+    the MTP figure is the cost of a verify step, not a speed-up."""
+    import torch
+
+    from knurlogic_b200 import decoder
+    cfg = decoder.CONFIGS["c5"]
+    torch.cuda.empty_cache()
+    model = decoder.build(cfg, seed=1, device=dev)
+    g = torch.Generator(device=dev).manual_seed(2)
+    prompts = torch.randint(0, cfg.vocab, (batch, prompt), generator=g, device=dev)
+    decoder.generate_greedy(model, prompts[:, :64], 4, graphs=True)          # warm-up
+    decoder.generate_mtp(model, prompts[:, :64], 4, k=k, graphs=True)
+    sg = {}
+    plain = decoder.generate_greedy(model, prompts, gen, graphs=True, stats=sg)
+    toks, sm = decoder.generate_mtp(model, prompts, gen, k=k, graphs=True)
+    r = {"workload": "c5", "layers": cfg.layers, "hidden": cfg.hidden, "heads": f"{cfg.heads}/{cfg.kv_heads}x{cfg.head_dim}",
+         "experts": f"{cfg.moe.experts} top-{cfg.moe.top_k}, I {cfg.moe.inter}, shared {cfg.moe.shared_inter}",
+         "vocab": cfg.vocab, "sequences": batch, "prompt_tokens": prompt, "generated_tokens_timed": gen,
+         "n_gpus": 1, "weights_gb": round(torch.cuda.memory_allocated(dev) / 1e9, 1),
+         "prefill_ms": round(sg["prefill_ms"], 1),
+         "prefill_tokens_per_s": round(batch * prompt / (sg["prefill_ms"] / 1e3), 1),
+         "greedy_ms_per_step": round(sg["decode_ms"] / (gen - 1), 3),
+         "greedy_tokens_per_s": round(batch * (gen - 1) / (sg["decode_ms"] / 1e3), 1),
+         "mtp_steps": sm["steps"], "mtp_ms_per_step": round(sm["decode_ms"] / max(sm["steps"], 1), 3),
+         "mtp_tokens_per_s": round(batch * (gen - 1) / (sm["decode_ms"] / 1e3), 1),
+         "mtp_acceptance": round(sm["accepted"] / max(sm["drafted"], 1), 4),
+         "mtp_tokens_equal_greedy": bool(torch.equal(plain, toks)),
+         "note": "one B200 (the baseline's C5 names 8 at TP=8); the first tokens of the 512; random-init weights"}
+    del model, prompts
+    torch.cuda.empty_cache()
+    return r
+
+
 def quick_value(workload, tp, rank, world, local, dev, steps, warmup):
     """tokens/s of `workload` split tp ways (world / tp replicas), graph
     replays over layer copies: a secondary figure beside the headline."""
@@ -540,6 +584,8 @@ def run_ours(args, world, rank, local):
         if world == 1 and workload == "c2":
             secondary["prefill"] = prefill_profile(dev)
             secondary["c4_tp1"] = quick_value("c4", 1, rank, world, local, dev, 100, 5)
+            if not args.no_decoder:
+                secondary["decoder_c5"] = decoder_profile(dev, args.decoder_tokens)
         elif world > 1 and tp > 1:
             secondary["c2_replicas"] = quick_value("c2", 1, rank, world, local, dev, 200, 10)
 

@@ -444,13 +444,13 @@ def generate_greedy(model: TextModel, prompts: torch.Tensor, steps: int, graphs:
     forward. prompts [B, P] int64 -> the next `steps` tokens [B, steps].
     graphs: each one-token step is one CUDA-graph replay (the position a
     device tensor). stats: filled with the device time of the prefill (and
-    first token) and of the decoding (prefill_ms, decode_ms)."""
+    first token; with graphs, the capture too) and of the decoding
+    (prefill_ms, decode_ms)."""
     B, P = prompts.shape
     clock = _Clock(stats)
     caches = model.new_caches(B, P + steps + 1, prompts.device)
     normed, _ = model(prompts, caches, 0)
     nxt = _argmax(model, normed[:, -1])
-    clock.mark(1)
     out = [nxt]
     if graphs and steps > 1:
         tok = nxt[:, None].clone()
@@ -460,12 +460,14 @@ def generate_greedy(model: TextModel, prompts: torch.Tensor, steps: int, graphs:
             return _argmax(model, model(tok, caches, pos)[0][:, -1])
 
         g = _Captured(step)
+        clock.mark(1)                                                # (the capture is not decoding)
         for _ in range(1, steps):
             y = g()
             out.append(y.clone())
             tok.copy_(y[:, None])
             pos.add_(1)
     else:
+        clock.mark(1)
         for s in range(1, steps):
             normed, _ = model(nxt[:, None], caches, P + s - 1)
             nxt = _argmax(model, normed[:, -1])
@@ -504,7 +506,6 @@ def generate_mtp(model: TextModel, prompts: torch.Tensor, steps: int, k: int = 3
     g = hp[:, -1:]
     drafts = [_argmax(model, hn[:, -1])]
     del normed, pre, hn, hp
-    clock.mark(1)                                                    # (the graph captures count as decoding)
     L = P                                                            # committed trunk positions
     out = [t1]
     if graphs:
@@ -531,6 +532,7 @@ def generate_mtp(model: TextModel, prompts: torch.Tensor, steps: int, k: int = 3
             return _argmax(model, n)[:, 0], p
 
         catchup, draft = _Captured(fc), _Captured(fd)
+    clock.mark(1)                                                    # (the captures are not decoding)
     while len(out) < steps:
         for i in range(1, k):                                        # head rows L .. L + k - 2
             if graphs:
