@@ -452,11 +452,32 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
             return check_launch("side stream join");
     }
     const RouteWs &rt = w.rt;
-    s = launch_router_route(x, static_cast<const uint16_t *>(b->router_w),
-                            shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr,
-                            T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, rt.cnt, rt.off,
-                            rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, b->router_mode, st);
-    if (s != VQMOE_OK || (s = mark(ev, n_ev, 1, st)) != VQMOE_OK) return s;
+    const uint16_t *rw = static_cast<const uint16_t *>(b->router_w);
+    const uint16_t *sgw = shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr;
+    if (tp) {
+        // under a split each rank routes T / n of the tokens (the exact
+        // logits are the router's cost and the same on every rank), then
+        // the ranks exchange the routing over peer memory (with one rank,
+        // the same path over its own buffer)
+        const int r0 = (int)((long long)T * tp->rank / tp->n), r1 = (int)((long long)T * (tp->rank + 1) / tp->n);
+        const int E1 = E + (sgw ? 1 : 0);
+        if (vq_in && (s = launch_to_f16(x, w.x16, (size_t)T * H, st)) != VQMOE_OK) return s;
+        if (r1 > r0 && (s = launch_router(x + (size_t)r0 * H, rw, sgw, r1 - r0, H, E, k, w.logits + (size_t)r0 * E1,
+                                          w.inds + (size_t)r0 * k, w.scores + (size_t)r0 * k,
+                                          w.sgate + r0, nullptr, b->router_mode, nullptr, st)) != VQMOE_OK)
+            return s;
+        TpArgs g = *tp;
+        g.err = w.status;
+        if ((s = launch_tp_gather(w.inds, w.scores, sgw ? w.sgate : nullptr, T, k, H, r0, r1, g, st)) != VQMOE_OK ||
+            (s = launch_route(w.inds, P, E, rt.cnt, rt.off, rt.list, rt.active, rt.rank, rt.zero, rt.zero_words,
+                              st)) != VQMOE_OK)
+            return s;
+    } else {
+        s = launch_router_route(x, rw, sgw, T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, rt.cnt, rt.off,
+                                rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, b->router_mode, st);
+        if (s != VQMOE_OK) return s;
+    }
+    if ((s = mark(ev, n_ev, 1, st)) != VQMOE_OK) return s;
     // the routed experts: gate/up + SwiGLU, then down (x routing weight)
     RoutedIO r1 = routed_io(rt, E, k, P, vq_in ? (const void *)w.x16 : (const void *)x, 0, w.act,
                             vq_dn, nullptr);
@@ -621,7 +642,7 @@ vqmoe_status vqmoe_sparse_moe_block(const vqmoe_block *blk, const void *x, int32
 size_t vqmoe_tp_buffer_bytes(int32_t hidden, int32_t tokens) {
     if (hidden <= 0 || tokens <= 0) return 0;
     const size_t T = (size_t)std::min<int>(tokens, kMaxTokensPerLaunch);
-    return kTpFlagBytes + 2 * T * (size_t)hidden * sizeof(uint16_t);
+    return tp_route_offset((int)T, hidden) + tp_route_bytes((int)T, 32);   // top_k <= 32
 }
 
 vqmoe_status vqmoe_sparse_moe_block_tp(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x, int32_t tokens,

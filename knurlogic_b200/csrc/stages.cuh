@@ -66,6 +66,14 @@ struct TpArgs {
 };
 vqmoe_status launch_tp_reduce(const uint16_t *ybuf, int T, int k, int H, const uint16_t *sh, const float *sg,
                               const TpArgs &a, uint16_t *out, cudaStream_t stream);
+// The split router's routing region in each rank's buffer (after the
+// partial and the result: [T][k] int32 expert ids, [T][k] float weights,
+// [T] float shared-expert gates), and the exchange that fills every rank's
+// routing arrays from the ranks' slices [r0, r1).
+size_t tp_route_offset(int T, int H);
+size_t tp_route_bytes(int T, int k);
+vqmoe_status launch_tp_gather(int32_t *inds, float *scores, float *sgate, int T, int k, int H, int r0, int r1,
+                              const TpArgs &a, cudaStream_t stream);
 
 // The routed experts with reference-layout VQ weights (VQMOE_FMT_VQ_REF):
 // phase 1 (r1, may be null) then phase 2, two launches.

@@ -38,7 +38,7 @@ namespace tp {
 
 // flag words of a rank's buffer
 constexpr int kEpoch = 0, kCountA = 1, kCountB = 2, kCountC = 3;
-constexpr int kArriveA = 8, kArriveB = 8 + kTpMaxRanks;
+constexpr int kArriveA = 8, kArriveB = 8 + kTpMaxRanks, kArriveG = 8 + 2 * kTpMaxRanks;
 
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
@@ -55,6 +55,12 @@ __device__ __forceinline__ uint4 ld_cv_v4(const void *p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p)
                  : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ld_cv_u32(const void *p) {
+    uint32_t v;
+    asm volatile("ld.global.cv.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -182,7 +188,69 @@ tp_reduce_kernel(const uint16_t *__restrict__ ybuf, int T, int k, int H, const u
     }
 }
 
+// The split router's exchange (one CTA): this rank routed tokens [r0, r1);
+// their expert ids, routing weights and shared-expert gates go into every
+// rank's routing region, the ranks meet at a flag barrier (kArriveG, the
+// call's epoch, bounded), and each rank copies the whole routing from its
+// own region back into its workspace arrays.
+__global__ void __launch_bounds__(256)
+tp_gather_kernel(int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate, int T, int k,
+                 int r0, int r1, size_t route_off, const TpArgs a) {
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(flags_of(a, a.rank) + kEpoch);
+    const int tid = threadIdx.x;
+    const int nk = (r1 - r0) * k;
+    for (int q = 0; q < a.n; ++q) {
+        uint8_t *reg = a.base[q] + route_off;
+        int32_t *ri = reinterpret_cast<int32_t *>(reg);
+        float *rs = reinterpret_cast<float *>(reg + (size_t)T * k * 4);
+        float *rg = reinterpret_cast<float *>(reg + (size_t)T * k * 8);
+        for (int i = tid; i < nk; i += blockDim.x) {
+            ri[r0 * k + i] = inds[r0 * k + i];
+            rs[r0 * k + i] = scores[r0 * k + i];
+        }
+        if (sgate)
+            for (int i = tid; i < r1 - r0; i += blockDim.x) rg[r0 + i] = sgate[r0 + i];
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        for (int q = 0; q < a.n; ++q) st_release_sys(flags_of(a, q) + kArriveG + a.rank, epoch + 1);
+        const long polls = a.wait_polls ? (long)a.wait_polls : (1L << 22);
+        const uint32_t *mine = flags_of(a, a.rank);
+        for (int q = 0; q < a.n; ++q) {
+            unsigned ns = 32;
+            for (long i = 1;; ++i) {
+                if (ld_acquire_sys(mine + kArriveG + q) >= epoch + 1) break;
+                if (i >= polls) {
+                    atomicExch(a.err, kWaitDependency);
+                    break;
+                }
+                __nanosleep(ns);
+                if (ns < 1024) ns <<= 1;
+            }
+        }
+    }
+    __syncthreads();
+    const uint8_t *reg = a.base[a.rank] + route_off;
+    for (int i = tid; i < T * k; i += blockDim.x) {
+        inds[i] = (int32_t)ld_cv_u32(reg + (size_t)i * 4);
+        scores[i] = __uint_as_float(ld_cv_u32(reg + ((size_t)T * k + i) * 4));
+    }
+    if (sgate)
+        for (int i = tid; i < T; i += blockDim.x) sgate[i] = __uint_as_float(ld_cv_u32(reg + ((size_t)2 * T * k + i) * 4));
+}
+
 }  // namespace tp
+
+size_t tp_route_offset(int T, int H) { return kTpFlagBytes + 2 * (size_t)T * H * sizeof(uint16_t); }
+
+size_t tp_route_bytes(int T, int k) { return ((size_t)2 * T * k + T) * 4; }
+
+vqmoe_status launch_tp_gather(int32_t *inds, float *scores, float *sgate, int T, int k, int H, int r0, int r1,
+                              const TpArgs &a, cudaStream_t stream) {
+    tp::tp_gather_kernel<<<1, 256, 0, stream>>>(inds, scores, sgate, T, k, r0, r1, tp_route_offset(T, H), a);
+    return check_launch("tp_gather_kernel");
+}
 
 vqmoe_status launch_tp_reduce(const uint16_t *ybuf, int T, int k, int H, const uint16_t *sh, const float *sg,
                               const TpArgs &a, uint16_t *out, cudaStream_t stream) {
