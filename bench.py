@@ -358,12 +358,13 @@ def tp_share(blocks, x, group, world, local, dev, n):
 
 
 def tp_reduce_share(blocks, x, tp, local, dev, n):
-    """The peer-memory reduction's share of a split step. Per step the same
-    layer copy runs twice: the unsplit entry into bf16 (its combine kernel,
-    no reduction) and the split entry (the fused combine + reduction kernel,
-    which meets the peers inside), CUDA events around each; the difference
-    of the averages is what the reduction adds. Averaged over n steps, max
-    over ranks (every rank makes the same calls)."""
+    """The split block's stages and the reduction's share. Per step the same
+    layer copy runs twice: the unsplit entry into bf16 (the whole router,
+    its combine kernel, no reduction) and the split entry with events
+    between its stages (router on T/n tokens + routing exchange + sort,
+    routed experts, side-stream join, the fused combine + float32 reduction
+    over NVLink peer memory). Averages over n steps, max over ranks (every
+    rank makes the same calls)."""
     import ctypes
 
     import torch
@@ -372,7 +373,7 @@ def tp_reduce_share(blocks, x, tp, local, dev, n):
     from knurlogic_b200 import _lib
     T = x.shape[0]
     L = len(blocks)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(n)]
     stream = torch.cuda.current_stream(dev)
     for row in evs:
         for e in row:
@@ -388,23 +389,26 @@ def tp_reduce_share(blocks, x, tp, local, dev, n):
         evs[i][0].record(stream)
         _lib.call("vqmoe_sparse_moe_block", ctypes.byref(descs[b]), x.data_ptr(), T, out.data_ptr(),
                   _lib.OUT_BF16, wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream)
-        evs[i][1].record(stream)
-        _lib.call("vqmoe_sparse_moe_block_tp", ctypes.byref(descs[b]), ctypes.byref(tps[b]), x.data_ptr(), T,
-                  out.data_ptr(), wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream)
-        evs[i][2].record(stream)
+        arr = (ctypes.c_void_p * 5)(*[e.cuda_event for e in evs[i][1:6]])
+        _lib.call("vqmoe_sparse_moe_block_tp_timed", ctypes.byref(descs[b]), ctypes.byref(tps[b]), x.data_ptr(), T,
+                  out.data_ptr(), wss[b].data_ptr(), wss[b].numel(), stream.cuda_stream, arr, 5)
     torch.cuda.synchronize(dev)
     rows = evs[min(10, n - 1):]
-    plain = sum(r[0].elapsed_time(r[1]) for r in rows) / len(rows)
-    fused = sum(r[1].elapsed_time(r[2]) for r in rows) / len(rows)
-    t = torch.tensor([plain, fused], device=dev)
+
+    def mean(a, b):
+        return sum(r[a].elapsed_time(r[b]) for r in rows) / len(rows)
+
+    vals = [mean(0, 1), mean(1, 5), mean(1, 2), mean(2, 3), mean(3, 4), mean(4, 5)]
+    t = torch.tensor(vals, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    plain, fused = (float(v) for v in t.tolist())
-    return {"block_ms": round(plain, 5), "split_call_ms": round(fused, 5),
-            "reduce_extra_ms": round(fused - plain, 5), "reduce_share": round((fused - plain) / fused, 4),
+    plain, call, router, experts, wait, reduce = (float(v) for v in t.tolist())
+    return {"block_ms": round(plain, 5), "split_call_ms": round(call, 5),
+            "split_stages_ms": {"router_exchange_sort_ms": round(router, 5), "experts_ms": round(experts, 5),
+                                "shared_wait_ms": round(wait, 5), "fused_reduce_ms": round(reduce, 5)},
+            "reduce_share": round(reduce / call, 4),
             "nvlink_bytes_per_rank": 2 * T * x.shape[1] * 2 * (tp - 1) // tp,
-            "note": "the same copy run unsplit-entry (combine kernel, no reduction) then split-entry (the fused "
-                    "combine + float32 reduction over NVLink peer memory); the extra includes waiting for the "
-                    "slowest rank"}
+            "note": "unsplit entry (whole router, combine kernel, no reduction) against the split entry's stages; "
+                    "the fused reduce includes waiting for the slowest rank"}
 
 
 def decoder_profile(dev, gen, batch=32, prompt=8192, k=3):

@@ -242,6 +242,16 @@ VQMOE_API vqmoe_status vqmoe_sparse_moe_block_tp(const vqmoe_block *blk, const v
                                                  void *workspace, size_t workspace_bytes,
                                                  void *stream);
 
+/* vqmoe_sparse_moe_block_tp that also records five caller-created CUDA
+ * events on `stream` (as vqmoe_sparse_moe_block_timed): before the router,
+ * after the split router and the routing exchange and sort, after the routed
+ * experts, after the join of the shared expert's side stream, and after the
+ * fused combine + reduction. For profiling; tokens <= 2048. */
+VQMOE_API vqmoe_status vqmoe_sparse_moe_block_tp_timed(const vqmoe_block *blk, const vqmoe_tp *tp,
+                                                       const void *x, int32_t tokens, void *out,
+                                                       void *workspace, size_t workspace_bytes, void *stream,
+                                                       void *const *events, int32_t n_events);
+
 /* SwitchGLU.__call__: y[T, k, H] bf16 = down(bf16(act(gate(x))) * up(x))
  * for each (token, slot) of indices [T, k] int32; act = gate->activation
  * (SwiGLU or GeGLU). */

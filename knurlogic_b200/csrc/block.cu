@@ -645,8 +645,9 @@ size_t vqmoe_tp_buffer_bytes(int32_t hidden, int32_t tokens) {
     return tp_route_offset((int)T, hidden) + tp_route_bytes((int)T, 32);   // top_k <= 32
 }
 
-vqmoe_status vqmoe_sparse_moe_block_tp(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x, int32_t tokens,
-                                       void *out, void *workspace, size_t workspace_bytes, void *stream) {
+static vqmoe_status block_tp_impl(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x, int32_t tokens,
+                                  void *out, void *workspace, size_t workspace_bytes, void *stream,
+                                  cudaEvent_t *ev, int n_ev) {
     if (!tp) return set_error(VQMOE_BAD_POINTER, "block_tp: null split descriptor");
     if (tp->world < 1 || tp->world > kTpMaxRanks || tp->rank < 0 || tp->rank >= tp->world)
         return set_error(VQMOE_BAD_SHAPE, "block_tp: rank %d of %d (at most %d ranks)", tp->rank, tp->world,
@@ -667,7 +668,22 @@ vqmoe_status vqmoe_sparse_moe_block_tp(const vqmoe_block *blk, const vqmoe_tp *t
         if (!aligned_ptr(tp->buffers[q])) return set_error(VQMOE_BAD_POINTER, "block_tp: buffer of rank %d", q);
         a.base[q] = static_cast<uint8_t *>(tp->buffers[q]);
     }
-    return block_impl(blk, x, tokens, out, VQMOE_OUT_BF16, workspace, workspace_bytes, stream, nullptr, 0, &a);
+    return block_impl(blk, x, tokens, out, VQMOE_OUT_BF16, workspace, workspace_bytes, stream, ev, n_ev, &a);
+}
+
+vqmoe_status vqmoe_sparse_moe_block_tp(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x, int32_t tokens,
+                                       void *out, void *workspace, size_t workspace_bytes, void *stream) {
+    return block_tp_impl(blk, tp, x, tokens, out, workspace, workspace_bytes, stream, nullptr, 0);
+}
+
+vqmoe_status vqmoe_sparse_moe_block_tp_timed(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x,
+                                             int32_t tokens, void *out, void *workspace, size_t workspace_bytes,
+                                             void *stream, void *const *events, int32_t n_events) {
+    if (!events || n_events < 5) return set_error(VQMOE_BAD_POINTER, "block_tp_timed: five events needed");
+    if (tokens > kMaxTokensPerLaunch)
+        return set_error(VQMOE_BAD_SHAPE, "timed block: at most %d tokens", kMaxTokensPerLaunch);
+    return block_tp_impl(blk, tp, x, tokens, out, workspace, workspace_bytes, stream,
+                         reinterpret_cast<cudaEvent_t *>(const_cast<void **>(events)), n_events);
 }
 
 vqmoe_status vqmoe_sparse_moe_block_timed(const vqmoe_block *blk, const void *x, int32_t tokens,

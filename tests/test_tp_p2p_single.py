@@ -63,3 +63,31 @@ def test_world_of_one_equals_the_block():
     st = _lib.lib().vqmoe_sparse_moe_block_tp(ctypes.byref(b), ctypes.byref(tp), x.data_ptr(), T, out.data_ptr(),
                                              ws.data_ptr(), ws.numel(), stream)
     assert _lib.STATUS[st] == "WORKSPACE_TOO_SMALL"
+
+
+def test_timed_entry_records_the_stages():
+    cfg = synth.CONFIGS["c2"]
+    w = synth.make_weights(cfg, seed=62, scales="random")
+    blk = SparseMoeBlock.from_weights({k: v.to(DEV) for k, v in w.items()}, cfg.top_k)
+    T = cfg.tokens
+    need = _lib.lib().vqmoe_tp_buffer_bytes(cfg.hidden, T)
+    buf = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    tp = _lib.Tp(rank=0, world=1, buffer_bytes=need)
+    tp.buffers[0] = buf.data_ptr()
+    b = blk._desc()
+    ws = blk.workspace(T, torch.device(DEV))
+    x = synth.make_input(cfg, seed=62).to(DEV)
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream().cuda_stream
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    for e in evs:
+        e.record()
+    arr = (ctypes.c_void_p * 5)(*[e.cuda_event for e in evs])
+    _lib.call("vqmoe_sparse_moe_block_tp_timed", ctypes.byref(b), ctypes.byref(tp), x.data_ptr(), T, out.data_ptr(),
+              ws.data_ptr(), ws.numel(), stream, arr, 5)
+    torch.cuda.synchronize()
+    assert torch.equal(out, blk(x))
+    assert all(evs[i].elapsed_time(evs[i + 1]) >= 0 for i in range(4))
+    st = _lib.lib().vqmoe_sparse_moe_block_tp_timed(ctypes.byref(b), ctypes.byref(tp), x.data_ptr(), T,
+                                                   out.data_ptr(), ws.data_ptr(), ws.numel(), stream, arr, 4)
+    assert _lib.STATUS[st] == "BAD_POINTER"
