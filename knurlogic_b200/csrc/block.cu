@@ -455,23 +455,41 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
     const uint16_t *rw = static_cast<const uint16_t *>(b->router_w);
     const uint16_t *sgw = shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr;
     if (tp) {
-        // under a split each rank routes T / n of the tokens (the exact
-        // logits are the router's cost and the same on every rank), then
-        // the ranks exchange the routing over peer memory (with one rank,
-        // the same path over its own buffer)
+        // under a split each rank computes the exact logits of T / n of the
+        // tokens (the router's cost, the same on every rank otherwise); the
+        // ranks exchange them over peer memory and every rank selects and
+        // sorts the whole routing (with one rank, the same path over its own
+        // buffer). Above the select kernel's size the ranks route their own
+        // tokens and exchange the routing instead.
         const int r0 = (int)((long long)T * tp->rank / tp->n), r1 = (int)((long long)T * (tp->rank + 1) / tp->n);
         const int E1 = E + (sgw ? 1 : 0);
-        if (vq_in && (s = launch_to_f16(x, w.x16, (size_t)T * H, st)) != VQMOE_OK) return s;
-        if (r1 > r0 && (s = launch_router(x + (size_t)r0 * H, rw, sgw, r1 - r0, H, E, k, w.logits + (size_t)r0 * E1,
-                                          w.inds + (size_t)r0 * k, w.scores + (size_t)r0 * k,
-                                          w.sgate + r0, nullptr, b->router_mode, nullptr, st)) != VQMOE_OK)
-            return s;
         TpArgs g = *tp;
         g.err = w.status;
-        if ((s = launch_tp_gather(w.inds, w.scores, sgw ? w.sgate : nullptr, T, k, H, r0, r1, g, st)) != VQMOE_OK ||
-            (s = launch_route(w.inds, P, E, rt.cnt, rt.off, rt.list, rt.active, rt.rank, rt.zero, rt.zero_words,
-                              st)) != VQMOE_OK)
-            return s;
+        if (vq_in && (s = launch_to_f16(x, w.x16, (size_t)T * H, st)) != VQMOE_OK) return s;
+        if (T <= kSelectMaxTok && E <= 1024) {
+            if (r1 > r0 && (s = launch_logits(x + (size_t)r0 * H, rw, sgw, r1 - r0, H, E, E1,
+                                              w.logits + (size_t)r0 * E1, nullptr, st)) != VQMOE_OK)
+                return s;
+            void *arrays[3] = {w.logits, nullptr, nullptr};
+            const int widths[3] = {E1, 0, 0};
+            if ((s = launch_tp_gather(arrays, widths, T, H, r0, r1, reinterpret_cast<uint32_t *>(rt.cnt), E + 1, g,
+                                      st)) != VQMOE_OK ||
+                (s = launch_select(w.logits, T, E, E1, k, sgw != nullptr, w.inds, w.scores, w.sgate, rt.cnt, rt.off,
+                                   rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, b->router_mode, st)) != VQMOE_OK)
+                return s;
+        } else {
+            if (r1 > r0 && (s = launch_router(x + (size_t)r0 * H, rw, sgw, r1 - r0, H, E, k,
+                                              w.logits + (size_t)r0 * E1, w.inds + (size_t)r0 * k,
+                                              w.scores + (size_t)r0 * k, w.sgate + r0, nullptr, b->router_mode,
+                                              nullptr, st)) != VQMOE_OK)
+                return s;
+            void *arrays[3] = {w.inds, w.scores, sgw ? w.sgate : nullptr};
+            const int widths[3] = {k, k, sgw ? 1 : 0};
+            if ((s = launch_tp_gather(arrays, widths, T, H, r0, r1, nullptr, 0, g, st)) != VQMOE_OK ||
+                (s = launch_route(w.inds, P, E, rt.cnt, rt.off, rt.list, rt.active, rt.rank, rt.zero, rt.zero_words,
+                                  st)) != VQMOE_OK)
+                return s;
+        }
     } else {
         s = launch_router_route(x, rw, sgw, T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, rt.cnt, rt.off,
                                 rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, b->router_mode, st);
@@ -642,7 +660,7 @@ vqmoe_status vqmoe_sparse_moe_block(const vqmoe_block *blk, const void *x, int32
 size_t vqmoe_tp_buffer_bytes(int32_t hidden, int32_t tokens) {
     if (hidden <= 0 || tokens <= 0) return 0;
     const size_t T = (size_t)std::min<int>(tokens, kMaxTokensPerLaunch);
-    return tp_route_offset((int)T, hidden) + tp_route_bytes((int)T, 32);   // top_k <= 32
+    return tp_route_offset((int)T, hidden) + tp_route_bytes((int)T);
 }
 
 static vqmoe_status block_tp_impl(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x, int32_t tokens,

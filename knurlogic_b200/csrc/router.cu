@@ -592,7 +592,6 @@ __device__ __forceinline__ void topk_warp(const float *__restrict__ lr, int E, i
 // zeroes them, and this kernel reads nothing before it has waited for that
 // kernel. The order of pairs inside an expert's list is the atomics'
 // (each pair's output does not depend on it). Zeroes `zero`.
-constexpr int kSelectMaxTok = 512;
 constexpr int kSelectWarps = 8;
 template <int EPL>
 __global__ void __launch_bounds__(kSelectWarps * 32)
@@ -727,7 +726,7 @@ static vqmoe_status launch_topk(const float *logits, int T, int E, int E1, int k
 // routing kernel's counters; only launches of up to kSelectMaxTok tokens pass it)
 vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t *wsg, int T, int H,
                            int E, int E1, float *logits, uint16_t *x16, cudaStream_t stream,
-                           uint32_t *zero2 = nullptr, int nzero2 = 0) {
+                           uint32_t *zero2, int nzero2) {
     size_t smem = (size_t)kRouterTok * H * sizeof(uint16_t);
     vqmoe_status s = ensure_dynamic_smem(reinterpret_cast<const void *>(router_logits_kernel), smem, "router");
     if (s != VQMOE_OK) return s;
@@ -778,6 +777,14 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
     vqmoe_status s = launch_logits(x, w, wsg, T, H, E, E1, logits, x16, stream,
                                    reinterpret_cast<uint32_t *>(cnt), E + 1);
     if (s != VQMOE_OK) return s;
+    return launch_select(logits, T, E, E1, k, wsg != nullptr, inds, scores, sgate, cnt, off, list, active,
+                         rank_scratch, zero, zero_words, mode, stream);
+}
+
+vqmoe_status launch_select(const float *logits, int T, int E, int E1, int k, bool has_shared, int32_t *inds,
+                           float *scores, float *sgate, int32_t *cnt, int32_t *off, int32_t *list, int32_t *active,
+                           int32_t *rank_scratch, uint32_t *zero, int zero_words, int mode, cudaStream_t stream) {
+    if (T > kSelectMaxTok || E > 1024) return set_error(VQMOE_BAD_SHAPE, "select: T %d E %d", T, E);
     const int epl = (E + 31) / 32;
     auto fn = epl <= 1 ? router_select_kernel<1>
               : epl <= 2 ? router_select_kernel<2>
@@ -785,7 +792,7 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
               : epl <= 8 ? router_select_kernel<8>
                          : router_select_kernel<16>;
     if (launch_pdl(fn, dim3((T + kSelectWarps - 1) / kSelectWarps), dim3(kSelectWarps * 32), 0, stream, logits, T,
-                   E, E1, k, (int)(wsg != nullptr), inds, scores, sgate, cnt, off, list, active, rank_scratch, zero,
+                   E, E1, k, (int)has_shared, inds, scores, sgate, cnt, off, list, active, rank_scratch, zero,
                    zero_words, mode, static_cast<const float *>(nullptr)) != cudaSuccess)
         return check_launch("router_select_kernel");
     return check_launch("router_select_kernel");

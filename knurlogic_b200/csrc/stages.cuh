@@ -19,6 +19,17 @@ vqmoe_status launch_router_route(const uint16_t *x, const uint16_t *w, const uin
                                  int32_t *list, int32_t *active, int32_t *rank_scratch,
                                  uint32_t *zero, int zero_words, int mode, cudaStream_t stream);
 vqmoe_status launch_to_f16(const uint16_t *x, uint16_t *x16, size_t n, cudaStream_t stream);
+// The router's pieces, for the tensor split's router: exact logits of T
+// tokens ([T][E1] float; zero2[0 .. nzero2) cleared on the way), and the
+// top-k + routing sort of up to kSelectMaxTok tokens from given logits
+// (cnt[0 .. E] zero on entry).
+constexpr int kSelectMaxTok = 512;
+vqmoe_status launch_logits(const uint16_t *x, const uint16_t *w, const uint16_t *wsg, int T, int H, int E, int E1,
+                           float *logits, uint16_t *x16, cudaStream_t stream, uint32_t *zero2 = nullptr,
+                           int nzero2 = 0);
+vqmoe_status launch_select(const float *logits, int T, int E, int E1, int k, bool has_shared, int32_t *inds,
+                           float *scores, float *sgate, int32_t *cnt, int32_t *off, int32_t *list, int32_t *active,
+                           int32_t *rank_scratch, uint32_t *zero, int zero_words, int mode, cudaStream_t stream);
 vqmoe_status launch_rms_norm(const uint16_t *x, const uint16_t *w, int T, int H, float eps, uint16_t *out,
                              cudaStream_t stream);
 
@@ -66,14 +77,16 @@ struct TpArgs {
 };
 vqmoe_status launch_tp_reduce(const uint16_t *ybuf, int T, int k, int H, const uint16_t *sh, const float *sg,
                               const TpArgs &a, uint16_t *out, cudaStream_t stream);
-// The split router's routing region in each rank's buffer (after the
-// partial and the result: [T][k] int32 expert ids, [T][k] float weights,
-// [T] float shared-expert gates), and the exchange that fills every rank's
-// routing arrays from the ranks' slices [r0, r1).
+// The split router's routing region in each rank's buffer, after the
+// partial and the result: kTpRouteWords 32-bit words per token (the router's
+// logits, E + 1 <= 1025 of them, or its expert ids, weights and gate), and
+// the exchange that fills every rank's arrays (up to three, `widths` words
+// per token each) from the ranks' row slices [r0, r1).
+constexpr int kTpRouteWords = 1025;
 size_t tp_route_offset(int T, int H);
-size_t tp_route_bytes(int T, int k);
-vqmoe_status launch_tp_gather(int32_t *inds, float *scores, float *sgate, int T, int k, int H, int r0, int r1,
-                              const TpArgs &a, cudaStream_t stream);
+size_t tp_route_bytes(int T);
+vqmoe_status launch_tp_gather(void *const *arrays, const int *widths, int T, int H, int r0, int r1, uint32_t *zero,
+                              int nzero, const TpArgs &a, cudaStream_t stream);
 
 // The routed experts with reference-layout VQ weights (VQMOE_FMT_VQ_REF):
 // phase 1 (r1, may be null) then phase 2, two launches.

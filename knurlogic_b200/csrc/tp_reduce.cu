@@ -188,28 +188,33 @@ tp_reduce_kernel(const uint16_t *__restrict__ ybuf, int T, int k, int H, const u
     }
 }
 
-// The split router's exchange (one CTA): this rank routed tokens [r0, r1);
-// their expert ids, routing weights and shared-expert gates go into every
-// rank's routing region, the ranks meet at a flag barrier (kArriveG, the
-// call's epoch, bounded), and each rank copies the whole routing from its
-// own region back into its workspace arrays.
+// The split router's exchange (one CTA per call): this rank computed rows
+// [r0, r1) of up to three row-major 32-bit arrays (widths w0..w2; a width 0
+// or a null array is skipped) -- the router's logits, or its expert ids,
+// weights and shared-expert gates. Its rows go into every rank's routing
+// region, the ranks meet at a flag barrier (kArriveG, the call's epoch,
+// bounded), and each rank copies all T rows from its own region back into
+// its arrays. zero[0 .. nzero) is cleared on the way (the select kernel's
+// counters, which the next kernel needs zeroed).
+struct GatherArrays {
+    uint32_t *p[3];
+    int w[3];
+};
+
 __global__ void __launch_bounds__(256)
-tp_gather_kernel(int32_t *__restrict__ inds, float *__restrict__ scores, float *__restrict__ sgate, int T, int k,
-                 int r0, int r1, size_t route_off, const TpArgs a) {
+tp_gather_kernel(GatherArrays g, int T, int r0, int r1, size_t route_off, uint32_t *zero, int nzero, const TpArgs a) {
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(flags_of(a, a.rank) + kEpoch);
     const int tid = threadIdx.x;
-    const int nk = (r1 - r0) * k;
+    for (int i = tid; i < nzero; i += blockDim.x) zero[i] = 0u;
     for (int q = 0; q < a.n; ++q) {
-        uint8_t *reg = a.base[q] + route_off;
-        int32_t *ri = reinterpret_cast<int32_t *>(reg);
-        float *rs = reinterpret_cast<float *>(reg + (size_t)T * k * 4);
-        float *rg = reinterpret_cast<float *>(reg + (size_t)T * k * 8);
-        for (int i = tid; i < nk; i += blockDim.x) {
-            ri[r0 * k + i] = inds[r0 * k + i];
-            rs[r0 * k + i] = scores[r0 * k + i];
+        uint32_t *reg = reinterpret_cast<uint32_t *>(a.base[q] + route_off);
+        for (int m = 0; m < 3; ++m) {
+            if (g.p[m] && g.w[m]) {
+                const int W = g.w[m];
+                for (int i = tid; i < (r1 - r0) * W; i += blockDim.x) reg[(size_t)r0 * W + i] = g.p[m][(size_t)r0 * W + i];
+            }
+            reg += (size_t)T * g.w[m];
         }
-        if (sgate)
-            for (int i = tid; i < r1 - r0; i += blockDim.x) rg[r0 + i] = sgate[r0 + i];
     }
     __syncthreads();
     if (tid == 0) {
@@ -231,24 +236,33 @@ tp_gather_kernel(int32_t *__restrict__ inds, float *__restrict__ scores, float *
         }
     }
     __syncthreads();
-    const uint8_t *reg = a.base[a.rank] + route_off;
-    for (int i = tid; i < T * k; i += blockDim.x) {
-        inds[i] = (int32_t)ld_cv_u32(reg + (size_t)i * 4);
-        scores[i] = __uint_as_float(ld_cv_u32(reg + ((size_t)T * k + i) * 4));
+    const uint32_t *reg = reinterpret_cast<const uint32_t *>(a.base[a.rank] + route_off);
+    for (int m = 0; m < 3; ++m) {
+        if (g.p[m] && g.w[m]) {
+            const size_t n = (size_t)T * g.w[m];
+            for (size_t i = tid; i < n; i += blockDim.x) g.p[m][i] = ld_cv_u32(reg + i);
+        }
+        reg += (size_t)T * g.w[m];
     }
-    if (sgate)
-        for (int i = tid; i < T; i += blockDim.x) sgate[i] = __uint_as_float(ld_cv_u32(reg + ((size_t)2 * T * k + i) * 4));
 }
 
 }  // namespace tp
 
 size_t tp_route_offset(int T, int H) { return kTpFlagBytes + 2 * (size_t)T * H * sizeof(uint16_t); }
 
-size_t tp_route_bytes(int T, int k) { return ((size_t)2 * T * k + T) * 4; }
+size_t tp_route_bytes(int T) { return (size_t)T * kTpRouteWords * 4; }
 
-vqmoe_status launch_tp_gather(int32_t *inds, float *scores, float *sgate, int T, int k, int H, int r0, int r1,
-                              const TpArgs &a, cudaStream_t stream) {
-    tp::tp_gather_kernel<<<1, 256, 0, stream>>>(inds, scores, sgate, T, k, r0, r1, tp_route_offset(T, H), a);
+vqmoe_status launch_tp_gather(void *const *arrays, const int *widths, int T, int H, int r0, int r1, uint32_t *zero,
+                              int nzero, const TpArgs &a, cudaStream_t stream) {
+    tp::GatherArrays g{};
+    int words = 0;
+    for (int m = 0; m < 3; ++m) {
+        g.p[m] = static_cast<uint32_t *>(arrays[m]);
+        g.w[m] = widths[m];
+        words += widths[m];
+    }
+    if (words > kTpRouteWords) return set_error(VQMOE_BAD_SHAPE, "split router: %d words per token", words);
+    tp::tp_gather_kernel<<<1, 256, 0, stream>>>(g, T, r0, r1, tp_route_offset(T, H), zero, nzero, a);
     return check_launch("tp_gather_kernel");
 }
 
