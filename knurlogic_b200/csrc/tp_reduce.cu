@@ -37,7 +37,7 @@ namespace vqmoe {
 namespace tp {
 
 // flag words of a rank's buffer
-constexpr int kEpoch = 0, kCountA = 1, kCountB = 2, kCountC = 3;
+constexpr int kEpoch = 0, kCountA = 1, kCountB = 2, kCountC = 3, kCountG = 4;
 constexpr int kArriveA = 8, kArriveB = 8 + kTpMaxRanks, kArriveG = 8 + 2 * kTpMaxRanks;
 
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
@@ -182,20 +182,23 @@ tp_reduce_kernel(const uint16_t *__restrict__ ybuf, int T, int k, int H, const u
             mine[kCountA] = 0u;
             mine[kCountB] = 0u;
             mine[kCountC] = 0u;
+            mine[kCountG] = 0u;
             __threadfence();
             atomicExch(mine + kEpoch, epoch + 1);
         }
     }
 }
 
-// The split router's exchange (one CTA per call): this rank computed rows
-// [r0, r1) of up to three row-major 32-bit arrays (widths w0..w2; a width 0
-// or a null array is skipped) -- the router's logits, or its expert ids,
-// weights and shared-expert gates. Its rows go into every rank's routing
-// region, the ranks meet at a flag barrier (kArriveG, the call's epoch,
-// bounded), and each rank copies all T rows from its own region back into
-// its arrays. zero[0 .. nzero) is cleared on the way (the select kernel's
-// counters, which the next kernel needs zeroed).
+// The split router's exchange: this rank computed rows [r0, r1) of up to
+// three row-major 32-bit arrays (widths w0..w2; a width 0 or a null array is
+// skipped) -- the router's logits, or its expert ids, weights and
+// shared-expert gates. Every CTA stores a share of those rows into every
+// rank's routing region; the ranks meet at a flag barrier (rank_barrier on
+// kCountG / kArriveG, the call's epoch, bounded); then every CTA copies a
+// share of all T rows from this rank's region back into the arrays. zero[0
+// .. nzero) is cleared on the way (the select kernel's counters). The
+// counter is cleared by the call's combine + reduction kernel, which always
+// follows.
 struct GatherArrays {
     uint32_t *p[3];
     int w[3];
@@ -204,45 +207,31 @@ struct GatherArrays {
 __global__ void __launch_bounds__(256)
 tp_gather_kernel(GatherArrays g, int T, int r0, int r1, size_t route_off, uint32_t *zero, int nzero, const TpArgs a) {
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(flags_of(a, a.rank) + kEpoch);
-    const int tid = threadIdx.x;
-    for (int i = tid; i < nzero; i += blockDim.x) zero[i] = 0u;
-    for (int q = 0; q < a.n; ++q) {
-        uint32_t *reg = reinterpret_cast<uint32_t *>(a.base[q] + route_off);
-        for (int m = 0; m < 3; ++m) {
-            if (g.p[m] && g.w[m]) {
-                const int W = g.w[m];
-                for (int i = tid; i < (r1 - r0) * W; i += blockDim.x) reg[(size_t)r0 * W + i] = g.p[m][(size_t)r0 * W + i];
-            }
-            reg += (size_t)T * g.w[m];
-        }
-    }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence_system();
-        for (int q = 0; q < a.n; ++q) st_release_sys(flags_of(a, q) + kArriveG + a.rank, epoch + 1);
-        const long polls = a.wait_polls ? (long)a.wait_polls : (1L << 22);
-        const uint32_t *mine = flags_of(a, a.rank);
-        for (int q = 0; q < a.n; ++q) {
-            unsigned ns = 32;
-            for (long i = 1;; ++i) {
-                if (ld_acquire_sys(mine + kArriveG + q) >= epoch + 1) break;
-                if (i >= polls) {
-                    atomicExch(a.err, kWaitDependency);
-                    break;
-                }
-                __nanosleep(ns);
-                if (ns < 1024) ns <<= 1;
-            }
-        }
-    }
-    __syncthreads();
-    const uint32_t *reg = reinterpret_cast<const uint32_t *>(a.base[a.rank] + route_off);
+    const size_t gtid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0u;
+    size_t off = 0;                                     // words of the arrays before m
     for (int m = 0; m < 3; ++m) {
-        if (g.p[m] && g.w[m]) {
-            const size_t n = (size_t)T * g.w[m];
-            for (size_t i = tid; i < n; i += blockDim.x) g.p[m][i] = ld_cv_u32(reg + i);
+        const int W = g.w[m];
+        if (g.p[m] && W) {
+            const size_t lo = (size_t)r0 * W, n = (size_t)(r1 - r0) * W;
+            for (size_t i = gtid; i < n; i += stride) {
+                const uint32_t v = g.p[m][lo + i];
+                for (int q = 0; q < a.n; ++q)
+                    reinterpret_cast<uint32_t *>(a.base[q] + route_off)[off + lo + i] = v;
+            }
         }
-        reg += (size_t)T * g.w[m];
+        off += (size_t)T * W;
+    }
+    rank_barrier(a, kCountG, kArriveG, epoch);
+    const uint32_t *reg = reinterpret_cast<const uint32_t *>(a.base[a.rank] + route_off);
+    off = 0;
+    for (int m = 0; m < 3; ++m) {
+        const int W = g.w[m];
+        if (g.p[m] && W)
+            for (size_t i = gtid; i < (size_t)T * W; i += stride) g.p[m][i] = ld_cv_u32(reg + off + i);
+        off += (size_t)T * W;
     }
 }
 
@@ -262,7 +251,11 @@ vqmoe_status launch_tp_gather(void *const *arrays, const int *widths, int T, int
         words += widths[m];
     }
     if (words > kTpRouteWords) return set_error(VQMOE_BAD_SHAPE, "split router: %d words per token", words);
-    tp::tp_gather_kernel<<<1, 256, 0, stream>>>(g, T, r0, r1, tp_route_offset(T, H), zero, nzero, a);
+    // every CTA resident at once (they meet at the barrier): at most one per
+    // SM, about eight words per thread
+    const size_t n = (size_t)T * words;
+    const int grid = (int)std::max<size_t>(1, std::min<size_t>((n + 2047) / 2048, (size_t)sm_count()));
+    tp::tp_gather_kernel<<<grid, 256, 0, stream>>>(g, T, r0, r1, tp_route_offset(T, H), zero, nzero, a);
     return check_launch("tp_gather_kernel");
 }
 
