@@ -465,15 +465,15 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
         const int E1 = E + (sgw ? 1 : 0);
         TpArgs g = *tp;
         g.err = w.status;
-        if (vq_in && (s = launch_to_f16(x, w.x16, (size_t)T * H, st)) != VQMOE_OK) return s;
+        uint16_t *x16 = vq_in ? w.x16 : nullptr;
         if (T <= kSelectMaxTok && E <= 1024) {
             if (r1 > r0 && (s = launch_logits(x + (size_t)r0 * H, rw, sgw, r1 - r0, H, E, E1,
                                               w.logits + (size_t)r0 * E1, nullptr, st)) != VQMOE_OK)
                 return s;
             void *arrays[3] = {w.logits, nullptr, nullptr};
             const int widths[3] = {E1, 0, 0};
-            if ((s = launch_tp_gather(arrays, widths, T, H, r0, r1, reinterpret_cast<uint32_t *>(rt.cnt), E + 1, g,
-                                      st)) != VQMOE_OK ||
+            if ((s = launch_tp_gather(arrays, widths, T, H, r0, r1, reinterpret_cast<uint32_t *>(rt.cnt), E + 1, x,
+                                      x16, g, st)) != VQMOE_OK ||
                 (s = launch_select(w.logits, T, E, E1, k, sgw != nullptr, w.inds, w.scores, w.sgate, rt.cnt, rt.off,
                                    rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, b->router_mode, st)) != VQMOE_OK)
                 return s;
@@ -485,7 +485,7 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                 return s;
             void *arrays[3] = {w.inds, w.scores, sgw ? w.sgate : nullptr};
             const int widths[3] = {k, k, sgw ? 1 : 0};
-            if ((s = launch_tp_gather(arrays, widths, T, H, r0, r1, nullptr, 0, g, st)) != VQMOE_OK ||
+            if ((s = launch_tp_gather(arrays, widths, T, H, r0, r1, nullptr, 0, x, x16, g, st)) != VQMOE_OK ||
                 (s = launch_route(w.inds, P, E, rt.cnt, rt.off, rt.list, rt.active, rt.rank, rt.zero, rt.zero_words,
                                   st)) != VQMOE_OK)
                 return s;

@@ -81,12 +81,13 @@ vqmoe_status launch_tp_reduce(const uint16_t *ybuf, int T, int k, int H, const u
 // partial and the result: kTpRouteWords 32-bit words per token (the router's
 // logits, E + 1 <= 1025 of them, or its expert ids, weights and gate), and
 // the exchange that fills every rank's arrays (up to three, `widths` words
-// per token each) from the ranks' row slices [r0, r1).
+// per token each) from the ranks' row slices [r0, r1); with x16 it also
+// writes the fp16 copy of x [T][H] the VQ experts read.
 constexpr int kTpRouteWords = 1025;
 size_t tp_route_offset(int T, int H);
 size_t tp_route_bytes(int T);
 vqmoe_status launch_tp_gather(void *const *arrays, const int *widths, int T, int H, int r0, int r1, uint32_t *zero,
-                              int nzero, const TpArgs &a, cudaStream_t stream);
+                              int nzero, const uint16_t *x, uint16_t *x16, const TpArgs &a, cudaStream_t stream);
 
 // The routed experts with reference-layout VQ weights (VQMOE_FMT_VQ_REF):
 // phase 1 (r1, may be null) then phase 2, two launches.

@@ -205,12 +205,23 @@ struct GatherArrays {
 };
 
 __global__ void __launch_bounds__(256)
-tp_gather_kernel(GatherArrays g, int T, int r0, int r1, size_t route_off, uint32_t *zero, int nzero, const TpArgs a) {
+tp_gather_kernel(GatherArrays g, int T, int r0, int r1, size_t route_off, uint32_t *zero, int nzero,
+                 const uint16_t *__restrict__ x, uint16_t *__restrict__ x16, size_t nx8, const TpArgs a) {
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(flags_of(a, a.rank) + kEpoch);
     const size_t gtid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     if (blockIdx.x == 0)
         for (int i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0u;
+    // the VQ experts' fp16 copy of all T tokens (bf16 -> fp16, saturated),
+    // while the peers' rows are on their way
+    for (size_t v = gtid; v < nx8; v += stride) {
+        const uint4 val = reinterpret_cast<const uint4 *>(x)[v];
+        uint32_t u[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            u[j] = (uint32_t)bf16_to_f16_sat(u[j] & 0xFFFFu) | ((uint32_t)bf16_to_f16_sat(u[j] >> 16) << 16);
+        reinterpret_cast<uint4 *>(x16)[v] = make_uint4(u[0], u[1], u[2], u[3]);
+    }
     size_t off = 0;                                     // words of the arrays before m
     for (int m = 0; m < 3; ++m) {
         const int W = g.w[m];
@@ -242,7 +253,7 @@ size_t tp_route_offset(int T, int H) { return kTpFlagBytes + 2 * (size_t)T * H *
 size_t tp_route_bytes(int T) { return (size_t)T * kTpRouteWords * 4; }
 
 vqmoe_status launch_tp_gather(void *const *arrays, const int *widths, int T, int H, int r0, int r1, uint32_t *zero,
-                              int nzero, const TpArgs &a, cudaStream_t stream) {
+                              int nzero, const uint16_t *x, uint16_t *x16, const TpArgs &a, cudaStream_t stream) {
     tp::GatherArrays g{};
     int words = 0;
     for (int m = 0; m < 3; ++m) {
@@ -253,9 +264,11 @@ vqmoe_status launch_tp_gather(void *const *arrays, const int *widths, int T, int
     if (words > kTpRouteWords) return set_error(VQMOE_BAD_SHAPE, "split router: %d words per token", words);
     // every CTA resident at once (they meet at the barrier): at most one per
     // SM, about eight words per thread
-    const size_t n = (size_t)T * words;
+    const size_t nx8 = x16 ? (size_t)T * H / 8 : 0;
+    const size_t n = std::max<size_t>((size_t)T * words, nx8);
     const int grid = (int)std::max<size_t>(1, std::min<size_t>((n + 2047) / 2048, (size_t)sm_count()));
-    tp::tp_gather_kernel<<<grid, 256, 0, stream>>>(g, T, r0, r1, tp_route_offset(T, H), zero, nzero, a);
+    tp::tp_gather_kernel<<<grid, 256, 0, stream>>>(g, T, r0, r1, tp_route_offset(T, H), zero, nzero, x, x16, nx8,
+                                                   a);
     return check_launch("tp_gather_kernel");
 }
 
