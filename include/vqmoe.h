@@ -252,6 +252,27 @@ VQMOE_API vqmoe_status vqmoe_sparse_moe_block_tp_timed(const vqmoe_block *blk, c
                                                        void *workspace, size_t workspace_bytes, void *stream,
                                                        void *const *events, int32_t n_events);
 
+/* Bytes of one rank's buffer for the expert split (its expert outputs
+ * [T*k][H] bf16 and its result region [T][H] bf16 behind the flags), for
+ * up to `tokens` tokens per call. */
+VQMOE_API size_t vqmoe_ep_buffer_bytes(int32_t hidden, int32_t tokens, int32_t top_k);
+
+/* The SparseMoeBlock with its experts split by id across the ranks (expert
+ * parallelism, an alternative to the tensor split at large E; the reference
+ * has no EP): rank r of n holds experts [r*E/n, (r+1)*E/n) whole -- the
+ * three linears carry E/n experts, uint8 dim-4 VQ in the device layout --
+ * and the full router and shared expert. Every rank routes every token, runs
+ * the pairs of its own experts, writing their outputs into its buffer, and
+ * ONE kernel then sums each token's k slots in slot order over peer memory,
+ * reading each slot from its expert's owner, and adds the gated shared
+ * expert: the unsplit block's combine bit for bit, into out [T, H] bf16 on
+ * every rank. Same call rules as vqmoe_sparse_moe_block_tp (the vqmoe_tp
+ * descriptor, buffer_bytes >= vqmoe_ep_buffer_bytes, zeroed once). The
+ * decode path only: fewer than 32 pairs per expert per 2048-token chunk. */
+VQMOE_API vqmoe_status vqmoe_sparse_moe_block_ep(const vqmoe_block *blk, const vqmoe_tp *ep, const void *x,
+                                                 int32_t tokens, void *out, void *workspace,
+                                                 size_t workspace_bytes, void *stream);
+
 /* SwitchGLU.__call__: y[T, k, H] bf16 = down(bf16(act(gate(x))) * up(x))
  * for each (token, slot) of indices [T, k] int32; act = gate->activation
  * (SwiGLU or GeGLU). */

@@ -66,6 +66,9 @@ SIGNATURES = [
     ("vqmoe_tp_buffer_bytes", c_size_t, [c_int32, c_int32]),
     ("vqmoe_sparse_moe_block_tp", c_int32,
      [POINTER(Block), POINTER(Tp), c_void_p, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("vqmoe_ep_buffer_bytes", c_size_t, [c_int32, c_int32, c_int32]),
+    ("vqmoe_sparse_moe_block_ep", c_int32,
+     [POINTER(Block), POINTER(Tp), c_void_p, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("vqmoe_sparse_moe_block_tp_timed", c_int32,
      [POINTER(Block), POINTER(Tp), c_void_p, c_int32, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p, c_int32]),
     ("vqmoe_last_error", c_char_p, []),

@@ -16,6 +16,7 @@
 #include <map>
 #include <mutex>
 
+#include "layout.cuh"
 #include "stages.cuh"
 
 namespace vqmoe {
@@ -431,6 +432,32 @@ static vqmoe_status run_shared(const vqmoe_block *b, const uint16_t *x, int T, c
                                w.sh, rt.spart_dn, rt.ssem_dn, st);
 }
 
+// The expert split: keep only this rank's experts [own0, own1) in the list
+// of active experts the expert kernel takes its tiles from (in order).
+__global__ void __launch_bounds__(1024) filter_active_kernel(int32_t *__restrict__ active, int E, int own0, int own1) {
+    __shared__ int s_keep[1024];
+    __shared__ int s_n;
+    const int tid = threadIdx.x;
+    const int n = active[E];
+    const int e = tid < n ? active[tid] : -1;
+    const int keep = e >= own0 && e < own1;
+    s_keep[tid] = keep;
+    __syncthreads();
+    if (tid == 0) {
+        int c = 0;
+        for (int i = 0; i < n; ++i) {
+            const int kk = s_keep[i];
+            s_keep[i] = c;
+            c += kk;
+        }
+        s_n = c;
+    }
+    __syncthreads();
+    if (keep) active[s_keep[tid]] = e;
+    __syncthreads();
+    if (tid == 0) active[E] = s_n;
+}
+
 static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                               void *out, int out_f32, const BlockWs &w,
                               cudaStream_t st, cudaEvent_t *ev = nullptr, int n_ev = 0,
@@ -454,7 +481,16 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
     const RouteWs &rt = w.rt;
     const uint16_t *rw = static_cast<const uint16_t *>(b->router_w);
     const uint16_t *sgw = shared ? static_cast<const uint16_t *>(b->shared_expert_gate_w) : nullptr;
-    if (tp) {
+    if (tp && tp->ep_local) {
+        // the expert split: every rank routes every token, then keeps the
+        // experts it owns
+        s = launch_router_route(x, rw, sgw, T, H, E, k, w.logits, w.inds, w.scores, w.sgate, w.x16, rt.cnt, rt.off,
+                                rt.list, rt.active, rt.rank, rt.zero, rt.zero_words, b->router_mode, st);
+        if (s != VQMOE_OK) return s;
+        const int own0 = tp->rank * tp->ep_local;
+        filter_active_kernel<<<1, 1024, 0, st>>>(rt.active, E, own0, own0 + tp->ep_local);
+        if ((s = check_launch("filter_active_kernel")) != VQMOE_OK) return s;
+    } else if (tp) {
         // under a split each rank computes the exact logits of T / n of the
         // tokens (the router's cost, the same on every rank otherwise); the
         // ranks exchange them over peer memory and every rank selects and
@@ -501,13 +537,24 @@ static vqmoe_status run_block(const vqmoe_block *b, const uint16_t *x, int T,
                             vq_dn, nullptr);
     r1.xs = w.xs;
     r1.act = b->gate.activation;
-    RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, w.ybuf, 0, w.scores);
+    // the expert split: the owned pairs' outputs go straight into this
+    // rank's buffer, where the other ranks read them
+    uint16_t *ybuf = tp && tp->ep_local ? reinterpret_cast<uint16_t *>(tp->base[tp->rank] + kTpFlagBytes) : w.ybuf;
+    RoutedIO r2 = routed_io(rt, E, k, P, w.act, 1, ybuf, 0, w.scores);
     s = launch_experts(&b->gate, &b->up, &r1, &b->down, r2, rt.zero, w.status, (uint32_t)b->wait_polls, st,
                        ev && n_ev > 5 ? ev[5] : nullptr);
     if (s != VQMOE_OK || (s = mark(ev, n_ev, 2, st)) != VQMOE_OK) return s;
     if (shared && cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
         return check_launch("side stream join");
     if ((s = mark(ev, n_ev, 3, st)) != VQMOE_OK) return s;
+    if (tp && tp->ep_local) {
+        TpArgs a = *tp;
+        a.err = w.status;
+        if ((s = launch_ep_reduce(w.inds, T, k, H, tp->ep_local, shared ? w.sh : nullptr, w.sgate, a,
+                                  static_cast<uint16_t *>(out), st)) != VQMOE_OK)
+            return s;
+        return mark(ev, n_ev, 4, st);
+    }
     if (tp) {
         // the combine and the split's reduction, one kernel over peer memory
         TpArgs a = *tp;
@@ -692,6 +739,59 @@ static vqmoe_status block_tp_impl(const vqmoe_block *blk, const vqmoe_tp *tp, co
 vqmoe_status vqmoe_sparse_moe_block_tp(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x, int32_t tokens,
                                        void *out, void *workspace, size_t workspace_bytes, void *stream) {
     return block_tp_impl(blk, tp, x, tokens, out, workspace, workspace_bytes, stream, nullptr, 0);
+}
+
+size_t vqmoe_ep_buffer_bytes(int32_t hidden, int32_t tokens, int32_t top_k) {
+    if (hidden <= 0 || tokens <= 0 || top_k <= 0) return 0;
+    return ep_buffer_bytes(std::min<int>(tokens, kMaxTokensPerLaunch), top_k, hidden);
+}
+
+vqmoe_status vqmoe_sparse_moe_block_ep(const vqmoe_block *blk, const vqmoe_tp *ep, const void *x, int32_t tokens,
+                                       void *out, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!blk || !ep) return set_error(VQMOE_BAD_POINTER, "block_ep: null descriptor");
+    const int n = ep->world, E = blk->num_experts, H = blk->hidden, k = blk->top_k;
+    if (n < 1 || n > kTpMaxRanks || ep->rank < 0 || ep->rank >= n)
+        return set_error(VQMOE_BAD_SHAPE, "block_ep: rank %d of %d (at most %d ranks)", ep->rank, n, kTpMaxRanks);
+    if (ep->wait_polls < 0) return set_error(VQMOE_BAD_SHAPE, "block_ep: wait_polls %d", ep->wait_polls);
+    if (E <= 0 || E % n) return set_error(VQMOE_BAD_SHAPE, "block_ep: %d experts over %d ranks", E, n);
+    if (H <= 0 || H % (8 * n)) return set_error(VQMOE_BAD_SHAPE, "block_ep: hidden %d, %d ranks", H, n);
+    if (tokens <= 0 || k <= 0) return set_error(VQMOE_BAD_SHAPE, "tokens %d top_k %d", tokens, k);
+    const int El = E / n, own0 = ep->rank * El;
+    const int chunk = std::min<int>(tokens, kMaxTokensPerLaunch);
+    if (prefill_regime(true, E, chunk * k))
+        return set_error(VQMOE_BAD_SHAPE, "block_ep: %d pairs over %d experts (the decode path: fewer than 32 a "
+                         "expert)", chunk * k, E);
+    if ((size_t)ep->buffer_bytes < vqmoe_ep_buffer_bytes(H, tokens, k))
+        return set_error(VQMOE_WORKSPACE_TOO_SMALL, "block_ep: buffers of %lld < %zu bytes",
+                         (long long)ep->buffer_bytes, vqmoe_ep_buffer_bytes(H, tokens, k));
+    // the rank's E / n experts are addressed by their global ids: each VQ
+    // layout pointer is moved back by own0 experts' worth of tiles
+    vqmoe_block b2 = *blk;
+    vqmoe_linear *L[3] = {&b2.gate, &b2.up, &b2.down};
+    for (vqmoe_linear *l : L) {
+        if (l->format != VQMOE_FMT_VQ_U8)
+            return set_error(VQMOE_BAD_FORMAT, "block_ep: experts in the uint8 dim-4 VQ layout only");
+        if (l->num_experts != El)
+            return set_error(VQMOE_BAD_SHAPE, "block_ep: a rank holds %d experts, got %d", El, l->num_experts);
+        const VqGeom G{1, l->out_features, l->in_features};
+        const size_t cstride = (size_t)G.code_bytes(), sstride = (size_t)G.scale_elems() * 2;
+        const uintptr_t c = reinterpret_cast<uintptr_t>(l->codes), sc = reinterpret_cast<uintptr_t>(l->scales);
+        if (!c || !sc || c < own0 * cstride || sc < own0 * sstride)
+            return set_error(VQMOE_BAD_POINTER, "block_ep: expert weights");
+        l->codes = reinterpret_cast<const void *>(c - own0 * cstride);
+        l->scales = reinterpret_cast<const void *>(sc - own0 * sstride);
+        l->num_experts = E;
+    }
+    TpArgs a{};
+    a.rank = ep->rank;
+    a.n = n;
+    a.wait_polls = (uint32_t)ep->wait_polls;
+    a.ep_local = El;
+    for (int q = 0; q < n; ++q) {
+        if (!aligned_ptr(ep->buffers[q])) return set_error(VQMOE_BAD_POINTER, "block_ep: buffer of rank %d", q);
+        a.base[q] = static_cast<uint8_t *>(ep->buffers[q]);
+    }
+    return block_impl(&b2, x, tokens, out, VQMOE_OUT_BF16, workspace, workspace_bytes, stream, nullptr, 0, &a);
 }
 
 vqmoe_status vqmoe_sparse_moe_block_tp_timed(const vqmoe_block *blk, const vqmoe_tp *tp, const void *x,

@@ -74,9 +74,16 @@ struct TpArgs {
     uint8_t *base[kTpMaxRanks];
     uint32_t *err;             // the call's status word
     uint32_t wait_polls;       // polls of each barrier wait (0: about four seconds)
+    int ep_local;              // expert split: experts per rank (0: the tensor split)
 };
 vqmoe_status launch_tp_reduce(const uint16_t *ybuf, int T, int k, int H, const uint16_t *sh, const float *sg,
                               const TpArgs &a, uint16_t *out, cudaStream_t stream);
+// The expert split (TpArgs with ep_local = E / n experts per rank): each
+// rank's buffer holds kTpFlagBytes of flags, its expert outputs [T*k][H] bf16
+// (the pairs of the experts it owns), then its result region [T][H] bf16.
+size_t ep_buffer_bytes(int T, int k, int H);
+vqmoe_status launch_ep_reduce(const int32_t *inds, int T, int k, int H, int ep_local, const uint16_t *sh,
+                              const float *sg, const TpArgs &a, uint16_t *out, cudaStream_t stream);
 // The split router's routing region in each rank's buffer, after the
 // partial and the result: kTpRouteWords 32-bit words per token (the router's
 // logits, E + 1 <= 1025 of them, or its expert ids, weights and gate), and

@@ -98,6 +98,24 @@ __device__ void rank_barrier(const TpArgs &a, int count, int arrive, uint32_t ep
     __syncthreads();
 }
 
+// The call's last CTA (every CTA has read the epoch and passed the call's
+// barriers by then) clears the counters and advances the epoch.
+__device__ void finish_call(const TpArgs &a, uint32_t epoch) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t *mine = flags_of(a, a.rank);
+        const uint32_t old = atomicAdd(mine + kCountC, 1u);
+        if (old == gridDim.x - 1) {
+            mine[kCountA] = 0u;
+            mine[kCountB] = 0u;
+            mine[kCountC] = 0u;
+            mine[kCountG] = 0u;
+            __threadfence();
+            atomicExch(mine + kEpoch, epoch + 1);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(256)
 tp_reduce_kernel(const uint16_t *__restrict__ ybuf, int T, int k, int H, const uint16_t *__restrict__ sh,
                  const float *__restrict__ sg, const TpArgs a, uint16_t *__restrict__ out) {
@@ -172,21 +190,69 @@ tp_reduce_kernel(const uint16_t *__restrict__ ybuf, int T, int k, int H, const u
     const uint8_t *red = a.base[a.rank] + kTpFlagBytes + part_bytes;
     for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < nvec; v += stride)
         reinterpret_cast<uint4 *>(out)[v] = ld_cv_v4(red + v * 16);
-    // the call's last CTA (every CTA has read the epoch and passed both
-    // barriers by then) clears the counters and advances the epoch
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        uint32_t *mine = flags_of(a, a.rank);
-        const uint32_t old = atomicAdd(mine + kCountC, 1u);
-        if (old == gridDim.x - 1) {
-            mine[kCountA] = 0u;
-            mine[kCountB] = 0u;
-            mine[kCountC] = 0u;
-            mine[kCountG] = 0u;
-            __threadfence();
-            atomicExch(mine + kEpoch, epoch + 1);
+    finish_call(a, epoch);
+}
+
+// The expert split's combine and exchange. Every rank holds E / n whole
+// experts and wrote, into its own buffer, the outputs y[t, s] of the
+// (token, slot) pairs whose expert it owns. After a barrier each rank sums
+// one column slice of every token over its k slots in slot order, reading
+// each slot from the rank that owns its expert (owner = expert / (E / n)),
+// in float32 rounded once, adds the gated shared expert (every rank has
+// it), and stores the bf16 result into every rank's result region: the
+// unsplit block's combine (qwen3_5.py:181-187) bit for bit. A second barrier,
+// then each rank copies its result region into the output.
+__global__ void __launch_bounds__(256)
+ep_reduce_kernel(const int32_t *__restrict__ inds, int T, int k, int H, int ep_local, const uint16_t *__restrict__ sh,
+                 const float *__restrict__ sg, const TpArgs a, uint16_t *__restrict__ out) {
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(flags_of(a, a.rank) + kEpoch);
+    const int vpr = H / 8;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t ybytes = (size_t)T * k * H * 2;
+    rank_barrier(a, kCountA, kArriveA, epoch);          // every rank's expert outputs are in place
+    const int spr = vpr / a.n;
+    const size_t nsl = (size_t)T * spr;
+    for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < nsl; v += stride) {
+        const int tkn = (int)(v / spr), c8 = a.rank * spr + (int)(v - (size_t)tkn * spr);
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+        for (int s = 0; s < k; ++s) {
+            const int e = inds[(size_t)tkn * k + s];
+            const int q = min(e / ep_local, a.n - 1);
+            const uint4 y = ld_cv_v4(a.base[q] + kTpFlagBytes + (((size_t)tkn * k + s) * H + c8 * 8) * 2);
+            const uint32_t u[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] += bf16_to_f32(u[j] & 0xFFFFu);
+                acc[2 * j + 1] += bf16_to_f32(u[j] >> 16);
+            }
         }
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = bf16r(acc[i]);
+        if (sh) {
+            const float gate = sg[tkn];
+            const uint4 sv = *reinterpret_cast<const uint4 *>(sh + (size_t)tkn * H + c8 * 8);
+            const uint32_t u[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                r[2 * j] = bf16r(r[2 * j] + bf16r(gate * bf16_to_f32(u[j] & 0xFFFFu)));
+                r[2 * j + 1] = bf16r(r[2 * j + 1] + bf16r(gate * bf16_to_f32(u[j] >> 16)));
+            }
+        }
+        uint32_t p[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[j] = (uint32_t)f32_to_bf16(r[2 * j]) | ((uint32_t)f32_to_bf16(r[2 * j + 1]) << 16);
+        const uint4 res = make_uint4(p[0], p[1], p[2], p[3]);
+        const size_t off = ((size_t)tkn * vpr + c8) * 16;
+        for (int q = 0; q < a.n; ++q) *reinterpret_cast<uint4 *>(a.base[q] + kTpFlagBytes + ybytes + off) = res;
     }
+    rank_barrier(a, kCountB, kArriveB, epoch);
+    const uint8_t *red = a.base[a.rank] + kTpFlagBytes + ybytes;
+    for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < (size_t)T * vpr; v += stride)
+        reinterpret_cast<uint4 *>(out)[v] = ld_cv_v4(red + v * 16);
+    finish_call(a, epoch);
 }
 
 // The split router's exchange: this rank computed rows [r0, r1) of up to
@@ -270,6 +336,16 @@ vqmoe_status launch_tp_gather(void *const *arrays, const int *widths, int T, int
     tp::tp_gather_kernel<<<grid, 256, 0, stream>>>(g, T, r0, r1, tp_route_offset(T, H), zero, nzero, x, x16, nx8,
                                                    a);
     return check_launch("tp_gather_kernel");
+}
+
+size_t ep_buffer_bytes(int T, int k, int H) { return kTpFlagBytes + ((size_t)T * k + T) * H * sizeof(uint16_t); }
+
+vqmoe_status launch_ep_reduce(const int32_t *inds, int T, int k, int H, int ep_local, const uint16_t *sh,
+                              const float *sg, const TpArgs &a, uint16_t *out, cudaStream_t stream) {
+    const size_t nvec = (size_t)T * (H / 8);
+    const int grid = (int)std::max<size_t>(1, std::min<size_t>((nvec + 255) / 256, (size_t)sm_count()));
+    tp::ep_reduce_kernel<<<grid, 256, 0, stream>>>(inds, T, k, H, ep_local, sh, sg, a, out);
+    return check_launch("ep_reduce_kernel");
 }
 
 vqmoe_status launch_tp_reduce(const uint16_t *ybuf, int T, int k, int H, const uint16_t *sh, const float *sg,

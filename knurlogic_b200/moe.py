@@ -72,11 +72,16 @@ class SparseMoeBlock(nn.Module):
                  top_k: int, shared_expert: SharedExpert | None = None,
                  shared_expert_gate_weight: torch.Tensor | None = None,
                  sharding_group=None, router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM,
-                 tp_reduce: str = "p2p"):
+                 tp_reduce: str = "p2p", expert_split: bool = False):
         super().__init__()
         if tp_reduce not in ("p2p", "nccl"):
             raise ValueError(f"tp_reduce {tp_reduce!r} ('p2p' or 'nccl')")
-        self.tp_reduce = tp_reduce
+        if expert_split and sharding_group is None:
+            raise ValueError("expert_split needs the sharding group")
+        # expert_split: this rank holds E / n whole experts (ids rank*E/n ..)
+        # instead of a cut of every expert; reduced over peer memory
+        self.expert_split = bool(expert_split)
+        self.tp_reduce = "p2p" if expert_split else tp_reduce
         self._tp = None
         E, H = gate_weight.shape
         self.num_experts, self.hidden = int(E), int(H)
@@ -98,12 +103,19 @@ class SparseMoeBlock(nn.Module):
         # phase 1 tiles (0: the library default, about four seconds)
         self.wait_polls = 0
         sm = switch_mlp
+        held = E
+        if expert_split:
+            import torch.distributed as dist
+            n = dist.get_world_size(sharding_group)
+            if E % n:
+                raise ValueError(f"expert split: {E} experts over {n} ranks")
+            held = E // n
         for name, mod, shape in (("gate_proj", sm.gate_proj, None),
                                  ("up_proj", sm.up_proj, None),
                                  ("down_proj", sm.down_proj, None)):
-            if mod.num_experts != E:
+            if mod.num_experts != held:
                 raise ValueError(f"switch_mlp.{name}: {mod.num_experts} experts, "
-                                 f"router {E}")
+                                 f"router {E}" + (f" over the split ({held} a rank)" if expert_split else ""))
         if sm.gate_proj.input_dims != H or sm.down_proj.output_dims != H:
             raise ValueError("switch_mlp does not map hidden size "
                              f"{H} -> {H}")
@@ -155,7 +167,10 @@ class SparseMoeBlock(nn.Module):
         barrier so that no rank's kernel meets another's unzeroed flags."""
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
-        need = _lib.lib().vqmoe_tp_buffer_bytes(self.hidden, min(tokens, 2048))
+        if self.expert_split:
+            need = _lib.lib().vqmoe_ep_buffer_bytes(self.hidden, min(tokens, 2048), self.top_k)
+        else:
+            need = _lib.lib().vqmoe_tp_buffer_bytes(self.hidden, min(tokens, 2048))
         if self._tp is not None and self._tp[0] >= need and self._tp[1].device == device:
             return self._tp[2]
         g = self.sharding_group
@@ -180,10 +195,13 @@ class SparseMoeBlock(nn.Module):
         T = x2d.shape[0]
         b = self._desc()
         ws = self.workspace(T, x2d.device)
+        if self.expert_split and out.dtype != torch.bfloat16:
+            raise TypeError("the expert split writes a bf16 output")
         if self.sharding_group is not None and self.tp_reduce == "p2p" and out.dtype == torch.bfloat16:
             tp = self.tp_buffers(T, x2d.device)
-            _lib.call("vqmoe_sparse_moe_block_tp", ctypes.byref(b), ctypes.byref(tp), x2d.data_ptr(), T,
-                      out.data_ptr(), ws.data_ptr(), ws.numel(), c_stream(x2d.device))
+            _lib.call("vqmoe_sparse_moe_block_ep" if self.expert_split else "vqmoe_sparse_moe_block_tp",
+                      ctypes.byref(b), ctypes.byref(tp), x2d.data_ptr(), T, out.data_ptr(), ws.data_ptr(),
+                      ws.numel(), c_stream(x2d.device))
             return out
         odt = _lib.OUT_F32 if out.dtype == torch.float32 else _lib.OUT_BF16
         _lib.call("vqmoe_sparse_moe_block", ctypes.byref(b), x2d.data_ptr(), T,
@@ -210,7 +228,7 @@ class SparseMoeBlock(nn.Module):
     def from_weights(cls, w: dict, top_k: int, prefix: str = "mlp.",
                      group_size: int | None = None, sharding_group=None,
                      router_mode: int = _lib.ROUTER_SOFTMAX_TOPK_RENORM, activation=None,
-                     bits: int | None = None, tp_reduce: str = "p2p"):
+                     bits: int | None = None, tp_reduce: str = "p2p", expert_split: bool = False):
         """Build from a state dict with the reference's names:
         `{prefix}gate.weight`; `{prefix}switch_mlp.{gate,up,down}_proj.`
         `{codes, codebook, vq_scales}` (VQ), `{weight, scales, biases}`
@@ -258,7 +276,8 @@ class SparseMoeBlock(nn.Module):
                               w[f"{p}shared_expert.down_proj.weight"])
             seg = w[f"{p}shared_expert_gate.weight"]
         return cls(w[f"{p}gate.weight"], SwitchGLU(**projs, activation=activation), top_k, se, seg,
-                   sharding_group=sharding_group, router_mode=router_mode, tp_reduce=tp_reduce)
+                   sharding_group=sharding_group, router_mode=router_mode, tp_reduce=tp_reduce,
+                   expert_split=expert_split)
 
 
 class CapturedBlock:

@@ -1,11 +1,14 @@
-"""The tensor split on 2, 4 and 8 GPUs (each skipped with fewer): each rank
-builds its cut with `tensor_split.build_block` and runs the block through
-the C ABI; the ranks' partials are reduced either by the peer-memory kernel (the combine
-and the float32 reduction in one kernel, `vqmoe_sparse_moe_block_tp`, over
-torch symmetric-memory buffers) or over NCCL. Rank 0 compares both with the
-oracle's tensor-split block and checks that they agree with each other, over
-eager calls, repeated calls (the kernel's barrier epochs advance) and CUDA
-graph replays."""
+"""The tensor split and the expert split on 2, 4 and 8 GPUs (each skipped
+with fewer). For the tensor split each rank builds its cut with
+`tensor_split.build_block` and runs the block through the C ABI; the ranks'
+partials are reduced either by the peer-memory kernel (the combine and the
+float32 reduction in one kernel, `vqmoe_sparse_moe_block_tp`, over torch
+symmetric-memory buffers) or over NCCL, and rank 0 compares both with the
+oracle's tensor-split block and with each other. For the expert split
+(`expert_split.build_block`, `vqmoe_sparse_moe_block_ep`) each rank holds
+whole experts and rank 0 requires the unsplit block's output bit for bit.
+All over eager calls, repeated calls (the kernels' barrier epochs advance)
+and CUDA-graph replays."""
 import os
 import socket
 
@@ -14,7 +17,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from knurlogic_b200 import CapturedBlock, synth, tensor_split
+from knurlogic_b200 import CapturedBlock, SparseMoeBlock, expert_split, synth, tensor_split
 from oracle import moe_ref as R
 from tests.conftest import assert_bf16_close, oracle_params, to_np
 
@@ -57,6 +60,19 @@ def _rank(rank, N, port, q):
             out[mode] = ys
             del cap, blk
             torch.cuda.synchronize(dev)
+        # the expert split: whole experts by id, the combine over peer memory
+        blk = expert_split.build_block(wd, CFG.top_k, rank, N, dist.group.WORLD)
+        ys = [to_np(blk(synth.make_input(CFG, seed=seed).to(dev))) for seed in (8, 9, 10)]
+        blk.check_status()
+        cap = CapturedBlock(blk, CFG.tokens)
+        for seed in (11, 12):
+            ys.append(to_np(cap(synth.make_input(CFG, seed=seed).to(dev)).clone()))
+        cap.check_status()
+        out["ep"] = ys
+        del cap, blk
+        full = SparseMoeBlock.from_weights(wd, CFG.top_k)     # the unsplit block, this GPU alone
+        out["full"] = [to_np(full(synth.make_input(CFG, seed=seed).to(dev))) for seed in (8, 9, 10, 11, 12)]
+        torch.cuda.synchronize(dev)
         # every rank's kernels and collectives end here, before rank 0's checks
         # (a failed check must not leave a peer inside a collective)
         dist.barrier()
@@ -68,6 +84,8 @@ def _rank(rank, N, port, q):
                 ref = R.tp_sparse_moe_block(to_np(synth.make_input(CFG, seed=seed)), p, CFG.top_k, vq=True, n=N)
                 assert_bf16_close(out["p2p"][i], ref, f"tp{N} p2p call {i}")
                 assert_bf16_close(out["nccl"][i], ref, f"tp{N} nccl call {i}")
+                # the expert split's combine is the block's own: bit for bit
+                assert np.array_equal(out["ep"][i], out["full"][i]), f"ep{N} call {i}"
                 a = out["p2p"][i].astype(np.float32)
                 b = out["nccl"][i].astype(np.float32)
                 ulp = np.abs(a - b) / np.maximum(np.abs(a), 1e-30)
