@@ -468,6 +468,39 @@ def quick_value(workload, tp, rank, world, local, dev, steps, warmup):
             "ms_per_step": round(ms / steps, 5), "steps": steps}
 
 
+def quick_value_ep(workload, rank, world, local, dev, steps, warmup):
+    """tokens/s of `workload` with its experts split by id over all `world`
+    ranks (`expert_split`: whole experts, every rank routes every token, the
+    combine over peer memory), graph replays over layer copies: the
+    alternative to the tensor split, beside the headline."""
+    import math
+
+    import torch.distributed as dist
+
+    from knurlogic_b200 import expert_split, synth
+    cfg = synth.CONFIGS[workload]
+    shapes = {"mlp.switch_mlp.gate_proj.codes": (cfg.experts, cfg.inter, cfg.hidden // 4),
+              "mlp.switch_mlp.gate_proj.codebook": (cfg.codebook_size, cfg.dim),
+              "mlp.gate.weight": (cfg.experts, cfg.hidden)}
+    why = expert_split.refusals(shapes, world)
+    if why:
+        return {"workload": workload, "refused": "; ".join(why)}
+    per_layer = synth.algorithmic_bytes(cfg, cfg.experts) / world
+    L = max(2, min(16, math.ceil(3 * 126e6 / per_layer) + 1))
+    blocks = []
+    for i in range(L):
+        w = synth.make_weights(cfg, seed=300 + i, device=dev, scales="ones")
+        blocks.append(expert_split.build_block(w, cfg.top_k, rank, world, dist.group.WORLD))
+        del w
+    x = synth.make_input(cfg, seed=11, device=dev)
+    G = Graphs(blocks, x, world, dist.group.WORLD, dev)
+    ms = timed(G.replay, steps, warmup, world, local, dev)
+    del G, blocks
+    return {"workload": workload, "tokens": cfg.tokens, "expert_parallel": world, "replicas": 1,
+            "value": round(cfg.tokens * steps / (ms / 1e3), 1), "unit": UNIT,
+            "ms_per_step": round(ms / steps, 5), "steps": steps}
+
+
 def prefill_profile(dev, steps=100, warmup=5):
     """c3 (4096 prefill tokens, Zipf 1.1) on this GPU: the step time of the
     whole block (graph replays over layer copies, so weights stream from
@@ -592,6 +625,8 @@ def run_ours(args, world, rank, local):
                 secondary["decoder_c5"] = decoder_profile(dev, args.decoder_tokens)
         elif world > 1 and tp > 1:
             secondary["c2_replicas"] = quick_value("c2", 1, rank, world, local, dev, 200, 10)
+            if workload == "c4" and tp == world:
+                secondary["c4_expert_split"] = quick_value_ep("c4", rank, world, local, dev, 200, 10)
 
     if rank != 0:
         return None
