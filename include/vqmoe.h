@@ -24,16 +24,21 @@
  *   vqmoe_prepare_vq        loading VQSwitchLinear.codes / .vq_scales
  *       (deepseek_v4.py:111-130 layout) into the device layout the kernels
  *       read
+ *   vqmoe_sparse_moe_block_tp  the tensor-split block with its Reduce
+ *       (src/knurlogic/engine/split/tensor.py:159-187) fused over NVLink
+ *       peer memory; vqmoe_sparse_moe_block_ep the same block with whole
+ *       experts split by id (no counterpart in the reference)
+ *   vqmoe_add_rms_norm      the decoder's residual add + RMSNorm
+ *       (qwen3_5.py:120-130, 578-587)
  *
  * Numerics (matching the reference's rounding order, qwen3_5.py:35-40,
  * 108-112, 170-192): bf16 matmul outputs; fp32 softmax / top-k /
  * renormalisation with weights rounded to bf16; silu / sigmoid in fp32
  * rounded once; the top-k sum in fp32 rounded once. VQ weights dequantise
  * to W = fp16(f32(codebook[code][j]) * f32(vq_scale)) (vqmoe_dequant, bit
- * for bit) and the VQ matmul takes the bf16 activations as fp16 (saturated
- * at +-65504); the matmul kernels apply each 64-input group's scale to the
- * fp32 partial sum of that group instead of to each weight, which differs
- * from the dequantised form by at most half an fp16 step per weight.
+ * for bit, on every expert path: decode, prefill and the reference-layout
+ * kernel) and the VQ matmul takes the bf16 activations as fp16 (saturated
+ * at +-65504), with fp16 x fp16 products accumulated in fp32.
  */
 #ifndef VQMOE_H_
 #define VQMOE_H_

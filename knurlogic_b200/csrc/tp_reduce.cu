@@ -27,7 +27,13 @@
 // on (its output is then wrong; nothing hangs).
 //
 // Each rank's symmetric buffer: kTpFlagBytes of flags and counters, its
-// partial [T][H] bf16, its result region [T][H] bf16.
+// partial [T][H] bf16, its result region [T][H] bf16, then the split
+// router's region (tp_gather_kernel: each rank's exact logits of T/n of the
+// tokens, or its routing, exchanged the same way before the experts run).
+//
+// The expert split (ep_reduce_kernel) uses the same flags and barriers over
+// another layout: the rank's expert outputs [T*k][H] bf16 (the pairs of the
+// experts it owns), then its result region [T][H] bf16.
 #include <algorithm>
 
 #include "stages.cuh"
